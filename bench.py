@@ -1,0 +1,357 @@
+"""Benchmark of the decode W4A16-LoRA GEMV (Qwen3-4B gate_proj shape).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One step = one W4A16-LoRA GEMV call: x [1, 2560] fp16 times a GPTQ int4
+weight [2560, 9728] (group 128, packed qzeros) plus a rank-16 LoRA
+(alpha / r = 2), output [1, 9728] fp16.  Algorithmic bytes per call:
+qweight 12,451,840 + scales 389,120 + qzeros 97,280 + A 81,920 + B 311,296 +
+x 5,120 + y 19,456 = 13,356,032 B.
+
+value  : device throughput in GB/s (algorithmic bytes / CUDA-event time) over
+         K back-to-back calls replayed from a CUDA graph; each call reads a
+         different weight set from a rotation whose total size exceeds 2x L2,
+         so every call streams its weights from HBM.  Summed over ranks for
+         N > 1 (independent replicas, weak scaling), time = max over ranks.
+e2e    : the same metric through the public Python API
+         (qextract_infer_b200.w4a16_lora_gemv) with x copied host->device from
+         pinned memory and y copied back every step.
+roofline, cpu_baseline, clocks, gpu_launches: see the keys in the JSON line.
+
+Under torchrun every rank runs its own replica; rank 0 prints one JSON line.
+``--impl reference`` times the CPU restatement of the reference's algorithm
+(oracle/qx_oracle.c, all host cores) on the same workload; ranks > 0 exit.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M, K, N, RANK, GROUP, ALPHA = 1, 2560, 9728, 16, 128, 32.0
+BYTES_PER_CALL = (K // 8 * N * 4 + K // GROUP * N * 2 + K // GROUP * N // 8 * 4 + K * RANK * 2
+                  + RANK * N * 2 + M * K * 2 + M * N * 2)
+METRIC = "W4A16-LoRA GEMV µs & HBM GB/s (% peak); Qwen3-8B decode tok/s @1/2/4/8 B200"
+WORKLOAD = ("decode W4A16-LoRA GEMV, Qwen3-4B gate_proj: x[1,2560] fp16 . GPTQ int4 W[2560,9728] "
+            "g128 packed qzeros + LoRA r16 alpha/r=2 -> y[1,9728] fp16")
+L2_BYTES = 126 * 1024 * 1024
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per launch of the GEMV kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "w4a16_gemv_decode.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms in a thread."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 7:
+                self.samples.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if s[3 + i].lower() in ("active", "1")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_gemv_baseline(seconds: float = 12.0, max_calls: int = 200, nthreads: int = 0):
+    """The C restatement of the reference algorithm (dequantise to fp16, fp32
+    GEMV + LoRA) on the host cores, on the full decode workload."""
+    from oracle import cbind, make_gemv_inputs
+    d = make_gemv_inputs(M, K, N, RANK, seed=0)
+    cbind.lib()
+    threads = nthreads or os.cpu_count() or 1
+    cbind.c_w4a16_lora_gemv(d["x"], d["qweight"], d["scales"], d["zeros"], d["lora_A"], d["lora_B"],
+                            GROUP, ALPHA, nthreads=threads)
+    n, t0 = 0, time.perf_counter()
+    while n < max_calls and (time.perf_counter() - t0) < seconds:
+        cbind.c_w4a16_lora_gemv(d["x"], d["qweight"], d["scales"], d["zeros"], d["lora_A"],
+                                d["lora_B"], GROUP, ALPHA, nthreads=threads)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": BYTES_PER_CALL * n / dt / 1e9, "unit": "GB/s", "cores": threads,
+            "kind": "port", "us_per_call": dt / n * 1e6,
+            "sample": f"{n} full decode-GEMV calls (K=2560, N=9728, r=16) in {dt:.1f} s with "
+                      f"oracle/qx_oracle.c on {threads} OpenMP threads"}
+
+
+def run_reference(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return 0
+    from oracle import cbind, make_gemv_inputs
+    threads = os.cpu_count() or 1
+    d = make_gemv_inputs(M, K, N, RANK, seed=0)
+    call = lambda: cbind.c_w4a16_lora_gemv(d["x"], d["qweight"], d["scales"], d["zeros"],  # noqa
+                                           d["lora_A"], d["lora_B"], GROUP, ALPHA, nthreads=threads)
+    steps = max(1, min(args.steps, 2000))
+    for _ in range(max(args.warmup, 1)):
+        call()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        call()
+    dt = time.perf_counter() - t0
+    gbs = BYTES_PER_CALL * steps / dt / 1e9
+    line = {"metric": METRIC, "value": gbs, "unit": "GB/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": dt / steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16 activations, int4 weights, fp32 accumulate",
+            "data": "synthetic (seeded; BASELINE decode-GEMV distributions)",
+            "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N, "rank": RANK, "group": GROUP},
+            "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": f"{steps} full decode-GEMV calls with oracle/qx_oracle.c "
+                                       f"(C restatement of the reference CPU path)"},
+            "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def make_weight_sets(torch, device, nsets, seed=0):
+    g = torch.Generator(device=device)
+    sets = []
+    for i in range(nsets):
+        g.manual_seed(seed + i)
+        qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), generator=g, device=device,
+                           dtype=torch.int32)
+        sc = (torch.rand(K // GROUP, N, generator=g, device=device) * 0.015 + 0.005).half()
+        qz = torch.full((K // GROUP, N // 8), 0x88888888 - 2 ** 32, dtype=torch.int32, device=device)
+        A = (torch.randn(K, RANK, generator=g, device=device) * 0.02).half()
+        B = (torch.randn(RANK, N, generator=g, device=device) * 0.02).half()
+        sets.append((qw, sc, qz, A, B))
+    return sets
+
+
+def run_b200(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_setup()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=__import__("datetime").timedelta(seconds=120))
+    device = torch.device("cuda", local if world > 1 else torch.cuda.current_device())
+    torch.cuda.set_device(device)
+    import qextract_infer_b200 as qx
+    from qextract_infer_b200 import _C
+    if not qx._C_AVAILABLE:
+        raise RuntimeError("native library missing")
+
+    nsets = int(np.ceil(2.2 * L2_BYTES / BYTES_PER_CALL))
+    sets = make_weight_sets(torch, device, nsets)
+    x = torch.randn(M, K, generator=torch.Generator(device=device).manual_seed(123), device=device).half()
+    # correctness gate on set 0 against the oracle (rank 0, cheap)
+    if rank == 0:
+        from oracle import cbind
+        qw, sc, qz, A, B = sets[0]
+        y = _C.w4a16_lora_gemv(x, qw, sc, qz, A, B, GROUP, ALPHA)
+        ref = cbind.c_w4a16_lora_gemv(x.cpu().numpy(), qw.cpu().numpy(), sc.cpu().numpy(),
+                                      qz.cpu().numpy(), A.cpu().numpy(), B.cpu().numpy(), GROUP, ALPHA)
+        err = np.abs(y.float().cpu().numpy() - ref.astype(np.float32))
+        bound = 1e-2 + 1e-2 * np.abs(ref.astype(np.float32))
+        if not np.all(err <= bound):
+            raise RuntimeError(f"bench correctness gate failed: max err {err.max()}")
+
+    stream = torch.cuda.Stream(device)
+    outs = [torch.empty(M, N, dtype=torch.float16, device=device) for _ in range(2)]
+
+    def step(i):
+        qw, sc, qz, A, B = sets[i % nsets]
+        return _C.w4a16_lora_gemv(x, qw, sc, qz, A, B, GROUP, ALPHA)
+
+    steps, warm = max(1, args.steps), max(3, args.warmup)
+    with torch.cuda.stream(stream):
+        for i in range(warm):  # eager warm-up (allocates the workspace)
+            step(i)
+    stream.synchronize()
+
+    def capture(nsteps, offset):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for i in range(nsteps):
+                step(offset + i)
+        return gr
+
+    g_warm = capture(warm, 0)
+    g_timed = capture(steps, warm)
+    for _ in range(2):
+        g_warm.replay()
+    stream.synchronize()
+    # sustained load so the clock sampler sees the GPU busy, then the timed region
+    sampler = ClockSampler(device.index)
+    with sampler:
+        t_end = time.time() + 1.0
+        while time.time() < t_end:
+            g_warm.replay()
+            stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        g_timed.replay()
+        ev1.record(stream)
+        ev1.synchronize()
+        torch.cuda.synchronize(device)
+        ms = ev0.elapsed_time(ev1)
+        # e2e through the public API: pinned host x -> device, GEMV, y -> pinned host
+        x_host = torch.randn(M, K).half().pin_memory()
+        y_host = torch.empty(M, N, dtype=torch.float16).pin_memory()
+        e_steps = max(1, min(steps, 2000))
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                xd = x_host.to(device, non_blocking=True)
+                qw, sc, qz, A, B = sets[i % nsets]
+                y_host.copy_(qx.w4a16_lora_gemv(xd, qw, sc, qz, A, B, GROUP, ALPHA), non_blocking=True)
+            stream.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(e_steps):
+                xd = x_host.to(device, non_blocking=True)
+                qw, sc, qz, A, B = sets[i % nsets]
+                y_host.copy_(qx.w4a16_lora_gemv(xd, qw, sc, qz, A, B, GROUP, ALPHA), non_blocking=True)
+            e1.record(stream)
+            e1.synchronize()
+        e_ms = e0.elapsed_time(e1)
+    clocks = sampler.summary()
+
+    if world > 1:
+        t = torch.tensor([ms, e_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e_ms = float(t[0]), float(t[1])
+    per_call_s = ms / 1e3 / steps
+    achieved = BYTES_PER_CALL / per_call_s / 1e9  # one GPU, GB/s
+    peak, peak_kind = measured_peaks()
+    result = None
+    if rank == 0:
+        cpu = cpu_gemv_baseline() if world == 1 else None
+        result = {
+            "metric": METRIC,
+            "value": achieved * world,
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": steps,
+            "warmup": warm,
+            "ms_per_step": ms / steps,
+            "us_per_call": per_call_s * 1e6,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "fp16 activations, int4 weights, fp32 accumulate",
+            "data": "synthetic (seeded, on device; BASELINE decode-GEMV value distributions)",
+            "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N, "rank": RANK, "group": GROUP,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": f"inputs larger than L2: {nsets} rotating weight sets, "
+                             f"{nsets * BYTES_PER_CALL / 1e6:.0f} MB > 2x 126 MB"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "nominal_frac_8tbs": achieved / 8000.0,
+                         "traffic": profiled_traffic(),
+                         "algorithmic_bytes_per_launch": BYTES_PER_CALL,
+                         "kernel": "qx::gemv::w4a16_gemv_kernel<1>"},
+            "e2e": {"value": BYTES_PER_CALL * e_steps / (e_ms / 1e3) / 1e9 * world, "unit": "GB/s",
+                    "us_per_call": e_ms * 1e3 / e_steps,
+                    "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
+                    "api": "qextract_infer_b200.w4a16_lora_gemv (ctypes C-ABI)"},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "gpu_launches": steps,
+        }
+    if world > 1:
+        dist.barrier()
+        del g_timed, g_warm
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

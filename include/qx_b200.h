@@ -1,0 +1,144 @@
+/*
+ * qx_b200.h -- C ABI of libqx_b200.so, the sm_100a (B200) kernels behind the
+ * QExtract-Infer operator API.
+ *
+ * Conventions
+ *   - All pointers are device pointers unless stated otherwise; fp16 data is
+ *     passed as `const void*` / `void*` holding IEEE binary16 values.
+ *   - Every tensor is dense row-major (C-contiguous).
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  All work is
+ *     enqueued on it; nothing synchronises the host.
+ *   - Nothing here allocates device memory.  Ops that need scratch take a
+ *     caller-owned `workspace`; its required size comes from the matching
+ *     `*_workspace_size` function.
+ *   - Return value: 0 on success, negative on error (QX_ERR_*); the message
+ *     of the last error on the calling thread is returned by qx_last_error().
+ *
+ * The reference interface each entry point replaces is cited as
+ * path:line within the QExtract-Infer project.
+ */
+#ifndef QX_B200_H_
+#define QX_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* qx_stream_t; /* == cudaStream_t */
+
+#define QX_OK 0
+#define QX_ERR_INVALID (-1)
+#define QX_ERR_CUDA (-2)
+#define QX_ERR_WORKSPACE (-3)
+#define QX_ERR_UNSUPPORTED (-4)
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* qx_last_error(void);
+/* Library version string. */
+const char* qx_version(void);
+
+/* ------------------------------------------------------------------------
+ * W4A16(-LoRA) GEMV.
+ * Replaces w4a16_lora_gemv() (csrc/kernels/w4a16_lora_gemv.cu:268-323) and
+ * w4a16_gemv() (:233-265), bound at csrc/binding.cpp:44-56.
+ *
+ *   y[M, N] = fp16( x[M, K] . dequant(qweight) + lora_scale * (x . A) . B )
+ *
+ *   x        fp16  [M, K]           (M = product of the leading dims)
+ *   qweight  int32 [K/8, N]         nibble i of qweight[p, n] = W_q[8p+i, n]
+ *   scales   fp16  [K/group, N]
+ *   zeros    zeros_packed == 0: fp16 [K/group, N]  (reference kernel format)
+ *            zeros_packed == 1: int32 [K/group, N/8] GPTQ qzeros, z = nibble + zero_offset
+ *   lora_A   fp16  [K, rank]   lora_B fp16 [rank, N]   (rank == 0: no LoRA; A, B may be NULL)
+ *   lora_scale  = lora_alpha / rank   (the reference computes it at w4a16_lora_gemv.cu:221)
+ *   y        fp16  [M, N]
+ * Constraints: K % 32 == 0, group_size % 32 == 0, K % group_size == 0,
+ * N % 8 == 0, rank in {0, 8, 16, 32, 64, 128}, x/qweight/lora_A 16-byte aligned.
+ * Any M >= 1 (rows are processed 32 at a time).
+ * workspace: >= qx_w4a16_gemv_workspace_size(M, K, N, rank, group_size) bytes,
+ * 256-byte aligned, zero-filled before its first use; every call leaves it
+ * zero-filled again.  Calls that share a workspace must be stream-ordered.
+ * ---------------------------------------------------------------------- */
+size_t qx_w4a16_gemv_workspace_size(int M, int K, int N, int rank, int group_size);
+
+int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const void* scales,
+                       const void* zeros, int zeros_packed, int zero_offset,
+                       const void* lora_A, const void* lora_B, void* y,
+                       int M, int K, int N, int rank, int group_size, float lora_scale,
+                       void* workspace, size_t workspace_bytes, qx_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Fused RMSNorm.  Replaces fused_rmsnorm() (csrc/kernels/rmsnorm.cu:162-210,
+ * bound at csrc/binding.cpp:36-38).
+ *   y[r, :] = fp16( (x[r, :] * rsqrt(mean(x[r, :]^2) + eps)) * w )
+ * x, y fp16 [rows, H]; w fp16 [H].  Any H >= 1; H % 8 == 0 and 16-byte
+ * aligned rows take the vector path.
+ * ---------------------------------------------------------------------- */
+int qx_fused_rmsnorm(const void* x, const void* weight, void* y, int64_t rows, int hidden,
+                     float eps, qx_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Fused SwiGLU.  Replaces fused_swiglu() (csrc/kernels/swiglu.cu:94-135,
+ * bound at csrc/binding.cpp:40-42).
+ *   y[i] = fp16( g[i] * sigmoid(g[i]) * u[i] ),  i < n
+ * ---------------------------------------------------------------------- */
+int qx_fused_swiglu(const void* gate, const void* up, void* y, int64_t n, qx_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * StreamingLLM ring KV cache (sink + circular window).
+ * Replaces RingBufferKVCache::append / get_kv / get_valid_length
+ * (csrc/kv_cache/ring_buffer.cu:109-209, bound at csrc/binding.cpp:59-74)
+ * and the Python twins in qextract/kv_cache.py:75-152.
+ *
+ * Layer storage: k_cache, v_cache fp16 [batch, sink + window, kv_heads, head_dim].
+ * `count` is the number of tokens written before this call (write_count in
+ * the reference).  Token j of the chunk goes to slot write_pos(count + j):
+ *   write_pos(c) = c < sink ? c : sink + (c - sink) % window.
+ * Appending T tokens at once leaves the cache exactly as T single-token
+ * appends would (later tokens win a slot).  Advancing `count` (after the
+ * last layer) is the caller's job, as in the reference.
+ * ---------------------------------------------------------------------- */
+int qx_ring_append(void* k_cache, void* v_cache, const void* new_k, const void* new_v,
+                   int batch, int tokens, int kv_heads, int head_dim, int sink, int window,
+                   int64_t count, qx_stream_t stream);
+
+/* Logical-order slot list (sinks, then the ring from its oldest token) for
+ * `count` written tokens; writes valid_length(count) int32 indices to
+ * `slots` (device) and returns that length (>= 0) or a negative status. */
+int64_t qx_ring_slot_indices(int32_t* slots, int sink, int window, int64_t count,
+                             qx_stream_t stream);
+
+/* Materialise K and V in logical order, the reference get_kv():
+ * out fp16 [batch, valid_length(count), kv_heads, head_dim]. */
+int qx_ring_gather(const void* k_cache, const void* v_cache, void* k_out, void* v_out,
+                   int batch, int kv_heads, int head_dim, int sink, int window, int64_t count,
+                   qx_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * GQA decode attention read in place from the ring (no gather).  New
+ * component (the reference has no attention kernel); semantics: HF Qwen3
+ * eager attention over the cache's valid slots (qextract/kv_cache.py:121-142
+ * order is irrelevant to the result).
+ *   q fp16 [batch, q_heads, head_dim] (post-RoPE), caches as above,
+ *   out fp16 [batch, q_heads, head_dim];  q_heads % kv_heads == 0,
+ *   head_dim == 128, q_heads / kv_heads <= 16.
+ * softmax_scale <= 0 selects 1/sqrt(head_dim).
+ * workspace: >= qx_decode_attention_workspace_size(...) bytes, 256-byte
+ * aligned, zero-filled before first use, left zero-filled by every call.
+ * ---------------------------------------------------------------------- */
+size_t qx_decode_attention_workspace_size(int batch, int q_heads, int kv_heads, int head_dim,
+                                          int sink, int window);
+
+int qx_decode_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                        int batch, int q_heads, int kv_heads, int head_dim, int sink,
+                        int window, int64_t count, float softmax_scale, void* workspace,
+                        size_t workspace_bytes, qx_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QX_B200_H_ */

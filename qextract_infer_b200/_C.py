@@ -1,0 +1,308 @@
+"""Operator module with the names, arguments and error behaviour of the
+reference's ``qextract._C`` (pybind11 module, ``csrc/binding.cpp:32-74``),
+implemented over the C ABI of ``libqx_b200.so`` (``include/qx_b200.h``).
+
+Differences from the reference, all widening what it accepts:
+
+* ``w4a16_gemv`` / ``w4a16_lora_gemv`` take ``input`` of shape ``[K]`` or
+  ``[..., K]`` and return ``[N]`` / ``[..., N]`` (the reference reads
+  ``input.size(0)`` as K, ``csrc/kernels/w4a16_lora_gemv.cu:285``, so 2-D
+  inputs silently computed nothing);
+* ``zeros`` may be the reference's fp16 ``[G, N]`` or GPTQ-packed
+  ``qzeros`` int32 ``[G, N/8]`` (``zero_offset=1`` for the GPTQ-v1 "+1"
+  storage);
+* ``RingBufferKVCache.append`` also takes ``[T, H, D]`` and ``[B, T, H, D]``
+  chunks, and the cache adds ``decode_attention``.
+
+Every op runs on the current torch CUDA stream and raises if the native
+library is missing or the inputs are not CUDA tensors: there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _lib, _workspace
+
+__all__ = ["fused_rmsnorm", "fused_swiglu", "w4a16_gemv", "w4a16_lora_gemv",
+           "RingBufferKVCache", "decode_attention", "ring_slot_indices"]
+
+_LIB = _lib.load()  # fail at import time if the native library is absent
+_SUPPORTED_RANKS = (8, 16, 32, 64, 128)
+
+
+def _check_input(t: torch.Tensor, name: str):
+    # same conditions as CHECK_CUDA_INPUT (csrc/include/common.h:20-28)
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def _check_fp16(t: torch.Tensor, name: str):
+    if t.dtype != torch.float16:
+        raise RuntimeError(f"{name} must be float16, got {t.dtype}")
+
+
+def _stream(device: torch.device):
+    return torch.cuda.current_stream(device)
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+# ------------------------------------------------------------------ norms --
+def fused_rmsnorm(input: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """``fp16((x * rsqrt(mean(x^2) + eps)) * w)`` over the last dim
+    (reference: ``csrc/kernels/rmsnorm.cu:162-210``)."""
+    _check_input(input, "input")
+    _check_input(weight, "weight")
+    _check_fp16(input, "input")
+    _check_fp16(weight, "weight")
+    hidden = input.size(-1)
+    if weight.numel() != hidden:
+        raise RuntimeError(f"weight size mismatch: {weight.numel()} vs {hidden}")
+    out = torch.empty_like(input)
+    rows = input.numel() // hidden if hidden else 0
+    st = _stream(input.device)
+    _lib.check(_LIB.qx_fused_rmsnorm(input.data_ptr(), weight.data_ptr(), out.data_ptr(), rows,
+                                     hidden, float(eps), st.cuda_stream), "fused_rmsnorm")
+    return out
+
+
+def fused_swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """``fp16(silu(gate) * up)`` elementwise (reference: ``csrc/kernels/swiglu.cu:94-135``)."""
+    _check_input(gate, "gate")
+    _check_input(up, "up")
+    _check_fp16(gate, "gate")
+    if gate.shape != up.shape:
+        raise RuntimeError("gate and up must have same shape")
+    _check_fp16(up, "up")
+    out = torch.empty_like(gate)
+    st = _stream(gate.device)
+    _lib.check(_LIB.qx_fused_swiglu(gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.numel(),
+                                    st.cuda_stream), "fused_swiglu")
+    return out
+
+
+# ------------------------------------------------------------------- GEMV --
+def _prepare_lora(lora_A, lora_B):
+    """Pad rank up to a supported value with zero rows/columns (exact: the
+    padding contributes 0 to x.A and to (x.A).B)."""
+    r = lora_A.size(1)
+    if r in _SUPPORTED_RANKS:
+        return lora_A, lora_B, r
+    rp = next((s for s in _SUPPORTED_RANKS if s >= r), None)
+    if rp is None:
+        raise RuntimeError(f"LoRA rank {r} > 128 is not supported")
+    A = torch.zeros(lora_A.size(0), rp, dtype=lora_A.dtype, device=lora_A.device)
+    B = torch.zeros(rp, lora_B.size(1), dtype=lora_B.dtype, device=lora_B.device)
+    A[:, :r] = lora_A
+    B[:r] = lora_B
+    return A, B, rp
+
+
+def _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale, zero_offset):
+    for t, n in ((input, "input"), (qweight, "qweight"), (scales, "scales"), (zeros, "zeros")):
+        _check_input(t, n)
+    _check_fp16(input, "input")
+    _check_fp16(scales, "scales")
+    if qweight.dtype != torch.int32 or qweight.dim() != 2:
+        raise RuntimeError("qweight must be int32 [K/8, N]")
+    K = input.size(-1)
+    N = qweight.size(1)
+    if qweight.size(0) * 8 != K:
+        raise RuntimeError(f"qweight has {qweight.size(0)} packed rows; input K={K} needs {K // 8}")
+    G = K // group_size if group_size > 0 else 0
+    if scales.dim() != 2 or scales.size(0) != G or scales.size(1) != N:
+        raise RuntimeError(f"scales must be [{G}, {N}], got {list(scales.shape)}")
+    if zeros.dtype == torch.int32:
+        packed = 1
+        if tuple(zeros.shape) != (G, N // 8):
+            raise RuntimeError(f"packed qzeros must be int32 [{G}, {N // 8}], got {list(zeros.shape)}")
+    elif zeros.dtype == torch.float16:
+        packed = 0
+        if tuple(zeros.shape) != (G, N):
+            raise RuntimeError(f"zeros must be fp16 [{G}, {N}], got {list(zeros.shape)}")
+    else:
+        raise RuntimeError(f"zeros must be float16 [G, N] or int32 qzeros [G, N/8], got {zeros.dtype}")
+    rank = 0
+    if lora_A is not None:
+        _check_input(lora_A, "lora_A")
+        _check_input(lora_B, "lora_B")
+        _check_fp16(lora_A, "lora_A")
+        _check_fp16(lora_B, "lora_B")
+        if lora_A.dim() != 2 or lora_A.size(0) != K or lora_B.dim() != 2 or \
+                lora_B.size(0) != lora_A.size(1) or lora_B.size(1) != N:
+            raise RuntimeError(f"lora_A must be [{K}, r] and lora_B [r, {N}]")
+        lora_A, lora_B, rank = _prepare_lora(lora_A, lora_B)
+    lead = input.shape[:-1]
+    M = int(np.prod(lead)) if len(lead) else 1
+    out = torch.empty(*lead, N, dtype=torch.float16, device=input.device)
+    dev = input.device
+    st = _stream(dev)
+    with torch.cuda.device(dev):
+        need = _LIB.qx_w4a16_gemv_workspace_size(max(M, 1), K, N, rank, group_size)
+        ws = _workspace.get(dev, st, need)
+        _lib.check(_LIB.qx_w4a16_lora_gemv(
+            input.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), packed,
+            int(zero_offset), _ptr(lora_A), _ptr(lora_B), out.data_ptr(), M, K, N, rank,
+            int(group_size), float(lora_scale), ws.data_ptr(), ws.numel(), st.cuda_stream),
+            "w4a16_gemv")
+    return out
+
+
+def w4a16_gemv(input, qweight, scales, zeros, group_size: int = 128, *, zero_offset: int = 0):
+    """``fp16(x . W)`` with ``W = s (q - z)`` from GPTQ int4 packing
+    (reference: ``csrc/kernels/w4a16_lora_gemv.cu:233-265``)."""
+    return _w4a16(input, qweight, scales, zeros, None, None, group_size, 0.0, zero_offset)
+
+
+def w4a16_lora_gemv(input, qweight, scales, zeros, lora_A, lora_B, group_size: int = 128,
+                    lora_alpha: float = 16.0, *, zero_offset: int = 0):
+    """``fp16(x . W + (alpha / r) (x . A) . B)``; ``r = lora_A.size(1)``
+    (reference: ``csrc/kernels/w4a16_lora_gemv.cu:268-323``)."""
+    r = lora_A.size(1)
+    scale = float(np.float32(lora_alpha) / np.float32(r))  # fp32 division, as w4a16_lora_gemv.cu:221
+    return _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, scale, zero_offset)
+
+
+# ------------------------------------------------------------- ring cache --
+def ring_slot_indices(count: int, sink: int, window: int, device) -> torch.Tensor:
+    """Logical-order slot list for ``count`` written tokens (int32, on device)."""
+    dev = torch.device(device)
+    valid = count if count <= sink else sink + min(count - sink, window)
+    out = torch.empty(max(valid, 1), dtype=torch.int32, device=dev)
+    st = _stream(dev)
+    n = _lib.check(_LIB.qx_ring_slot_indices(out.data_ptr(), sink, window, count, st.cuda_stream),
+                   "ring_slot_indices")
+    assert n == valid
+    return out[:valid]
+
+
+def decode_attention(q, k_cache, v_cache, count: int, sink: int, window: int,
+                     softmax_scale: float | None = None):
+    """GQA decode attention over the ring's valid slots, read in place.
+    ``q`` fp16 ``[B, Hq, D]``; ``k_cache``/``v_cache`` fp16 ``[B, S+W, Hkv, D]``."""
+    for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _check_input(t, n)
+        _check_fp16(t, n)
+    B, Hq, D = q.shape
+    if k_cache.dim() != 4 or k_cache.size(0) != B or k_cache.size(1) != sink + window or \
+            k_cache.size(3) != D or v_cache.shape != k_cache.shape:
+        raise RuntimeError("cache must be [B, sink + window, Hkv, D]")
+    Hkv = k_cache.size(2)
+    out = torch.empty_like(q)
+    dev = q.device
+    st = _stream(dev)
+    with torch.cuda.device(dev):
+        need = _LIB.qx_decode_attention_workspace_size(B, Hq, Hkv, D, sink, window)
+        ws = _workspace.get(dev, st, need)
+        _lib.check(_LIB.qx_decode_attention(
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), B, Hq, Hkv, D,
+            sink, window, int(count), float(softmax_scale or 0.0), ws.data_ptr(), ws.numel(),
+            st.cuda_stream), "decode_attention")
+    return out
+
+
+class RingBufferKVCache:
+    """StreamingLLM sink + ring-window KV cache (reference:
+    ``csrc/include/ring_buffer.h:32-77``, ``csrc/kv_cache/ring_buffer.cu``).
+
+    Storage: ``k``/``v`` fp16 ``[num_layers, batch, sink + window, kv_heads, head_dim]``
+    owned by this object.  ``write_count`` advances when the last layer is
+    appended (``ring_buffer.cu:138-140``).
+    """
+
+    def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, sink_size: int = 4,
+                 window_size: int = 4092, batch: int = 1, device=None):
+        if window_size < 1 or sink_size < 0:
+            raise RuntimeError("sink_size must be >= 0 and window_size >= 1")
+        self.num_layers, self.num_kv_heads, self.head_dim = num_layers, num_kv_heads, head_dim
+        self.sink_size, self.window_size = sink_size, window_size
+        self.total_size = sink_size + window_size
+        self.batch = batch
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if dev.type != "cuda":
+            raise RuntimeError("RingBufferKVCache lives on a CUDA device")
+        self.device = dev
+        shape = (num_layers, batch, self.total_size, num_kv_heads, head_dim)
+        self.k = torch.zeros(shape, dtype=torch.float16, device=dev)
+        self.v = torch.zeros(shape, dtype=torch.float16, device=dev)
+        self._write_count = 0
+
+    # --- reference methods (binding.cpp:67-74) ---
+    def append(self, new_k: torch.Tensor, new_v: torch.Tensor, layer_idx: int) -> None:
+        """``new_k``/``new_v``: ``[H, D]`` (one token, batch 1), ``[T, H, D]``
+        (batch 1) or ``[B, T, H, D]``."""
+        _check_input(new_k, "new_k")
+        _check_input(new_v, "new_v")
+        _check_fp16(new_k, "new_k")
+        _check_fp16(new_v, "new_v")
+        if new_k.shape != new_v.shape:
+            raise RuntimeError("new_k and new_v must have the same shape")
+        if not 0 <= layer_idx < self.num_layers:
+            raise RuntimeError(f"layer_idx {layer_idx} out of range")
+        if new_k.dim() == 2:
+            B, T = 1, 1
+        elif new_k.dim() == 3:
+            B, T = 1, new_k.size(0)
+        elif new_k.dim() == 4:
+            B, T = new_k.size(0), new_k.size(1)
+        else:
+            raise RuntimeError("new_k must be [H, D], [T, H, D] or [B, T, H, D]")
+        if B != self.batch or tuple(new_k.shape[-2:]) != (self.num_kv_heads, self.head_dim):
+            raise RuntimeError(f"new_k shape {list(new_k.shape)} does not match the cache "
+                               f"(batch={self.batch}, heads={self.num_kv_heads}, dim={self.head_dim})")
+        st = _stream(self.device)
+        _lib.check(_LIB.qx_ring_append(
+            self.k[layer_idx].data_ptr(), self.v[layer_idx].data_ptr(), new_k.data_ptr(),
+            new_v.data_ptr(), B, T, self.num_kv_heads, self.head_dim, self.sink_size,
+            self.window_size, self._write_count, st.cuda_stream), "ring_append")
+        if layer_idx == self.num_layers - 1:
+            self._write_count += T
+
+    def get_kv(self, layer_idx: int):
+        """(K, V) in logical order: ``[valid, H, D]`` for batch 1, else
+        ``[B, valid, H, D]`` (reference ``get_kv``, ``ring_buffer.cu:143-200``)."""
+        valid = self.get_valid_length()
+        shape = (self.batch, valid, self.num_kv_heads, self.head_dim)
+        ko = torch.empty(shape, dtype=torch.float16, device=self.device)
+        vo = torch.empty(shape, dtype=torch.float16, device=self.device)
+        st = _stream(self.device)
+        _lib.check(_LIB.qx_ring_gather(
+            self.k[layer_idx].data_ptr(), self.v[layer_idx].data_ptr(), ko.data_ptr(), vo.data_ptr(),
+            self.batch, self.num_kv_heads, self.head_dim, self.sink_size, self.window_size,
+            self._write_count, st.cuda_stream), "ring_gather")
+        if self.batch == 1:
+            return ko[0], vo[0]
+        return ko, vo
+
+    def get_valid_length(self) -> int:
+        c = self._write_count
+        if c <= self.sink_size:
+            return c
+        return self.sink_size + min(c - self.sink_size, self.window_size)
+
+    def get_total_written(self) -> int:
+        return self._write_count
+
+    def reset(self) -> None:
+        self._write_count = 0
+
+    # --- additions ---
+    def slot_indices(self) -> torch.Tensor:
+        return ring_slot_indices(self._write_count, self.sink_size, self.window_size, self.device)
+
+    def decode_attention(self, q: torch.Tensor, layer_idx: int,
+                         softmax_scale: float | None = None) -> torch.Tensor:
+        """Attention of ``q`` (``[B, Hq, D]`` or ``[Hq, D]``) over this layer's
+        valid slots, read in place."""
+        squeeze = q.dim() == 2
+        if squeeze:
+            q = q.unsqueeze(0)
+        out = decode_attention(q, self.k[layer_idx], self.v[layer_idx], self._write_count,
+                               self.sink_size, self.window_size, softmax_scale)
+        return out[0] if squeeze else out

@@ -1,0 +1,383 @@
+// GQA decode attention read in place from the StreamingLLM ring (sm_100a).
+//
+// New component: the reference has no attention kernel; it only materialises
+// K/V in logical order (get_kv, csrc/kv_cache/ring_buffer.cu:143-200) for an
+// external attention.  Softmax is order-independent, and the valid slots of
+// the ring are always the physical prefix [0, valid_length(count)) (sinks
+// fill 0..S-1, the window fills S..S+W-1 in order before it wraps), so this
+// kernel streams that prefix directly: no index list, no gather copy.
+//
+// Math (HF Qwen3 eager attention, transformers models/qwen3/modeling_qwen3.py:
+// repeat_kv + softmax(q k^T / sqrt(D)) v):  query head h reads KV head
+// h / (Hq / Hkv).  The G = Hq / Hkv query heads of one KV head are the 16
+// rows of an mma.sync m16n8k16 tile (rows >= G are zero padding), so every K/V
+// byte is read once per (sequence, KV head).
+//
+// Work decomposition (flash-decoding): grid = (chunks, batch * Hkv); a CTA
+// (4 warps) owns a chunk of slots, each warp takes 16-slot tiles staged by
+// cp.async into XOR-swizzled shared memory (double buffered), computes
+// S = Q K^T and O += P V on the tensor cores with an online softmax in fp32,
+// the warps merge in shared memory, each CTA writes (max, sum, O) for its
+// chunk, and the last CTA of each (sequence, KV head) merges the chunks and
+// writes fp16.
+#include <algorithm>
+#include <cmath>
+
+#include "qx_b200.h"
+#include "qx_common.cuh"
+
+namespace qx {
+namespace attn {
+
+constexpr int D = 128;
+constexpr int WARPS = 4;
+constexpr int THREADS = WARPS * 32;
+constexpr int TILE = 16;
+constexpr int ROW_BYTES = D * 2;                 // 256
+constexpr int TILE_BYTES = TILE * ROW_BYTES;     // 4 KB
+constexpr int WARP_SMEM = 2 * 2 * TILE_BYTES;    // 2 stages x (K, V)
+constexpr int SMEM = WARPS * WARP_SMEM;          // 64 KB
+constexpr int CHUNK_ALIGN = WARPS * TILE;        // 64 slots
+constexpr int CTAS_PER_SM = 3;
+constexpr int PSTRIDE = D + 2;                   // floats per (row) partial: m, l, O[D]
+
+struct Params {
+  const __half* q;
+  const __half* k;
+  const __half* v;
+  __half* out;
+  int Hq, Hkv, G, cap, valid, chunk, nch;
+  float scale_log2;
+  float* part;          // [B*Hkv][nch][G][PSTRIDE]
+  unsigned* counters;   // [B*Hkv]
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// byte offset of 16-byte chunk `ch` of tile row `r` (XOR swizzle: conflict-free ldmatrix)
+__device__ __forceinline__ uint32_t swz(int r, int ch) {
+  return uint32_t(r * ROW_BYTES + ((ch ^ (r & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ unsigned s_is_last;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int bh = blockIdx.y, ci = blockIdx.x;
+  const int b = bh / p.Hkv, kvh = bh - b * p.Hkv;
+  const int c0 = ci * p.chunk;
+  const int c1 = min(p.valid, c0 + p.chunk);
+  const int ntiles = (c1 - c0 + TILE - 1) / TILE;
+
+  const size_t slot_stride = size_t(p.Hkv) * D;  // halves between consecutive slots
+  const __half* kb = p.k + (size_t(b) * p.cap * p.Hkv + kvh) * D;
+  const __half* vb = p.v + (size_t(b) * p.cap * p.Hkv + kvh) * D;
+  unsigned char* wsm = smem + warp * WARP_SMEM;
+  const uint32_t wsm_u = smem_u32(wsm);
+
+  // Q fragments (rows = query heads of this KV head, k = head dim)
+  uint32_t qa[8][4];
+  {
+    const __half* qb = p.q + (size_t(b) * p.Hq + size_t(kvh) * p.G) * D;
+    const bool r0 = g < p.G, r1 = g + 8 < p.G;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int d0 = kk * 16 + 2 * c;
+      qa[kk][0] = r0 ? *reinterpret_cast<const uint32_t*>(qb + g * D + d0) : 0u;
+      qa[kk][1] = r1 ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * D + d0) : 0u;
+      qa[kk][2] = r0 ? *reinterpret_cast<const uint32_t*>(qb + g * D + d0 + 8) : 0u;
+      qa[kk][3] = r1 ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * D + d0 + 8) : 0u;
+    }
+  }
+
+  auto issue_tile = [&](int t, int stage) {
+    const uint32_t ks = wsm_u + stage * 2 * TILE_BYTES;
+    const uint32_t vs = ks + TILE_BYTES;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = i * 32 + lane;
+      const int r = idx >> 4, ch = idx & 15;
+      const int slot = c0 + t * TILE + r;
+      const bool ok = slot < c1;
+      const size_t off = ok ? size_t(slot) * slot_stride + ch * 8 : 0;
+      cp_async16(ks + swz(r, ch), kb + off, ok ? 16 : 0);
+      cp_async16(vs + swz(r, ch), vb + off, ok ? 16 : 0);
+    }
+    cp_async_commit();
+  };
+
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+
+  if (warp < ntiles) issue_tile(warp, 0);
+  for (int it = 0, t = warp; t < ntiles; ++it, t += WARPS) {
+    const int tn = t + WARPS;
+    if (tn < ntiles) {
+      issue_tile(tn, (it + 1) & 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncwarp();
+    const uint32_t ks = wsm_u + (it & 1) * 2 * TILE_BYTES;
+    const uint32_t vs = ks + TILE_BYTES;
+
+    // S = Q K^T : two n-tiles of 8 slots
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    {
+      const int mi = lane >> 3, ri = lane & 7;
+      const int row = 8 * (mi >> 1) + ri;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t bk[4];
+        ldsm_x4(bk, ks + swz(row, 2 * kk + (mi & 1)));
+        mma_16816(s[0], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], bk[0], bk[1]);
+        mma_16816(s[1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], bk[2], bk[3]);
+      }
+    }
+    // scale (log2 domain) and mask slots beyond the chunk
+    const int sbase = c0 + t * TILE;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int slot = sbase + 8 * j + 2 * c + (e & 1);
+        s[j][e] = slot < c1 ? s[j][e] * p.scale_log2 : -INFINITY;
+      }
+    // online softmax: rows g (e = 0,1) and g + 8 (e = 2,3)
+    float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+    float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m_r[0], mx0), mn1 = fmaxf(m_r[1], mx1);
+    const float al0 = exp2f(m_r[0] - mn0), al1 = exp2f(m_r[1] - mn1);
+    m_r[0] = mn0;
+    m_r[1] = mn1;
+    float pr[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      pr[j][0] = exp2f(s[j][0] - mn0);
+      pr[j][1] = exp2f(s[j][1] - mn0);
+      pr[j][2] = exp2f(s[j][2] - mn1);
+      pr[j][3] = exp2f(s[j][3] - mn1);
+    }
+    l_r[0] = l_r[0] * al0 + ((pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]));
+    l_r[1] = l_r[1] * al1 + ((pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]));
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= al0;
+      o[j][1] *= al0;
+      o[j][2] *= al1;
+      o[j][3] *= al1;
+    }
+    const uint32_t pa0 = pack_h2(pr[0][0], pr[0][1]);
+    const uint32_t pa1 = pack_h2(pr[0][2], pr[0][3]);
+    const uint32_t pa2 = pack_h2(pr[1][0], pr[1][1]);
+    const uint32_t pa3 = pack_h2(pr[1][2], pr[1][3]);
+    // O += P V : 16 n-tiles of 8 head dims
+    {
+      const int mi = lane >> 3, ri = lane & 7;
+      const int row = 8 * (mi & 1) + ri;
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        uint32_t bv[4];
+        ldsm_x4_t(bv, vs + swz(row, 2 * jj + (mi >> 1)));
+        mma_16816(o[2 * jj], pa0, pa1, pa2, pa3, bv[0], bv[1]);
+        mma_16816(o[2 * jj + 1], pa0, pa1, pa2, pa3, bv[2], bv[3]);
+      }
+    }
+    __syncwarp();
+  }
+  l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 1);
+  l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 2);
+  l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 1);
+  l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 2);
+
+  // merge the warps of this CTA in shared memory (reuses the tile buffers)
+  __syncthreads();
+  float* Os = reinterpret_cast<float*>(smem);            // [WARPS][16][D]
+  float* ms = Os + WARPS * 16 * D;                        // [WARPS][16]
+  float* ls = ms + WARPS * 16;                            // [WARPS][16]
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int d = 8 * j + 2 * c;
+    *reinterpret_cast<float2*>(Os + (warp * 16 + g) * D + d) = make_float2(o[j][0], o[j][1]);
+    *reinterpret_cast<float2*>(Os + (warp * 16 + g + 8) * D + d) = make_float2(o[j][2], o[j][3]);
+  }
+  if (c == 0) {
+    ms[warp * 16 + g] = m_r[0];
+    ms[warp * 16 + g + 8] = m_r[1];
+    ls[warp * 16 + g] = l_r[0];
+    ls[warp * 16 + g + 8] = l_r[1];
+  }
+  __syncthreads();
+  float* mypart = p.part + (size_t(bh) * p.nch + ci) * p.G * PSTRIDE;
+  {
+    const int d = tid;  // THREADS == D
+    for (int r = 0; r < p.G; ++r) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) mx = fmaxf(mx, ms[w * 16 + r]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) {
+        const float f = ms[w * 16 + r] == -INFINITY ? 0.f : exp2f(ms[w * 16 + r] - mx);
+        L = fmaf(ls[w * 16 + r], f, L);
+        O = fmaf(Os[(w * 16 + r) * D + d], f, O);
+      }
+      mypart[r * PSTRIDE + 2 + d] = O;
+      if (d == 0) {
+        mypart[r * PSTRIDE] = mx;
+        mypart[r * PSTRIDE + 1] = L;
+      }
+    }
+  }
+
+  // the last CTA of this (sequence, KV head) merges the chunks
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(p.counters + bh, 1u);
+    s_is_last = (prev == unsigned(p.nch - 1)) ? 1u : 0u;
+  }
+  __syncthreads();
+  if (!s_is_last) return;
+  __threadfence();
+  {
+    const int d = tid;
+    const float* pb = p.part + size_t(bh) * p.nch * p.G * PSTRIDE;
+    for (int r = 0; r < p.G; ++r) {
+      float mx = -INFINITY;
+      for (int k = 0; k < p.nch; ++k) mx = fmaxf(mx, __ldcg(pb + (size_t(k) * p.G + r) * PSTRIDE));
+      float L = 0.f, O = 0.f;
+      for (int k = 0; k < p.nch; ++k) {
+        const float* pk = pb + (size_t(k) * p.G + r) * PSTRIDE;
+        const float mk = __ldcg(pk);
+        const float f = mk == -INFINITY ? 0.f : exp2f(mk - mx);
+        L = fmaf(__ldcg(pk + 1), f, L);
+        O = fmaf(__ldcg(pk + 2 + d), f, O);
+      }
+      p.out[(size_t(b) * p.Hq + size_t(kvh) * p.G + r) * D + d] = __float2half_rn(O / L);
+    }
+  }
+  if (tid == 0) p.counters[bh] = 0u;
+}
+
+struct Plan {
+  int chunk, nch, nch_max;
+  size_t off_part, total;
+};
+
+static Plan make_plan(int batch, int kv_heads, int G, int cap, int valid, int sms) {
+  Plan pl{};
+  const int bh = batch * kv_heads;
+  const int target = std::max(1, sms * CTAS_PER_SM / std::max(1, bh));
+  const int max_by_cap = std::max(1, (cap + CHUNK_ALIGN - 1) / CHUNK_ALIGN);
+  pl.nch_max = std::min(target, max_by_cap);
+  const int v = std::max(valid, 1);
+  const int nch0 = std::max(1, std::min(target, (v + CHUNK_ALIGN - 1) / CHUNK_ALIGN));
+  int chunk = (v + nch0 - 1) / nch0;
+  chunk = (chunk + CHUNK_ALIGN - 1) / CHUNK_ALIGN * CHUNK_ALIGN;
+  pl.chunk = chunk;
+  pl.nch = (v + chunk - 1) / chunk;
+  pl.off_part = (size_t(bh) * 4 + 255) & ~size_t(255);
+  pl.total = pl.off_part + size_t(bh) * pl.nch_max * G * PSTRIDE * 4;
+  return pl;
+}
+
+}  // namespace attn
+}  // namespace qx
+
+using namespace qx;
+
+extern "C" size_t qx_decode_attention_workspace_size(int batch, int q_heads, int kv_heads,
+                                                     int head_dim, int sink, int window) {
+  if (batch <= 0 || kv_heads <= 0 || q_heads <= 0 || q_heads % kv_heads || window < 1 || sink < 0)
+    return 0;
+  (void)head_dim;
+  return attn::make_plan(batch, kv_heads, q_heads / kv_heads, sink + window, sink + window,
+                         device_sm_count())
+      .total;
+}
+
+extern "C" int qx_decode_attention(const void* q, const void* k_cache, const void* v_cache,
+                                   void* out, int batch, int q_heads, int kv_heads, int head_dim,
+                                   int sink, int window, int64_t count, float softmax_scale,
+                                   void* workspace, size_t workspace_bytes, qx_stream_t stream) {
+  QX_REQUIRE(batch > 0 && q_heads > 0 && kv_heads > 0 && q_heads % kv_heads == 0,
+             "decode_attention: bad heads q=%d kv=%d", q_heads, kv_heads);
+  QX_REQUIRE(head_dim == attn::D, "decode_attention: head_dim=%d unsupported (128)", head_dim);
+  QX_REQUIRE(q_heads / kv_heads <= 16, "decode_attention: GQA group %d > 16",
+             q_heads / kv_heads);
+  QX_REQUIRE(sink >= 0 && window >= 1, "decode_attention: sink=%d window=%d", sink, window);
+  QX_REQUIRE(count > 0, "decode_attention: empty cache (count=%lld)", (long long)count);
+  QX_REQUIRE(q && k_cache && v_cache && out, "decode_attention: null pointer");
+  QX_REQUIRE(aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(q, 4) && aligned(out, 2),
+             "decode_attention: misaligned tensors");
+  const int cap = sink + window;
+  const int64_t valid64 = count <= sink ? count : sink + std::min<int64_t>(count - sink, window);
+  const int valid = int(valid64);
+  const int G = q_heads / kv_heads;
+  const attn::Plan pl = attn::make_plan(batch, kv_heads, G, cap, valid, device_sm_count());
+  if (!workspace || workspace_bytes < pl.total || !aligned(workspace, 256))
+    return fail(QX_ERR_WORKSPACE, "decode_attention: workspace needs %zu bytes, 256-byte aligned",
+                pl.total);
+  attn::Params prm{};
+  prm.q = static_cast<const __half*>(q);
+  prm.k = static_cast<const __half*>(k_cache);
+  prm.v = static_cast<const __half*>(v_cache);
+  prm.out = static_cast<__half*>(out);
+  prm.Hq = q_heads;
+  prm.Hkv = kv_heads;
+  prm.G = G;
+  prm.cap = cap;
+  prm.valid = valid;
+  prm.chunk = pl.chunk;
+  prm.nch = pl.nch;
+  const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf(float(head_dim));
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  prm.counters = reinterpret_cast<unsigned*>(ws);
+  prm.part = reinterpret_cast<float*>(ws + pl.off_part);
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    QX_CUDA_TRY(cudaFuncSetAttribute(attn::decode_attn_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM),
+                "decode_attention: set smem limit");
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  attn::decode_attn_kernel<<<dim3(pl.nch, batch * kv_heads), attn::THREADS, attn::SMEM, st>>>(prm);
+  return check_launch("decode_attention");
+}
