@@ -210,7 +210,7 @@ def run_b200(args):
     if not qx._C_AVAILABLE:
         raise RuntimeError("native library missing")
 
-    nsets = int(np.ceil(2.2 * L2_BYTES / BYTES_PER_CALL))
+    nsets = args.nsets or int(np.ceil(2.2 * L2_BYTES / BYTES_PER_CALL))
     sets = make_weight_sets(torch, device, nsets)
     x = torch.randn(M, K, generator=torch.Generator(device=device).manual_seed(123), device=device).half()
     # correctness gate on set 0 against the oracle (rank 0, cheap)
@@ -270,9 +270,9 @@ def run_b200(args):
         # e2e through the public API: pinned host x -> device, GEMV, y -> pinned host
         x_host = torch.randn(M, K).half().pin_memory()
         y_host = torch.empty(M, N, dtype=torch.float16).pin_memory()
-        e_steps = max(1, min(steps, 2000))
+        e_steps = 0 if args.skip_e2e else max(1, min(steps, 2000))
         with torch.cuda.stream(stream):
-            for i in range(3):
+            for i in range(3 if e_steps else 0):
                 xd = x_host.to(device, non_blocking=True)
                 qw, sc, qz, A, B = sets[i % nsets]
                 y_host.copy_(qx.w4a16_lora_gemv(xd, qw, sc, qz, A, B, GROUP, ALPHA), non_blocking=True)
@@ -287,7 +287,7 @@ def run_b200(args):
                 y_host.copy_(qx.w4a16_lora_gemv(xd, qw, sc, qz, A, B, GROUP, ALPHA), non_blocking=True)
             e1.record(stream)
             e1.synchronize()
-        e_ms = e0.elapsed_time(e1)
+        e_ms = e0.elapsed_time(e1) if e_steps else float("nan")
     clocks = sampler.summary()
 
     if world > 1:
@@ -299,7 +299,7 @@ def run_b200(args):
     peak, peak_kind = measured_peaks()
     result = None
     if rank == 0:
-        cpu = cpu_gemv_baseline() if world == 1 else None
+        cpu = cpu_gemv_baseline() if (world == 1 and not args.skip_cpu) else None
         result = {
             "metric": METRIC,
             "value": achieved * world,
@@ -324,7 +324,8 @@ def run_b200(args):
                          "traffic": profiled_traffic(),
                          "algorithmic_bytes_per_launch": BYTES_PER_CALL,
                          "kernel": "qx::gemv::w4a16_gemv_kernel<1>"},
-            "e2e": {"value": BYTES_PER_CALL * e_steps / (e_ms / 1e3) / 1e9 * world, "unit": "GB/s",
+            "e2e": None if not e_steps else {
+                    "value": BYTES_PER_CALL * e_steps / (e_ms / 1e3) / 1e9 * world, "unit": "GB/s",
                     "us_per_call": e_ms * 1e3 / e_steps,
                     "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
                     "api": "qextract_infer_b200.w4a16_lora_gemv (ctypes C-ABI)"},
@@ -347,6 +348,10 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--nsets", type=int, default=0,
+                    help="weight sets in the rotation (default: enough for > 2x L2)")
+    ap.add_argument("--skip-e2e", action="store_true", help="omit the public-API timing")
+    ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -145,7 +145,7 @@ def _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale
     st = _stream(dev)
     with torch.cuda.device(dev):
         need = _LIB.qx_w4a16_gemv_workspace_size(max(M, 1), K, N, rank, group_size)
-        ws = _workspace.get(dev, st, need)
+        ws = _workspace.get(dev, st, need, "w4a16_gemv")
         _lib.check(_LIB.qx_w4a16_lora_gemv(
             input.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), packed,
             int(zero_offset), _ptr(lora_A), _ptr(lora_B), out.data_ptr(), M, K, N, rank,
@@ -199,7 +199,7 @@ def decode_attention(q, k_cache, v_cache, count: int, sink: int, window: int,
     st = _stream(dev)
     with torch.cuda.device(dev):
         need = _LIB.qx_decode_attention_workspace_size(B, Hq, Hkv, D, sink, window)
-        ws = _workspace.get(dev, st, need)
+        ws = _workspace.get(dev, st, need, "decode_attention")
         _lib.check(_LIB.qx_decode_attention(
             q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), B, Hq, Hkv, D,
             sink, window, int(count), float(softmax_scale or 0.0), ws.data_ptr(), ws.numel(),

@@ -1,10 +1,12 @@
-"""Per-(device, stream) scratch buffers for the kernels that reduce across CTAs.
+"""Per-(device, stream, op) scratch buffers for the kernels that reduce across CTAs.
 
 The library allocates nothing itself.  The split-K GEMV and the split-slot
-decode attention need a small workspace whose counters start at zero; every
-kernel leaves its counters at zero again, so one zero-filled buffer per
-stream is reused across calls (calls on one stream are ordered, so they never
-overlap on the buffer).
+decode attention need a workspace whose counter region starts at zero; each
+kernel leaves its counters at zero again (the rest of the buffer holds
+partial results), so one zero-filled buffer per (stream, op) is reused across
+calls.  Calls on one stream are ordered and never overlap on the buffer; ops
+of different kinds get different buffers because one op's partials would
+otherwise sit where the other keeps its counters.
 """
 
 from __future__ import annotations
@@ -17,10 +19,10 @@ _lock = threading.Lock()
 _buffers: dict = {}
 
 
-def get(device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> torch.Tensor:
+def get(device: torch.device, stream: torch.cuda.Stream, nbytes: int, op: str) -> torch.Tensor:
     """A zero-initialised uint8 buffer of at least ``nbytes`` (256-byte aligned)
-    dedicated to ``stream`` on ``device``."""
-    key = (device.index, stream.cuda_stream)
+    dedicated to ``op`` on ``stream`` of ``device``."""
+    key = (device.index, stream.cuda_stream, op)
     with _lock:
         buf = _buffers.get(key)
         if buf is None or buf.numel() < nbytes:

@@ -40,6 +40,7 @@ constexpr int SMEM = WARPS * WARP_SMEM;          // 64 KB
 constexpr int CHUNK_ALIGN = WARPS * TILE;        // 64 slots
 constexpr int CTAS_PER_SM = 3;
 constexpr int PSTRIDE = D + 2;                   // floats per (row) partial: m, l, O[D]
+constexpr int COUNTER_SLOTS = 4096;              // fixed counter region at the workspace start
 
 struct Params {
   const __half* q;
@@ -309,7 +310,7 @@ static Plan make_plan(int batch, int kv_heads, int G, int cap, int valid, int sm
   chunk = (chunk + CHUNK_ALIGN - 1) / CHUNK_ALIGN * CHUNK_ALIGN;
   pl.chunk = chunk;
   pl.nch = (v + chunk - 1) / chunk;
-  pl.off_part = (size_t(bh) * 4 + 255) & ~size_t(255);
+  pl.off_part = size_t(COUNTER_SLOTS) * 4;
   pl.total = pl.off_part + size_t(bh) * pl.nch_max * G * PSTRIDE * 4;
   return pl;
 }
@@ -340,6 +341,8 @@ extern "C" int qx_decode_attention(const void* q, const void* k_cache, const voi
              q_heads / kv_heads);
   QX_REQUIRE(sink >= 0 && window >= 1, "decode_attention: sink=%d window=%d", sink, window);
   QX_REQUIRE(count > 0, "decode_attention: empty cache (count=%lld)", (long long)count);
+  QX_REQUIRE(batch * kv_heads <= attn::COUNTER_SLOTS, "decode_attention: batch*kv_heads > %d",
+             attn::COUNTER_SLOTS);
   QX_REQUIRE(q && k_cache && v_cache && out, "decode_attention: null pointer");
   QX_REQUIRE(aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(q, 4) && aligned(out, 2),
              "decode_attention: misaligned tensors");

@@ -45,6 +45,9 @@ constexpr int U = 8;              // k-steps of weights held in registers at onc
 constexpr int MROWS = 32;         // batch rows per launch (4 n-tiles of 8)
 constexpr int HMC = 2;            // batch rows per pass of the LoRA-down loop
 constexpr int TS_CAP = 48;        // max k-steps per split (bounds shared memory)
+// The workspace starts with a fixed-size counter region, so that counters of
+// one call never overlap the partials of a call with a different shape.
+constexpr int COUNTER_SLOTS = 8192;
 // residency the split heuristic plans for (and the kernel's launch bound)
 __host__ __device__ constexpr int ctas_per_sm(int nt) { return nt == 1 ? 3 : 2; }
 
@@ -90,7 +93,7 @@ static Plan make_plan(int M, int K, int N, int rank, int group, int sms) {
             + size_t(2) * pl.ng_max * COLS * 4         // sc, zs
             + size_t(pl.NT) * 8 * rank * 4             // hs
             + size_t(WARPS) * HMC * rank * 4;          // red
-  pl.off_partial = align256(size_t(pl.tiles) * 4);
+  pl.off_partial = align256(size_t(COUNTER_SLOTS) * 4);
   pl.off_hpart = pl.off_partial + align256(size_t(S) * mc * N * 4);
   pl.total = pl.off_hpart + align256(size_t(pl.tiles) * S * mc * std::max(rank, 1) * 4);
   return pl;
@@ -408,6 +411,7 @@ extern "C" int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const v
   QX_REQUIRE(group_size > 0 && group_size % gemv::KSTEP == 0 && K % group_size == 0,
              "w4a16_gemv: group_size=%d must be a multiple of 32 dividing K=%d", group_size, K);
   QX_REQUIRE(N % 8 == 0, "w4a16_gemv: N=%d must be a multiple of 8", N);
+  QX_REQUIRE(N <= gemv::COLS * gemv::COUNTER_SLOTS, "w4a16_gemv: N=%d too large", N);
   QX_REQUIRE(rank == 0 || rank == 8 || rank == 16 || rank == 32 || rank == 64 || rank == 128,
              "w4a16_gemv: LoRA rank %d unsupported (0, 8, 16, 32, 64 or 128)", rank);
   QX_REQUIRE(x && qweight && scales && zeros && y, "w4a16_gemv: null tensor pointer");

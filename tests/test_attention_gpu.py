@@ -80,3 +80,13 @@ def test_cache_object_path(C):
     assert_close(out, ref, RTOL, ATOL, "cache object")
     pos = RingIndexOracle(4, 60).positions(100)
     np.testing.assert_array_equal(to_np(k), ks[pos])
+
+
+def test_after_gemv_with_many_tiles(C):
+    """Attention after a GEMV whose tile count exceeds 64 on the same stream
+    (the two ops keep separate workspaces)."""
+    from oracle import make_gemv_inputs
+    d = make_gemv_inputs(1, 1024, 24576, 16, seed=1)
+    t = {k: dev_tensor(v) for k, v in d.items()}
+    C.w4a16_lora_gemv(t["x"], t["qweight"], t["scales"], t["zeros"], t["lora_A"], t["lora_B"])
+    _run(C, 32, 32, 8, 4, 4092, 4096 + 5, seed=77)

@@ -189,13 +189,14 @@ def test_lora_contribution(C):
 def test_shared_workspace_across_shapes(C):
     """Counters are left at zero: interleaved shapes on one stream stay correct."""
     cases = [make_gemv_inputs(m, k, n, 16, seed=s) for (m, k, n, s) in
-             [(1, 2560, 9728, 1), (5, 4096, 1024, 2), (1, 12288, 4096, 3), (1, 2560, 9728, 1)]]
+             [(1, 2560, 9728, 1), (5, 4096, 1024, 2), (1, 12288, 4096, 3), (1, 2560, 9728, 1),
+              (1, 256, 1024, 4), (1, 1024, 24576, 5)]]
     outs = []
     for d in cases:
         t = _dev(d)
         outs.append(to_np(C.w4a16_lora_gemv(t["x"], t["qweight"], t["scales"], t["zeros"],
                                             t["lora_A"], t["lora_B"], 128, 32.0)))
-    for d, y in zip(cases[1:3], outs[1:3]):
+    for d, y in zip(cases[1:3] + cases[4:], outs[1:3] + outs[4:]):
         ref = cbind.c_w4a16_lora_gemv(d["x"], d["qweight"], d["scales"], d["zeros"], d["lora_A"],
                                       d["lora_B"], 128, 32.0)
         assert_close(y, ref, RTOL, ATOL, "interleaved")
