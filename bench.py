@@ -247,23 +247,26 @@ def run_b200(args):
 
     g_warm = capture(warm, 0)
     g_timed = capture(steps, warm)
-    for _ in range(2):
-        g_warm.replay()
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            g_warm.replay()
     stream.synchronize()
     # sustained load so the clock sampler sees the GPU busy, then the timed region
     sampler = ClockSampler(device.index)
     with sampler:
         t_end = time.time() + 1.0
         while time.time() < t_end:
-            g_warm.replay()
+            with torch.cuda.stream(stream):
+                g_warm.replay()
             stream.synchronize()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(device)
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ev0.record(stream)
-        g_timed.replay()
-        ev1.record(stream)
+        with torch.cuda.stream(stream):  # replay() launches on the current stream
+            ev0.record(stream)
+            g_timed.replay()
+            ev1.record(stream)
         ev1.synchronize()
         torch.cuda.synchronize(device)
         ms = ev0.elapsed_time(ev1)
@@ -342,6 +345,99 @@ def run_b200(args):
     return 0
 
 
+def _graph_time_us(torch, stream, fn, nsteps, reps=3):
+    """Capture fn(i) for i < nsteps into a CUDA graph; return the best of
+    `reps` replays in microseconds per step (CUDA events on `stream`)."""
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            fn(i)
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(nsteps):
+            fn(i)
+    g.replay()
+    stream.synchronize()
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1) * 1e3 / nsteps)
+    del g
+    return best
+
+
+def run_kernel_suite(args):
+    """Secondary kernels at the RMSNorm/SwiGLU and ring-cache configurations:
+    one JSON line per (kernel, shape) with us/call, GB/s and HBM fraction.
+    Inputs rotate over buffers totalling > 2x L2 where one call is smaller."""
+    import numpy as np
+    import torch
+    import qextract_infer_b200 as qx
+    from qextract_infer_b200 import _C
+    dev = torch.device("cuda", torch.cuda.current_device())
+    st = torch.cuda.Stream(dev)
+    peak, peak_kind = measured_peaks()
+    gen = torch.Generator(device=dev).manual_seed(1)
+    steps = max(50, min(args.steps, 400))
+
+    def nbuf(nbytes):
+        return int(min(64, max(1, np.ceil(2.2 * L2_BYTES / max(nbytes, 1)))))
+
+    def emit(kernel, shape, nbytes, us, extra=None):
+        gbs = nbytes / us / 1e3
+        d = {"metric": f"{kernel} us & HBM GB/s", "kernel": kernel, "shape": shape,
+             "us_per_call": us, "bytes_per_call": int(nbytes), "GB/s": gbs,
+             "hbm_frac": gbs / peak, "peak": peak, "peak_kind": peak_kind}
+        if extra:
+            d.update(extra)
+        print(json.dumps(d), flush=True)
+
+    for H in (2560, 4096):
+        w = (torch.randn(H, generator=gen, device=dev) * 0.1 + 1).half()
+        for T in (1, 8, 64, 4096):
+            nb = 2 * T * H * 2 + H * 2
+            xs = [torch.randn(T, H, generator=gen, device=dev).half() for _ in range(nbuf(nb))]
+            us = _graph_time_us(torch, st, lambda i: _C.fused_rmsnorm(xs[i % len(xs)], w, 1e-6), steps)
+            emit("fused_rmsnorm", {"T": T, "H": H}, nb, us)
+    for I in (9728, 12288):
+        for T in (1, 8, 64, 4096):
+            nb = 3 * T * I * 2
+            n = nbuf(nb)
+            gs = [torch.randn(T, I, generator=gen, device=dev).half() for _ in range(n)]
+            ups = [torch.randn(T, I, generator=gen, device=dev).half() for _ in range(n)]
+            us = _graph_time_us(torch, st, lambda i: _C.fused_swiglu(gs[i % n], ups[i % n]), steps)
+            emit("fused_swiglu", {"T": T, "I": I}, nb, us)
+    # ring cache, Qwen3-8B geometry: 36 layers x 8 KV heads x 128, 4 + 4092 slots
+    L, Hkv, D, S, W = 36, 8, 128, 4, 4092
+    cache = qx.QExtractKVCache(L, Hkv, D, sink_size=S, window_size=W)
+    for T in (2048, 1):
+        kn = torch.randn(T, Hkv, D, generator=gen, device=dev).half()
+        vn = torch.randn(T, Hkv, D, generator=gen, device=dev).half()
+        kk, vv = (kn, vn) if T > 1 else (kn[0], vn[0])
+        nb = 2 * 2 * T * Hkv * D * 2  # read new K/V + write K/V
+        us = _graph_time_us(torch, st, lambda i: cache.append(kk, vv, i % L), min(steps, 2 * L))
+        emit("ring_append", {"tokens": T, "kv_heads": Hkv, "head_dim": D, "sink": S, "window": W},
+             nb, us, {"per": "layer"})
+    # decode attention over a full ring (4096 valid slots) per layer, B = 1 and 32
+    for B in (1, 32):
+        c2 = qx.QExtractKVCache(L if B == 1 else 2, Hkv, D, sink_size=S, window_size=W, batch=B)
+        c2.k_cache.normal_(generator=gen)
+        c2.v_cache.normal_(generator=gen)
+        c2._backend._write_count = 32768 + 64
+        q = torch.randn(B, 32, D, generator=gen, device=dev).half()
+        nl = c2.num_layers
+        nb = B * (2 * (S + W) * Hkv * D * 2 + 2 * 32 * D * 2)
+        us = _graph_time_us(torch, st, lambda i: c2.decode_attention(q, i % nl), min(steps, 4 * nl))
+        emit("decode_attention", {"batch": B, "q_heads": 32, "kv_heads": Hkv, "head_dim": D,
+                                  "valid_slots": S + W}, nb, us, {"per": "layer"})
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -352,7 +448,11 @@ def main():
                     help="weight sets in the rotation (default: enough for > 2x L2)")
     ap.add_argument("--skip-e2e", action="store_true", help="omit the public-API timing")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline")
+    ap.add_argument("--workload", choices=["decode_gemv", "kernels"], default="decode_gemv",
+                    help="decode_gemv: the headline line; kernels: RMSNorm/SwiGLU/ring/attention lines")
     args = ap.parse_args()
+    if args.workload == "kernels":
+        return run_kernel_suite(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)

@@ -56,19 +56,24 @@ const char* qx_version(void);
  *   lora_scale  = lora_alpha / rank   (the reference computes it at w4a16_lora_gemv.cu:221)
  *   y        fp16  [M, N]
  * Constraints: K % 32 == 0, group_size % 32 == 0, K % group_size == 0,
- * N % 8 == 0, rank in {0, 8, 16, 32, 64, 128}, x/qweight/lora_A 16-byte aligned.
+ * N % 8 == 0, rank in {0, 8, 16, 32, 64, 128}; x, qweight, scales, lora_A,
+ * lora_B (and fp16 zeros) 16-byte aligned.
  * Any M >= 1 (rows are processed 32 at a time).
- * workspace: >= qx_w4a16_gemv_workspace_size(M, K, N, rank, group_size) bytes,
- * 256-byte aligned, zero-filled before its first use; every call leaves it
- * zero-filled again.  Calls that share a workspace must be stream-ordered.
+ * No workspace: each group of CTAs that splits K forms a thread-block cluster
+ * and reduces through distributed shared memory.
  * ---------------------------------------------------------------------- */
-size_t qx_w4a16_gemv_workspace_size(int M, int K, int N, int rank, int group_size);
-
 int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const void* scales,
                        const void* zeros, int zeros_packed, int zero_offset,
                        const void* lora_A, const void* lora_B, void* y,
                        int M, int K, int N, int rank, int group_size, float lora_scale,
-                       void* workspace, size_t workspace_bytes, qx_stream_t stream);
+                       qx_stream_t stream);
+
+/* Programmatic dependent launch for the GEMV (off by default).  When on, a
+ * GEMV may start while the previous kernel in its stream is still running:
+ * it streams its weights and stages scales / zeros / LoRA factors before
+ * waiting for that kernel, so those operands must not be written by the
+ * kernel immediately before it (true for model weights).  Returns 0. */
+int qx_set_pdl(int enable);
 
 /* ------------------------------------------------------------------------
  * Fused RMSNorm.  Replaces fused_rmsnorm() (csrc/kernels/rmsnorm.cu:162-210,

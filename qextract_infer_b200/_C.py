@@ -144,13 +144,10 @@ def _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale
     dev = input.device
     st = _stream(dev)
     with torch.cuda.device(dev):
-        need = _LIB.qx_w4a16_gemv_workspace_size(max(M, 1), K, N, rank, group_size)
-        ws = _workspace.get(dev, st, need, "w4a16_gemv")
         _lib.check(_LIB.qx_w4a16_lora_gemv(
             input.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), packed,
             int(zero_offset), _ptr(lora_A), _ptr(lora_B), out.data_ptr(), M, K, N, rank,
-            int(group_size), float(lora_scale), ws.data_ptr(), ws.numel(), st.cuda_stream),
-            "w4a16_gemv")
+            int(group_size), float(lora_scale), st.cuda_stream), "w4a16_gemv")
     return out
 
 

@@ -23,10 +23,10 @@ c_int, c_int64, c_float, c_size_t, c_void_p, c_char_p = (
 SIGNATURES = {
     "qx_last_error": (c_char_p, []),
     "qx_version": (c_char_p, []),
-    "qx_w4a16_gemv_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "qx_w4a16_lora_gemv": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p,
                                    c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float,
-                                   c_void_p, c_size_t, c_void_p]),
+                                   c_void_p]),
+    "qx_set_pdl": (c_int, [c_int]),
     "qx_fused_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_void_p]),
     "qx_fused_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "qx_ring_append": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
@@ -56,11 +56,15 @@ def load(path: str | None = None):
             raise ImportError(
                 f"qextract_infer_b200: native library not built ({p} missing); run "
                 "`python -m qextract_infer_b200.build`")
-        lib = ctypes.CDLL(p)
-        for name, (res, args) in SIGNATURES.items():
-            fn = getattr(lib, name)
-            fn.restype = res
-            fn.argtypes = args
+        try:
+            lib = ctypes.CDLL(p)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+        except (OSError, AttributeError) as e:  # unloadable or stale build
+            raise ImportError(f"qextract_infer_b200: cannot use {p}: {e}; rebuild with "
+                              "`python -m qextract_infer_b200.build --force`") from e
         _lib = lib
         return lib
 
