@@ -39,8 +39,12 @@ constexpr int WARP_SMEM = 2 * 2 * TILE_BYTES;    // 2 stages x (K, V)
 constexpr int SMEM = WARPS * WARP_SMEM;          // 64 KB
 constexpr int CHUNK_ALIGN = WARPS * TILE;        // 64 slots
 constexpr int CTAS_PER_SM = 3;
-constexpr int PSTRIDE = D + 2;                   // floats per (row) partial: m, l, O[D]
+constexpr int PSTRIDE = D + 4;                   // floats per (row) partial: m, l, pad, pad, O[D]
 constexpr int COUNTER_SLOTS = 4096;              // fixed counter region at the workspace start
+constexpr int MAX_CHUNKS = 64;                   // bounds the merge's shared memory
+static_assert(THREADS == D, "one thread per head dimension in the merges");
+static_assert(WARPS == 4, "the chunk merge interleaves 4 chunk subsets, one per warp");
+static_assert(2 * 16 * MAX_CHUNKS * 4 + 16 * 4 + 4 * 16 * D * 4 <= SMEM, "merge fits the tile smem");
 
 struct Params {
   const __half* q;
@@ -49,7 +53,7 @@ struct Params {
   __half* out;
   int Hq, Hkv, G, cap, valid, chunk, nch;
   float scale_log2;
-  float* part;          // [B*Hkv][nch][G][PSTRIDE]
+  float* part;          // [B*Hkv][nch][G][PSTRIDE], O 16-byte aligned
   unsigned* counters;   // [B*Hkv]
 };
 
@@ -255,7 +259,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
         L = fmaf(ls[w * 16 + r], f, L);
         O = fmaf(Os[(w * 16 + r) * D + d], f, O);
       }
-      mypart[r * PSTRIDE + 2 + d] = O;
+      mypart[r * PSTRIDE + 4 + d] = O;
       if (d == 0) {
         mypart[r * PSTRIDE] = mx;
         mypart[r * PSTRIDE + 1] = L;
@@ -274,20 +278,55 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
   if (!s_is_last) return;
   __threadfence();
   {
-    const int d = tid;
-    const float* pb = p.part + size_t(bh) * p.nch * p.G * PSTRIDE;
-    for (int r = 0; r < p.G; ++r) {
+    // Merge the chunks with every load issued up front (no serial chains):
+    // (1) all (max, sum) pairs, (2) the chunk weights, (3) O by 4 interleaved
+    // chunk subsets with 16-byte loads, (4) fixed-order sum of the subsets.
+    const int G = p.G, nch = p.nch;
+    const float* pb = p.part + size_t(bh) * nch * G * PSTRIDE;
+    float* sm_m = reinterpret_cast<float*>(smem);  // [G][nch]
+    float* sm_l = sm_m + G * nch;                  // [G][nch]
+    float* sm_L = sm_l + G * nch;                  // [16]
+    float* sm_o = sm_L + 16;                       // [4][G][D]
+    for (int i = tid; i < G * nch; i += THREADS) {
+      const int r = i / nch, k = i - r * nch;
+      const float* pk = pb + (size_t(k) * G + r) * PSTRIDE;
+      sm_m[i] = __ldcg(pk);
+      sm_l[i] = __ldcg(pk + 1);
+    }
+    __syncthreads();
+    if (tid < G) {
       float mx = -INFINITY;
-      for (int k = 0; k < p.nch; ++k) mx = fmaxf(mx, __ldcg(pb + (size_t(k) * p.G + r) * PSTRIDE));
-      float L = 0.f, O = 0.f;
-      for (int k = 0; k < p.nch; ++k) {
-        const float* pk = pb + (size_t(k) * p.G + r) * PSTRIDE;
-        const float mk = __ldcg(pk);
-        const float f = mk == -INFINITY ? 0.f : exp2f(mk - mx);
-        L = fmaf(__ldcg(pk + 1), f, L);
-        O = fmaf(__ldcg(pk + 2 + d), f, O);
+      for (int k = 0; k < nch; ++k) mx = fmaxf(mx, sm_m[tid * nch + k]);
+      float L = 0.f;
+      for (int k = 0; k < nch; ++k) {
+        const float f = sm_m[tid * nch + k] == -INFINITY ? 0.f : exp2f(sm_m[tid * nch + k] - mx);
+        sm_m[tid * nch + k] = f;  // reuse as the chunk weight
+        L = fmaf(sm_l[tid * nch + k], f, L);
       }
-      p.out[(size_t(b) * p.Hq + size_t(kvh) * p.G + r) * D + d] = __float2half_rn(O / L);
+      sm_L[tid] = L;
+    }
+    __syncthreads();
+    const int d4 = tid & 31, kq = tid >> 5;
+    for (int r = 0; r < G; ++r) {
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+      for (int k = kq; k < nch; k += 4) {
+        const float4 v =
+            __ldcg(reinterpret_cast<const float4*>(pb + (size_t(k) * G + r) * PSTRIDE + 4) + d4);
+        const float f = sm_m[r * nch + k];
+        a.x = fmaf(f, v.x, a.x);
+        a.y = fmaf(f, v.y, a.y);
+        a.z = fmaf(f, v.z, a.z);
+        a.w = fmaf(f, v.w, a.w);
+      }
+      *reinterpret_cast<float4*>(sm_o + (kq * G + r) * D + 4 * d4) = a;
+    }
+    __syncthreads();
+    const int d = tid;
+    for (int r = 0; r < G; ++r) {
+      const float O = ((sm_o[(0 * G + r) * D + d] + sm_o[(1 * G + r) * D + d]) +
+                       sm_o[(2 * G + r) * D + d]) + sm_o[(3 * G + r) * D + d];
+      p.out[(size_t(b) * p.Hq + size_t(kvh) * G + r) * D + d] = __float2half_rn(O / sm_L[r]);
     }
   }
   if (tid == 0) p.counters[bh] = 0u;
@@ -301,7 +340,7 @@ struct Plan {
 static Plan make_plan(int batch, int kv_heads, int G, int cap, int valid, int sms) {
   Plan pl{};
   const int bh = batch * kv_heads;
-  const int target = std::max(1, sms * CTAS_PER_SM / std::max(1, bh));
+  const int target = std::min(MAX_CHUNKS, std::max(1, sms * CTAS_PER_SM / std::max(1, bh)));
   const int max_by_cap = std::max(1, (cap + CHUNK_ALIGN - 1) / CHUNK_ALIGN);
   pl.nch_max = std::min(target, max_by_cap);
   const int v = std::max(valid, 1);
