@@ -44,7 +44,7 @@ constexpr int COUNTER_SLOTS = 4096;              // fixed counter region at the 
 constexpr int MAX_CHUNKS = 64;                   // bounds the merge's shared memory
 static_assert(THREADS == D, "one thread per head dimension in the merges");
 static_assert(WARPS == 4, "the chunk merge interleaves 4 chunk subsets, one per warp");
-static_assert(2 * 16 * MAX_CHUNKS * 4 + 16 * 4 + 4 * 16 * D * 4 <= SMEM, "merge fits the tile smem");
+static_assert(2 * 16 * MAX_CHUNKS * 4 + 32 * 4 + 4 * 16 * D * 4 <= SMEM, "merge fits the tile smem");
 
 struct Params {
   const __half* q;
@@ -286,7 +286,8 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
     float* sm_m = reinterpret_cast<float*>(smem);  // [G][nch]
     float* sm_l = sm_m + G * nch;                  // [G][nch]
     float* sm_L = sm_l + G * nch;                  // [16]
-    float* sm_o = sm_L + 16;                       // [4][G][D]
+    // [4][G][D], 16-byte aligned for the float4 stores
+    float* sm_o = sm_m + ((2 * G * nch + 16 + 3) & ~3);
     for (int i = tid; i < G * nch; i += THREADS) {
       const int r = i / nch, k = i - r * nch;
       const float* pk = pb + (size_t(k) * G + r) * PSTRIDE;

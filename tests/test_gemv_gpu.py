@@ -212,3 +212,25 @@ def test_error_messages(C):
         C.w4a16_gemv(t["x"], t["qweight"].t(), t["scales"], t["zeros"])
     with pytest.raises(RuntimeError, match="packed rows"):
         C.w4a16_gemv(t["x"][..., :128], t["qweight"], t["scales"], t["zeros"])
+
+
+@pytest.mark.parametrize("xscale", [1.0, 30.0])
+def test_accumulation_precision(C, xscale):
+    """The fp16 output stays within half an fp16 ulp (plus 1e-4 of the output
+    range) of a float64 evaluation with unrounded weights, including large
+    activations (the dot products carry the magic-number offsets until the
+    per-group correction)."""
+    d = make_gemv_inputs(4, 4096, 1024, 16, seed=21)
+    d["x"] = (d["x"].astype(np.float32) * xscale).astype(np.float16)
+    t = _dev(d)
+    y = to_np(C.w4a16_lora_gemv(t["x"], t["qweight"], t["scales"], t["zeros"], t["lora_A"],
+                                t["lora_B"], 128, 32.0)).astype(np.float64)
+    q = unpack_int4_rows(d["qweight"]).astype(np.float64)
+    z = unpack_qzeros(d["zeros"], 1024).astype(np.float64)
+    gidx = np.arange(4096) // 128
+    W = (q - z[gidx]) * d["scales"].astype(np.float64)[gidx]
+    x64 = d["x"].astype(np.float64)
+    y64 = x64 @ W + 2.0 * ((x64 @ d["lora_A"].astype(np.float64)) @ d["lora_B"].astype(np.float64))
+    ulp = np.spacing(np.abs(y64).astype(np.float16)).astype(np.float64)
+    excess = np.abs(y - y64) - 0.5 * ulp
+    assert excess.max() <= 1e-4 * np.abs(y64).max(), (excess.max(), np.abs(y64).max())
