@@ -142,6 +142,31 @@ int qx_decode_attention(const void* q, const void* k_cache, const void* v_cache,
                         int window, int64_t count, float softmax_scale, void* workspace,
                         size_t workspace_bytes, qx_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Allocation-free decode attention.  No counterpart in the reference.
+ * For callers that cannot allocate device memory when attention runs (a host
+ * framework that owns the device heap, a server plugin handed only its
+ * input/output buffers, or a path where cudaMalloc would synchronise the
+ * device): same arguments and results as qx_decode_attention, but the
+ * scratch is one array of QX_DECODE_ATTN_NOALLOC_SCRATCH_BYTES built into the
+ * library (held by every GPU that loads it until the process exits) instead
+ * of a caller workspace.  Shapes whose scratch exceeds that size are rejected
+ * with QX_ERR_UNSUPPORTED and a message (Qwen3-8B geometry, 32 query / 8 KV
+ * heads, 4 + 4092 slots, fits up to batch 32).
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) for that device; make that first call before any
+ * stream capture.  Each call clears the counters it needs with
+ * cudaMemsetAsync on `stream` and allocates nothing.  All calls share the
+ * one array: calls that overlap on the GPU (different streams, or different
+ * host threads) race on it and must be serialised by the caller.
+ * ---------------------------------------------------------------------- */
+#define QX_DECODE_ATTN_NOALLOC_SCRATCH_BYTES (4 << 20)
+
+int qx_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                void* out, int batch, int q_heads, int kv_heads, int head_dim,
+                                int sink, int window, int64_t count, float softmax_scale,
+                                qx_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

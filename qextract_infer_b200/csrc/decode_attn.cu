@@ -22,6 +22,7 @@
 // writes fp16.
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 #include "qx_b200.h"
 #include "qx_common.cuh"
@@ -423,4 +424,103 @@ extern "C" int qx_decode_attention(const void* q, const void* k_cache, const voi
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   attn::decode_attn_kernel<<<dim3(pl.nch, batch * kv_heads), attn::THREADS, attn::SMEM, st>>>(prm);
   return check_launch("decode_attention");
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of qx_decode_attention.
+//
+// Some callers cannot allocate device memory when they run attention: a host
+// framework that owns the device heap and forbids side allocations, a plugin
+// of an inference server that is handed only its input and output buffers, or
+// a latency-critical path where cudaMalloc/cudaFree would synchronise the
+// device.  This entry point keeps the kernel's scratch (the per-(sequence, KV
+// head) counters and the per-chunk partial results) in one array compiled into
+// the library instead of a caller workspace.
+namespace qx {
+namespace attn {
+
+// Every GPU that loads the library holds this array until the process exits.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[QX_DECODE_ATTN_NOALLOC_SCRATCH_BYTES];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64] = {};
+
+// Device address of the array on the current device, looked up once per device
+// (the host-side name is only a stand-in and must never reach a kernel).
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  QX_CUDA_TRY(cudaGetDevice(&dev), "decode_attention_noalloc: cudaGetDevice");
+  QX_REQUIRE(dev >= 0 && dev < 64, "decode_attention_noalloc: device index %d unsupported", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    QX_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch),
+                "decode_attention_noalloc: cudaGetSymbolAddress");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return QX_OK;
+}
+
+}  // namespace attn
+}  // namespace qx
+
+extern "C" int qx_decode_attention_noalloc(const void* q, const void* k_cache,
+                                           const void* v_cache, void* out, int batch, int q_heads,
+                                           int kv_heads, int head_dim, int sink, int window,
+                                           int64_t count, float softmax_scale,
+                                           qx_stream_t stream) {
+  QX_REQUIRE(batch > 0 && q_heads > 0 && kv_heads > 0 && q_heads % kv_heads == 0,
+             "decode_attention_noalloc: bad heads q=%d kv=%d", q_heads, kv_heads);
+  QX_REQUIRE(head_dim == attn::D, "decode_attention_noalloc: head_dim=%d unsupported (128)",
+             head_dim);
+  QX_REQUIRE(q_heads / kv_heads <= 16, "decode_attention_noalloc: GQA group %d > 16",
+             q_heads / kv_heads);
+  QX_REQUIRE(sink >= 0 && window >= 1, "decode_attention_noalloc: sink=%d window=%d", sink,
+             window);
+  QX_REQUIRE(count > 0, "decode_attention_noalloc: empty cache (count=%lld)", (long long)count);
+  QX_REQUIRE(batch * kv_heads <= attn::COUNTER_SLOTS,
+             "decode_attention_noalloc: batch*kv_heads > %d", attn::COUNTER_SLOTS);
+  QX_REQUIRE(q && k_cache && v_cache && out, "decode_attention_noalloc: null pointer");
+  QX_REQUIRE(aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(q, 4) && aligned(out, 2),
+             "decode_attention_noalloc: misaligned tensors");
+  const int cap = sink + window;
+  const int64_t valid64 = count <= sink ? count : sink + std::min<int64_t>(count - sink, window);
+  const int valid = int(valid64);
+  const int G = q_heads / kv_heads;
+  const attn::Plan pl = attn::make_plan(batch, kv_heads, G, cap, valid, device_sm_count());
+  if (pl.total > size_t(QX_DECODE_ATTN_NOALLOC_SCRATCH_BYTES))
+    return fail(QX_ERR_UNSUPPORTED,
+                "decode_attention_noalloc: this shape needs %zu bytes of scratch, more than the "
+                "%d-byte built-in array; use qx_decode_attention with a workspace",
+                pl.total, QX_DECODE_ATTN_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  const int src = attn::noalloc_scratch(&scratch);
+  if (src != QX_OK) return src;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // the counters must start at zero; the array keeps whatever the last call left
+  QX_CUDA_TRY(cudaMemsetAsync(scratch, 0, size_t(batch) * kv_heads * sizeof(unsigned), st),
+              "decode_attention_noalloc: clear counters");
+  attn::Params prm{};
+  prm.q = static_cast<const __half*>(q);
+  prm.k = static_cast<const __half*>(k_cache);
+  prm.v = static_cast<const __half*>(v_cache);
+  prm.out = static_cast<__half*>(out);
+  prm.Hq = q_heads;
+  prm.Hkv = kv_heads;
+  prm.G = G;
+  prm.cap = cap;
+  prm.valid = valid;
+  prm.chunk = pl.chunk;
+  prm.nch = pl.nch;
+  const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf(float(head_dim));
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  unsigned char* ws = static_cast<unsigned char*>(scratch);
+  prm.counters = reinterpret_cast<unsigned*>(ws);
+  prm.part = reinterpret_cast<float*>(ws + pl.off_part);
+  QX_CUDA_TRY(cudaFuncSetAttribute(attn::decode_attn_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM),
+              "decode_attention_noalloc: set smem limit");
+  attn::decode_attn_kernel<<<dim3(pl.nch, batch * kv_heads), attn::THREADS, attn::SMEM, st>>>(prm);
+  return check_launch("decode_attention_noalloc");
 }
