@@ -37,6 +37,15 @@ typedef struct CUstream_st* qx_stream_t; /* == cudaStream_t */
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* qx_last_error(void);
+
+/* Device-side failures that a kernel cannot return as a status: a bounded
+ * wait inside a kernel that timed out sets a bit here instead of hanging the
+ * GPU (the kernel then finishes with undefined output).  New component: the
+ * reference has no device-side error reporting. */
+#define QX_DEVERR_MBAR_TIMEOUT 1u
+/* Reads (and with reset != 0 clears) the sticky error bits of the current
+ * device; synchronises with the device. */
+int qx_get_device_error(unsigned* code, int reset);
 /* Library version string. */
 const char* qx_version(void);
 
@@ -60,7 +69,8 @@ const char* qx_version(void);
  * lora_B (and fp16 zeros) 16-byte aligned.
  * Any M >= 1 (rows are processed 32 at a time).
  * No workspace: each group of CTAs that splits K forms a thread-block cluster
- * and reduces through distributed shared memory.
+ * and reduces through distributed shared memory (st.async into the CTA that
+ * owns the columns).
  * ---------------------------------------------------------------------- */
 int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const void* scales,
                        const void* zeros, int zeros_packed, int zero_offset,
@@ -68,11 +78,14 @@ int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const void* scales
                        int M, int K, int N, int rank, int group_size, float lora_scale,
                        qx_stream_t stream);
 
-/* Programmatic dependent launch for the GEMV (off by default).  When on, a
- * GEMV may start while the previous kernel in its stream is still running:
- * it streams its weights and stages scales / zeros / LoRA factors before
- * waiting for that kernel, so those operands must not be written by the
- * kernel immediately before it (true for model weights).  Returns 0. */
+/* Programmatic dependent launch for the GEMV (on by default; 0 turns it
+ * off).  When on, a GEMV launches as soon as every CTA of the GEMV before it
+ * in the stream is running: it streams its weights and stages scales /
+ * zeros / LoRA factors while that kernel finishes, and waits for it only
+ * before reading x (and so before writing y).  Kernels that do not trigger
+ * early (every kernel outside this library) still complete first.  The
+ * weight operands must therefore not be written by a GEMV issued just
+ * before on the same stream (true for model weights).  Returns 0. */
 int qx_set_pdl(int enable);
 
 /* ------------------------------------------------------------------------

@@ -27,6 +27,7 @@ SIGNATURES = {
                                    c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float,
                                    c_void_p]),
     "qx_set_pdl": (c_int, [c_int]),
+    "qx_get_device_error": (c_int, [c_void_p, c_int]),
     "qx_fused_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_void_p]),
     "qx_fused_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "qx_ring_append": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,

@@ -8,54 +8,65 @@
 //
 // Work decomposition
 //   tile    = 256 output columns (8 warps x 32 columns).
-//   cluster = the S CTAs that split one tile's K range (grid (tiles, S),
-//             cluster dims (1, S, 1), S in {1,2,4,8,16}); sized so the whole
-//             grid is resident in one wave.
-//   k-step  = 32 rows of K = 4 packed int32 rows.  Lane (g = lane/4,
-//             c = lane%4) loads one 128-bit word per k-step: packed row
-//             4*ks + c, columns 4g..4g+3 of its warp, so each warp load is
-//             4 rows x 128 contiguous bytes and every weight byte is loaded
-//             once.  A rolling window of U k-steps stays in flight per thread.
+//   cluster = the S CTAs that split one tile's K range into whole
+//             quantisation groups (grid (tiles, S), cluster dims (1, S, 1),
+//             S in {1,2,4,8,16}, chosen with the occupancy API so the grid
+//             runs in as few waves as possible).
+//   weights = streamed by the TMA engine: one 2-D tensor copy per
+//             quantisation group (KPG*4 packed rows x 1056 B, the qweight
+//             viewed as 64-bit elements so that the 1 KB tile row plus 32 B
+//             of the next tile land as one box row), every group of the CTA
+//             in flight at once when shared memory allows (else a ring with
+//             full/empty mbarriers refilled by thread 0).  The 1056 B row
+//             pitch lets lane (g = lane/4, c = lane%4) read packed row
+//             4*ks + c, columns 4g..4g+3 of its warp, with conflict-free
+//             128-bit loads.  One TMA instruction moves ~17 KB.
 //   dot     = one LOP3 per nibble pair builds exact fp16 operands with the
 //             magic-number trick (Kim et al., "Who Says Elephants Can't Run",
 //             2022): (v & 0x000F000F) | 0x64006400 is the half2 (1024 + q_i,
 //             1024 + q_{i+4}) and (v & 0x00F000F0) | 0x64006400 is
-//             (1024 + 16 q_{i+1}, ...).  These feed mma.sync m16n8k16 with
-//             fp32 accumulation as they are: the activations staged for the
-//             "x16" slots are pre-scaled by 1/16 (exact), so every product is
-//             (1024 + q) x or (64 + q) x, and the offsets are removed with the
-//             zero point once per group:
+//             (1024 + 16 q_{i+1}, ...).  They feed mma.sync m16n8k16 with
+//             fp32 accumulation as they are: activations staged for the "x16"
+//             slots are pre-scaled by 1/16 (exact), so every product is
+//             (1024 + q) x or (64 + q) x, and the offsets leave with the zero
+//             point once per group:
 //               sum (q - z) x = C - (1024 + z) Xa - (64 + z) Xb,
-//             Xa / Xb = sums of x over the two nibble classes.  MMA rows are
-//             output columns, MMA columns batch rows (8 per n-tile), the MMA
-//             k order a fixed permutation of a k-step that the staged
-//             activations follow.  5 integer ops per 8 weights.
+//             Xa / Xb = sums of x over the two nibble classes of the group.
+//   statics = scales, zero points, the CTA's slice of LoRA A and the tile's
+//             LoRA B arrive by TMA on one mbarrier, activations on another.
 //   LoRA    = h_s = x[:, Ks] A[Ks, :] on the tensor cores (ldmatrix.trans of
-//             the staged A slice), the LoRA product being linear in K.
-//   static operands (scales, zeros, A slice, B share) are staged into shared
-//             memory with cp.async right after the weight loads are issued;
-//             activations are staged after griddepcontrol.wait, so with
-//             programmatic dependent launch the weight stream overlaps the
-//             previous kernel's tail.
-//   reduce  = each CTA leaves its fp32 base partial and h_s in shared memory;
-//             after a cluster barrier CTA j sums columns [j*256/S, (j+1)*256/S)
-//             over the S CTAs through distributed shared memory in rank order
-//             (deterministic), adds lora_scale * h.B and rounds once.  No
-//             global scratch, no atomics.
-#include <cooperative_groups.h>
+//             the staged A slice); the LoRA product is linear in K, so each
+//             CTA adds (alpha/r) h_s B[:, tile] into its own partial sums
+//             before the weight loop and no h is exchanged.
+//   reduce  = each CTA sends its fp32 partial of the columns owned by CTA j
+//             (columns [j*256/S, (j+1)*256/S)) straight into CTA j's shared
+//             memory with st.async, which completes on CTA j's receive
+//             mbarrier; CTA j waits for its expected bytes, sums the S slices
+//             in rank order (deterministic) and rounds once.  No global
+//             scratch, no atomics, no cluster-wide barrier at the end.
+// Programmatic dependent launch (on by default, qx_set_pdl(0) turns it off):
+// the kernel lets the next kernel in the stream launch at once, and waits for
+// the previous one only before it reads the activations.  Weights, scales,
+// zero points and LoRA factors are therefore read before that wait: they must
+// not be written by the kernel issued just before on the same stream.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <atomic>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "qx_b200.h"
 #include "qx_common.cuh"
 
-namespace cg = cooperative_groups;
-
 namespace qx {
 
-std::atomic<int> g_pdl_enabled{0};
+std::atomic<int> g_pdl_enabled{1};
+
+// Sticky device-side error word (QX_DEVERR_* bits), read by qx_get_device_error.
+static __device__ unsigned g_device_error = 0;
 
 namespace gemv {
 
@@ -63,14 +74,19 @@ constexpr int WARPS = 8;
 constexpr int THREADS = WARPS * 32;
 constexpr int COLS = WARPS * 32;  // output columns per tile
 constexpr int KSTEP = 32;         // K rows per step (4 packed rows)
-constexpr int U = 8;              // k-steps of weights in flight per thread
+constexpr int ROWB = 1056;        // smem bytes per staged packed row (1 KB + 32 B: no bank conflicts)
+constexpr int MAX_NST = 4;        // weight stages (quantisation groups) resident per CTA
 constexpr int MROWS = 32;         // batch rows per launch (4 n-tiles of 8)
 constexpr int MAX_S = 16;         // largest cluster (non-portable size)
 constexpr size_t SMEM_LIMIT = 227 * 1024;
 
 __host__ __device__ constexpr int ctas_per_sm(int nt) { return nt == 1 ? 3 : 2; }
 
-struct Params {
+struct alignas(64) Params {
+  CUtensorMap tw;  // qweight as u64 [K/8][N/2], box {132, KPG*4}
+  CUtensorMap tb;  // LoRA B fp16 [r][N], box {256, r}
+  CUtensorMap ts;  // scales fp16 [K/g][N], box {256, gmax}
+  CUtensorMap tz;  // fp16 zeros [K/g][N], box {256, gmax} (packed qzeros use plain loads)
   const __half* x;
   const uint32_t* qw;
   const __half* scales;
@@ -80,12 +96,12 @@ struct Params {
   __half* y;
   int M, K, N, rank, group, zeros_packed, zero_offset;
   float lora_scale;
-  int T, S, Ts_max, ng_max;
+  int T, S, Ts_max, gmax, nst, pdl;
 };
 
 // Shared-memory carve-up (byte offsets), identical on host and device.
 struct Layout {
-  unsigned xraw, xs, xks, sc, zs, As, Bs, part, hs, red, hsum, total;
+  unsigned bars, ring, sz_s, sz_z, sf, xraw, xs, xks, ab, hs, red, recv, total;
 };
 
 __host__ __device__ inline unsigned take(unsigned& o, size_t bytes) {
@@ -94,67 +110,40 @@ __host__ __device__ inline unsigned take(unsigned& o, size_t bytes) {
   return r;
 }
 
-// row stride of the staged activations (halves): +8 keeps ldmatrix rows on
-// distinct banks
+// row stride of the staged activations (halves): +8 puts consecutive rows
+// 4 banks apart, so 8 rows x 4 words of an MMA fragment hit distinct banks
 __host__ __device__ inline int xstride(int Ts_max) { return Ts_max * KSTEP + 8; }
 
-__host__ __device__ inline Layout layout(int NT, int Ts_max, int ng_max, int rank, int S) {
+// M = batch rows of this launch (<= 32), NT = 8-row MMA tiles covering them.
+__host__ __device__ inline Layout layout(int M, int NT, int KPG, int Ts_max, int rank, int S,
+                                         int nst, int zeros_packed) {
+  const int gmax = Ts_max / KPG;
   Layout L;
   unsigned o = 0;
-  const size_t Ksmax = size_t(Ts_max) * KSTEP, Mp = size_t(NT) * 8;
-  L.xraw = take(o, Mp * xstride(Ts_max) * 2);       // activations [Mp][Ks(+8)] as loaded
-  L.xs = take(o, size_t(Ts_max) * NT * 32 * 16);    // activations in MMA-B order
-  L.xks = take(o, size_t(Ts_max) * NT * 8 * 2 * 4); // per k-step (Xa, Xb) per row
-  L.sc = take(o, size_t(ng_max) * COLS * 2);        // scales fp16 [ng][256]
-  L.zs = take(o, size_t(ng_max) * COLS * 2);        // zeros fp16 [ng][256] or packed [ng][32]
-  L.As = take(o, Ksmax * rank * 2);                 // LoRA A slice [Ks][r]
-  L.Bs = take(o, size_t(rank) * (COLS / S) * 2);    // LoRA B share [r][256/S]
-  L.part = take(o, Mp * COLS * 4);                  // base partial [Mp][256]
-  L.hs = take(o, Mp * rank * 4);                    // h_s [Mp][r]
-  L.red = take(o, size_t(WARPS) * 16 * 8 * 4);      // LoRA-down split-k partials
-  L.hsum = take(o, Mp * rank * 4);                  // h summed over the cluster
+  const size_t Mp = size_t(NT) * 8;
+  L.bars = take(o, size_t(4 + 2 * nst) * 8);          // statics, x, B, recv, full[nst], empty[nst]
+  L.ring = take(o, size_t(nst) * KPG * 4 * ROWB);     // weight stages
+  L.sz_s = take(o, size_t(gmax) * COLS * 2);          // scales [gmax][256]
+  L.sz_z = take(o, size_t(gmax) * (zeros_packed ? COLS / 2 : COLS * 2));  // [gmax][32] u32 or [gmax][256] fp16
+  L.sf = take(o, size_t(gmax) * COLS * 8);            // (s, s*z) as floats [gmax][256]
+  L.xraw = take(o, size_t(M) * xstride(Ts_max) * 2);  // activations [M][Ks(+8)] as loaded
+  L.xs = take(o, size_t(Ts_max) * M * 4 * 16);        // activations in MMA-B order [t][m][c]
+  L.xks = take(o, size_t(gmax) * Mp * 2 * 4);         // per group (Off, Sx) per row [g][Mp]
+  // LoRA A slice [Ks][r] for the down-projection, then the LoRA B tile [r][256]
+  const size_t a_bytes = size_t(Ts_max) * KSTEP * rank * 2, b_bytes = size_t(rank) * COLS * 2;
+  L.ab = take(o, a_bytes > b_bytes ? a_bytes : b_bytes);
+  L.hs = take(o, size_t(M) * rank * 4);               // h_s [M][r]
+  L.red = take(o, rank > 0 ? size_t(WARPS) * 16 * (M < 8 ? M : 8) * 4 : 0);  // split-k partials [w][16][min(M,8)]
+  L.recv = take(o, size_t(M) * COLS * 4);             // partials pushed by the cluster [S][M][256/S]
   L.total = o;
   return L;
 }
 
 struct Plan {
-  int tiles, S, T, Ts_max, ng_max, NT;
+  int tiles, S, T, Ts_max, NT, nst;
   size_t smem;
 };
 
-static Plan make_plan(int M, int K, int N, int rank, int group, int sms) {
-  Plan pl{};
-  pl.tiles = (N + COLS - 1) / COLS;
-  pl.T = K / KSTEP;
-  const int mc = std::min(M, MROWS);
-  pl.NT = mc <= 8 ? 1 : (mc <= 16 ? 2 : 4);
-  const int target = sms * ctas_per_sm(pl.NT);
-  const int kpg = group / KSTEP;
-  const int Gt = K / group;  // splits hold whole quantisation groups
-  int S = 1;
-  while (S * 2 <= MAX_S && pl.tiles * S * 2 <= target && S * 2 <= Gt) S *= 2;
-  for (;;) {
-    pl.S = S;
-    pl.ng_max = (Gt + S - 1) / S;
-    pl.Ts_max = pl.ng_max * kpg;
-    pl.smem = layout(pl.NT, pl.Ts_max, pl.ng_max, rank, S).total;
-    if (pl.smem <= SMEM_LIMIT || S * 2 > MAX_S || S * 2 > Gt) break;
-    S *= 2;
-  }
-  return pl;
-}
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
-  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(src_bytes));
-}
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src));
-}
-__device__ __forceinline__ void cp_async_commit_wait_all() {
-  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
-}
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
 __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
@@ -169,33 +158,112 @@ __device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void* p) {
                : "=r"(r[0]), "=r"(r[1])
                : "r"(a));
 }
-// Weights are read once per call: load them with an L2 evict-first policy so
-// the stream does not push activations, scales or code out of L2.
-__device__ __forceinline__ uint64_t evict_first_policy() {
-  uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-  return pol;
-}
-__device__ __forceinline__ uint4 ldg_weights(const void* ptr, uint64_t pol) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(ptr), "l"(pol));
-  return r;
-}
 __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("mul.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+// Weights are read once per call: an L2 evict-first policy keeps the stream
+// from pushing activations, scales or code out of L2.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+               "r"(bytes)
+               : "memory");
+}
+// try_wait suspends the thread (up to the hint, 1 ms) until the phase completes,
+// so waiting warps leave the issue slots to the computing ones.
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred P; mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 P, [%1], %2, %3; "
+      "selp.u32 %0, 1, 0, P; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(1000000u)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Waits at most ~200 ms for the phase; on timeout records QX_DEVERR_MBAR_TIMEOUT
+// in the device error word (read with qx_get_device_error) and returns false.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try(bar, parity)) {
+    if (global_ns() - t0 > 200000000ull) {
+      atomicOr(&g_device_error, QX_DEVERR_MBAR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+// 1-D bulk copies global -> shared (no multicast), completion counted on `bar`
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+// 2-D tensor copy global -> shared (no multicast); coordinates in elements,
+// x innermost (x * element size is a multiple of 16 B at every call site)
+__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                       uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_2d_hint(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+// st.async of two floats into a peer CTA's shared memory; completion counted
+// in bytes on the peer's mbarrier (both addresses already mapped with mapa)
+__device__ __forceinline__ void st_async_f2(uint32_t raddr, float a, float b, uint32_t rbar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+          raddr),
+      "f"(a), "f"(b), "r"(rbar)
+      : "memory");
+}
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
 
-// KPG = k-steps per quantisation group (group_size / 32): splits cover whole
-// groups, so the per-group correction sits at compile-time positions of the
-// unrolled main loop.
+// KPG = k-steps per quantisation group (group_size / 32).
 template <int NT, int KPG>
-__global__ void __launch_bounds__(THREADS, ctas_per_sm(NT)) w4a16_gemv_kernel(const Params p) {
+__global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
+    w4a16_gemv_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(128) unsigned char smem[];
-  cg::cluster_group cluster = cg::this_cluster();
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -203,245 +271,174 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT)) w4a16_gemv_kernel(co
   const int s = blockIdx.y;  // == rank in the (1, S, 1) cluster
   const int S = p.S;
   const int Gt = p.T / KPG;  // quantisation groups along K
-  const int ks0 = (s * Gt / S) * KPG;
-  const int ks1 = ((s + 1) * Gt / S) * KPG;
-  const int Ts = ks1 - ks0;
+  const int gr0 = s * Gt / S, gr1 = (s + 1) * Gt / S;
+  const int ngrp = gr1 - gr0;
+  const int ks0 = gr0 * KPG;
+  const int Ts = ngrp * KPG;
   const int Ks = Ts * KSTEP;
   const int XS = xstride(p.Ts_max);
   const int M = p.M, N = p.N, R = p.rank;
   constexpr int Mp = NT * 8;
+  constexpr int STAGE = KPG * 4 * ROWB;
+  constexpr uint32_t STAGE_TX = uint32_t(STAGE);  // full box, zero-filled past N
+  const int nst = p.nst;
   const int n_tile0 = tile * COLS;
   const int lcol = warp * 32 + 4 * g;  // first of this lane's 4 columns (tile-local)
-  const int ncol = n_tile0 + lcol;
-  const bool col_ok = ncol < N;        // N % 8 == 0: all 4 columns valid or none
+  const bool col_ok = n_tile0 + lcol < N;  // N % 8 == 0: all 4 columns valid or none
   const int k0 = ks0 * KSTEP;
-  const int g_first = ks0 / KPG;
-  const int ng = (ks1 - ks0) / KPG;
-  const int CPR = COLS / S;            // columns this CTA finalises
+  const int CPR = COLS / S;            // columns each CTA of the cluster finalises
+  const int cb = n_tile0 + s * CPR;    // first column this CTA finalises
+  const int own_cols = max(0, min(CPR, N - cb));
 
-  const Layout L = layout(NT, p.Ts_max, p.ng_max, R, S);
+  const Layout L = layout(M, NT, KPG, p.Ts_max, R, S, nst, p.zeros_packed);
+  unsigned char* ring = smem + L.ring;
+  const unsigned char* sz_s = smem + L.sz_s;
+  unsigned char* sz_z = smem + L.sz_z;
   __half* xraw = reinterpret_cast<__half*>(smem + L.xraw);
   uint4* xs = reinterpret_cast<uint4*>(smem + L.xs);
   float* xks = reinterpret_cast<float*>(smem + L.xks);
-  __half* sc = reinterpret_cast<__half*>(smem + L.sc);
-  unsigned char* zsb = smem + L.zs;
-  __half* As = reinterpret_cast<__half*>(smem + L.As);
-  __half* Bs = reinterpret_cast<__half*>(smem + L.Bs);
-  float* part = reinterpret_cast<float*>(smem + L.part);
+  float2* sf = reinterpret_cast<float2*>(smem + L.sf);
+  const __half* As = reinterpret_cast<const __half*>(smem + L.ab);
+  const __half* Bs = reinterpret_cast<const __half*>(smem + L.ab);  // after the LoRA-down
   float* hs = reinterpret_cast<float*>(smem + L.hs);
   float* red = reinterpret_cast<float*>(smem + L.red);
-  float* hsum = reinterpret_cast<float*>(smem + L.hsum);
+  const float* recv = reinterpret_cast<const float*>(smem + L.recv);
+  const uint32_t bar_st = smem_addr(smem + L.bars);  // scales, zeros, LoRA A
+  const uint32_t bar_x = bar_st + 8;                 // activations
+  const uint32_t bar_b = bar_st + 16;                // LoRA B
+  const uint32_t bar_rv = bar_st + 24;               // partials from the cluster
+  const uint32_t full0 = bar_st + 32;                // full[i]  = full0 + 8 i
+  const uint32_t empty0 = full0 + 8 * nst;           // empty[i] = empty0 + 8 i
+  const int wx = n_tile0 / 2;  // tile origin in 64-bit elements (x * 8 B = tile * 1 KB)
+  const uint32_t ring_s = smem_addr(ring);
 
-  // 1. first window of weight loads (weights are static: no dependency wait)
-  const size_t row_step = size_t(4) * N;  // one k-step down the packed rows
-  const uint32_t* ld_ptr = p.qw + size_t(ks0 * 4 + c) * N + ncol;
-  const uint64_t pol = evict_first_policy();
-  uint4 w[U];
-#pragma unroll
-  for (int u = 0; u < U; ++u) {
-    w[u] = (col_ok && ks0 + u < ks1) ? ldg_weights(ld_ptr, pol) : make_uint4(0u, 0u, 0u, 0u);
-    ld_ptr += row_step;
-  }
-
-  // 2. stage the static operands with cp.async
-  for (int it = tid; it < ng * (COLS / 8); it += THREADS) {  // scales: 16 B = 8 columns
-    const int gi = it / (COLS / 8), ch = it - gi * (COLS / 8), n = n_tile0 + ch * 8;
-    const bool ok = n < N;
-    cp_async16(sc + gi * COLS + ch * 8, ok ? p.scales + size_t(g_first + gi) * N + n : p.scales,
-               ok ? 16 : 0);
-  }
-  if (p.zeros_packed) {
-    const int words = N >> 3;
-    for (int it = tid; it < ng * (COLS / 8); it += THREADS) {  // 1 word = 8 columns
-      const int gi = it / (COLS / 8), wd = it - gi * (COLS / 8), wn = (n_tile0 >> 3) + wd;
-      uint32_t* dst = reinterpret_cast<uint32_t*>(zsb) + gi * (COLS / 8) + wd;
-      if (wn < words)
-        cp_async4(dst, reinterpret_cast<const uint32_t*>(p.zeros) + size_t(g_first + gi) * words + wn);
-      else
-        *dst = 0u;
-    }
-  } else {
-    const __half* zh = reinterpret_cast<const __half*>(p.zeros);
-    for (int it = tid; it < ng * (COLS / 8); it += THREADS) {
-      const int gi = it / (COLS / 8), ch = it - gi * (COLS / 8), n = n_tile0 + ch * 8;
-      const bool ok = n < N;
-      cp_async16(reinterpret_cast<__half*>(zsb) + gi * COLS + ch * 8,
-                 ok ? zh + size_t(g_first + gi) * N + n : zh, ok ? 16 : 0);
-    }
-  }
-  if (R > 0) {
-    const int a_chunks = (Ks * R) >> 3;  // contiguous slice A[k0 : k0 + Ks, :]
-    const __half* Ab = p.A + size_t(k0) * R;
-    for (int it = tid; it < a_chunks; it += THREADS) cp_async16(As + it * 8, Ab + it * 8, 16);
-    const int bcpr = CPR >> 3;  // 16-byte chunks per B row share
-    const int cbase = n_tile0 + s * CPR;
-    for (int it = tid; it < R * bcpr; it += THREADS) {
-      const int rr = it / bcpr, ch = it - rr * bcpr, n = cbase + ch * 8;
-      const bool ok = n < N;
-      cp_async16(Bs + rr * CPR + ch * 8, ok ? p.B + size_t(rr) * N + n : p.B, ok ? 16 : 0);
-    }
-  }
-
-  // 3. activations may be produced by the previous kernel in the stream;
-  //    rows >= M are zero-filled
-  grid_dep_wait();
-  {
-    const int xchunks = Ks >> 3;
-    for (int it = tid; it < Mp * xchunks; it += THREADS) {
-      const int m = it / xchunks, ch = it - m * xchunks;
-      const bool ok = m < M;
-      cp_async16(xraw + m * XS + ch * 8, ok ? p.x + size_t(m) * p.K + k0 + ch * 8 : p.x,
-                 ok ? 16 : 0);
-    }
-  }
-  cp_async_commit_wait_all();
-  __syncthreads();
+  // The next kernel in the stream may launch as soon as every CTA of this one
+  // is resident: it only streams its own weights until it waits for us.
   grid_dep_launch();
 
-  // 4. activations in MMA-B order: (x0, x4, x1/16, x5/16, x2, x6, x3/16, x7/16)
-  //    per packed row, plus per-k-step sums over the two nibble classes
-  for (int it = tid; it < Ts * NT * 32; it += THREADS) {
-    const int t = it / (NT * 32);
-    const int rem = it - t * (NT * 32);
-    const int nt = rem >> 5, l = rem & 31, gg = l >> 2, cc = l & 3;
-    const int m = nt * 8 + gg;
-    const uint4 v = *reinterpret_cast<const uint4*>(xraw + m * XS + t * KSTEP + cc * 8);
-    uint4 o;
-    o.x = prmt(v.x, v.z, 0x5410u);                         // (x0, x4)
-    o.y = hmul2_u32(prmt(v.x, v.z, 0x7632u), 0x2C002C00u);  // (x1, x5) / 16
-    o.z = prmt(v.y, v.w, 0x5410u);                         // (x2, x6)
-    o.w = hmul2_u32(prmt(v.y, v.w, 0x7632u), 0x2C002C00u);  // (x3, x7) / 16
-    xs[it] = o;
-    const float2 a0 = h2_to_f2(v.x), a1 = h2_to_f2(v.y), a2 = h2_to_f2(v.z), a3 = h2_to_f2(v.w);
-    float xa = (a0.x + a1.x) + (a2.x + a3.x);  // x0 + x2 + x4 + x6
-    float xb = (a0.y + a1.y) + (a2.y + a3.y);  // x1 + x3 + x5 + x7
-    xa += __shfl_xor_sync(0xffffffffu, xa, 1);
-    xa += __shfl_xor_sync(0xffffffffu, xa, 2);
-    xb += __shfl_xor_sync(0xffffffffu, xb, 1);
-    xb += __shfl_xor_sync(0xffffffffu, xb, 2);
-    if (cc == 0)
-      *reinterpret_cast<float2*>(xks + ((t * NT + nt) * 8 + gg) * 2) = make_float2(xa, xb);
+  // 1. warp 0 starts every copy; only the activations wait for the previous
+  //    kernel in the stream.
+  if (warp == 0) {
+    const uint32_t xrow_bytes = uint32_t(Ks) * 2;
+    if (lane == 0) {
+      prefetch_tmap(&p.tw);
+      mbar_init(bar_st, 1);
+      mbar_init(bar_x, 1);
+      mbar_init(bar_b, 1);
+      mbar_init(bar_rv, 1);
+      for (int i = 0; i < nst; ++i) {
+        mbar_init(full0 + 8 * i, 1);
+        mbar_init(empty0 + 8 * i, WARPS);
+      }
+      asm volatile("fence.mbarrier_init.release.cluster;\nfence.proxy.async.shared::cta;" :::
+                       "memory");
+      // bytes the S CTAs of the cluster will send for this CTA's columns
+      mbar_expect_tx(bar_rv, uint32_t(S * M * own_cols) * 4u);
+      const uint32_t sz_bytes = uint32_t(p.gmax) * COLS * 2 * (p.zeros_packed ? 1 : 2);
+      mbar_expect_tx(bar_st, sz_bytes + uint32_t(Ks * R) * 2);
+      // scales / zero points of this CTA's groups (gmax rows; rows past the
+      // CTA's range are read but unused)
+      tma_2d(smem_addr(sz_s), &p.ts, n_tile0, gr0, bar_st);
+      if (!p.zeros_packed) tma_2d(smem_addr(sz_z), &p.tz, n_tile0, gr0, bar_st);
+      if (R > 0)  // LoRA: this CTA's rows of A (B follows once A is consumed)
+        bulk_g2s(smem_addr(As), p.A + size_t(k0) * R, uint32_t(Ks * R) * 2, bar_st);
+      const uint64_t pol = evict_first_policy();
+      for (int i = 0; i < min(ngrp, nst); ++i) {
+        mbar_expect_tx(full0 + 8 * i, STAGE_TX);
+        tma_2d_hint(ring_s + i * STAGE, &p.tw, wx, (ks0 + i * KPG) * 4, full0 + 8 * i, pol);
+      }
+      mbar_expect_tx(bar_x, uint32_t(M) * xrow_bytes);
+    }
+    __syncwarp();
+    if (p.pdl) {  // activations may come from the previous kernel in the stream
+      if (lane == 0) grid_dep_wait();
+      __syncwarp();
+    }
+    for (int m = lane; m < M; m += 32)
+      bulk_g2s(smem_addr(xraw + m * XS), p.x + size_t(m) * p.K + k0, xrow_bytes, bar_x);
   }
-  __syncthreads();
+  // Peers send partial sums only after every CTA of the cluster has
+  // initialised its receive barrier (arrive now, wait before sending).
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
-  // 5. main loop: tensor-core dot products on raw magic-number operands
-  float acc[2][NT][4], cgr[2][NT][4], xsa[NT][4];  // xsa: (Xa, Xb) for rows 2c, 2c+1
-#pragma unroll
-  for (int pp = 0; pp < 2; ++pp)
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[pp][nt][i] = cgr[pp][nt][i] = 0.f;
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) xsa[nt][0] = xsa[nt][1] = xsa[nt][2] = xsa[nt][3] = 0.f;
-
-  auto flush = [&](int gi) {
-    const uint2 sv2 = *reinterpret_cast<const uint2*>(sc + gi * COLS + lcol);
-    const float2 s01 = h2_to_f2(sv2.x), s23 = h2_to_f2(sv2.y);
-    const float sv[4] = {s01.x, s01.y, s23.x, s23.y};
-    float zv[4];
-    if (p.zeros_packed) {
-      const uint32_t wz = reinterpret_cast<const uint32_t*>(zsb)[gi * (COLS / 8) + (lcol >> 3)];
-      const int sh = (lcol & 7) * 4;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) zv[j] = float(((wz >> (sh + 4 * j)) & 0xFu) + unsigned(p.zero_offset));
-    } else {
-      const uint2 zv2 =
-          *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(zsb) + gi * COLS + lcol);
-      const float2 z01 = h2_to_f2(zv2.x), z23 = h2_to_f2(zv2.y);
-      zv[0] = z01.x;
-      zv[1] = z01.y;
-      zv[2] = z23.x;
-      zv[3] = z23.y;
+  // GPTQ qzeros rows are N/2 bytes (not always a 16 B multiple): plain loads
+  if (p.zeros_packed) {
+    const int zwords = N >> 3;
+    const uint32_t* zsrc = static_cast<const uint32_t*>(p.zeros);
+    for (int it = tid; it < p.gmax * (COLS / 8); it += THREADS) {
+      const int row = gr0 + (it >> 5), col = (n_tile0 >> 3) + (it & 31);
+      reinterpret_cast<uint32_t*>(sz_z)[it] =
+          (row < Gt && col < zwords) ? __ldg(zsrc + size_t(row) * zwords + col) : 0u;
     }
-#pragma unroll
-    for (int pp = 0; pp < 2; ++pp) {
-      const float za0 = 1024.f + zv[2 * pp], zb0 = 64.f + zv[2 * pp];
-      const float za1 = 1024.f + zv[2 * pp + 1], zb1 = 64.f + zv[2 * pp + 1];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const float* xv = xsa[nt];
-        acc[pp][nt][0] = fmaf(sv[2 * pp], cgr[pp][nt][0] - za0 * xv[0] - zb0 * xv[1], acc[pp][nt][0]);
-        acc[pp][nt][1] = fmaf(sv[2 * pp], cgr[pp][nt][1] - za0 * xv[2] - zb0 * xv[3], acc[pp][nt][1]);
-        acc[pp][nt][2] =
-            fmaf(sv[2 * pp + 1], cgr[pp][nt][2] - za1 * xv[0] - zb1 * xv[1], acc[pp][nt][2]);
-        acc[pp][nt][3] =
-            fmaf(sv[2 * pp + 1], cgr[pp][nt][3] - za1 * xv[2] - zb1 * xv[3], acc[pp][nt][3]);
-        cgr[pp][nt][0] = cgr[pp][nt][1] = cgr[pp][nt][2] = cgr[pp][nt][3] = 0.f;
-      }
-    }
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) xsa[nt][0] = xsa[nt][1] = xsa[nt][2] = xsa[nt][3] = 0.f;
-  };
+  }
+  __syncthreads();  // barriers initialised, zero points staged
+  mbar_wait(bar_st, 0);
+  mbar_wait(bar_x, 0);
 
-  static_assert(U % KPG == 0, "a register window holds whole groups");
-  int gi_cur = 0;  // group index relative to g_first
-  for (int base = ks0; base < ks1; base += U) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int ks = base + u;
-      if (ks < ks1) {
-        const uint32_t wv[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
-        w[u] = (col_ok && ks + U < ks1) ? ldg_weights(ld_ptr, pol) : make_uint4(0u, 0u, 0u, 0u);
-        ld_ptr += row_step;
-        uint32_t q[4][4];
-#pragma unroll
-        for (int jw = 0; jw < 4; ++jw) {
-          const uint32_t hi = wv[jw] >> 8;
-          q[jw][0] = lop3_and_or(wv[jw], 0x000F000Fu, 0x64006400u);  // (1024+q0, 1024+q4)
-          q[jw][1] = lop3_and_or(wv[jw], 0x00F000F0u, 0x64006400u);  // (1024+16q1, 1024+16q5)
-          q[jw][2] = lop3_and_or(hi, 0x000F000Fu, 0x64006400u);      // (1024+q2, 1024+q6)
-          q[jw][3] = lop3_and_or(hi, 0x00F000F0u, 0x64006400u);      // (1024+16q3, 1024+16q7)
-        }
-        const int t = ks - ks0;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const uint4 bx = xs[(t * NT + nt) * 32 + lane];
-          const float4 xk = *reinterpret_cast<const float4*>(xks + ((t * NT + nt) * 8 + 2 * c) * 2);
-          xsa[nt][0] += xk.x;
-          xsa[nt][1] += xk.y;
-          xsa[nt][2] += xk.z;
-          xsa[nt][3] += xk.w;
-#pragma unroll
-          for (int pp = 0; pp < 2; ++pp) {
-            mma_16816(cgr[pp][nt], q[2 * pp][0], q[2 * pp + 1][0], q[2 * pp][1], q[2 * pp + 1][1],
-                      bx.x, bx.y);
-            mma_16816(cgr[pp][nt], q[2 * pp][2], q[2 * pp + 1][2], q[2 * pp][3], q[2 * pp + 1][3],
-                      bx.z, bx.w);
-          }
-        }
-        if ((u + 1) % KPG == 0) {  // last k-step of a group (splits hold whole groups)
-          flush(gi_cur);
-          ++gi_cur;
-        }
+  // 2. activations in MMA-B order (x0, x4, x1/16, x5/16, x2, x6, x3/16, x7/16)
+  //    per packed row, and per group the sums over the two nibble classes.
+  //    Items (m, t, c) with c fastest: a group of row m is an aligned block
+  //    of 4*KPG lanes; the item count is padded to whole warps for the
+  //    shuffles.
+  {
+    const int tot = M * Ts * 4, totp = (tot + 31) & ~31;
+    for (int it = tid; it < totp; it += THREADS) {
+      const bool ok = it < tot;
+      const int mt = it >> 2, cc = it & 3;
+      const int m = ok ? mt / Ts : 0, t = ok ? mt - m * Ts : 0;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (ok) {
+        v = *reinterpret_cast<const uint4*>(xraw + m * XS + t * KSTEP + cc * 8);
+        uint4 o;
+        o.x = prmt(v.x, v.z, 0x5410u);                         // (x0, x4)
+        o.y = hmul2_u32(prmt(v.x, v.z, 0x7632u), 0x2C002C00u);  // (x1, x5) / 16
+        o.z = prmt(v.y, v.w, 0x5410u);                         // (x2, x6)
+        o.w = hmul2_u32(prmt(v.y, v.w, 0x7632u), 0x2C002C00u);  // (x3, x7) / 16
+        xs[(t * M + m) * 4 + cc] = o;
       }
+      const float2 a0 = h2_to_f2(v.x), a1 = h2_to_f2(v.y), a2 = h2_to_f2(v.z), a3 = h2_to_f2(v.w);
+      float xa = (a0.x + a1.x) + (a2.x + a3.x);  // x0 + x2 + x4 + x6
+      float xb = (a0.y + a1.y) + (a2.y + a3.y);  // x1 + x3 + x5 + x7
+#pragma unroll
+      for (int w = 1; w < 4 * KPG; w <<= 1) {
+        xa += __shfl_xor_sync(0xffffffffu, xa, w);
+        xb += __shfl_xor_sync(0xffffffffu, xb, w);
+      }
+      if (ok && cc == 0 && t % KPG == 0)  // (Off, Sx) = (1024 Xa + 64 Xb, Xa + Xb)
+        *reinterpret_cast<float2*>(xks + ((t / KPG) * Mp + m) * 2) =
+            make_float2(fmaf(1024.f, xa, 64.f * xb), xa + xb);
+    }
+    // scales and zero points of the CTA's groups as floats (s, s * z)
+    for (int it = tid; it < ngrp * COLS; it += THREADS) {
+      const int gi = it >> 8, col = it & (COLS - 1);
+      const float sc = __half2float(reinterpret_cast<const __half*>(sz_s)[it]);
+      float z;
+      if (p.zeros_packed)
+        z = float(((reinterpret_cast<const uint32_t*>(sz_z)[gi * (COLS / 8) + (col >> 3)] >>
+                    (4 * (col & 7))) & 0xFu) + unsigned(p.zero_offset));
+      else
+        z = __half2float(reinterpret_cast<const __half*>(sz_z)[it]);
+      sf[it] = make_float2(sc, sc * z);
     }
   }
 
-  // 6. base partial into shared memory: rows nt*8 + 2c (+1), columns lcol + 2pp (+1)
-#pragma unroll
-  for (int pp = 0; pp < 2; ++pp)
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int m0 = nt * 8 + 2 * c, cl = lcol + 2 * pp;
-      *reinterpret_cast<float2*>(part + m0 * COLS + cl) = make_float2(acc[pp][nt][0], acc[pp][nt][2]);
-      *reinterpret_cast<float2*>(part + (m0 + 1) * COLS + cl) =
-          make_float2(acc[pp][nt][1], acc[pp][nt][3]);
-    }
-
-  // 7. LoRA down-projection on the tensor cores: h_s^T[r][m] = A^T[r][Ks] . x^T[Ks][m]
-  //    16 x 8 output tiles (rank rows x batch rows); tiles over warps, and
-  //    when there are fewer tiles than warps the K range is split as well.
+  // 3. LoRA down-projection h_s^T[r][m] = A^T[r][Ks] . x^T[Ks][m] on the
+  //    tensor cores, 16 x 8 tiles (rank rows x batch rows) over warps, the K
+  //    range split too when there are fewer tiles than warps.
+  int nsplit = 1;
+  const int MR = M < 8 ? M : 8;  // rows kept in the split-k partials
   if (R > 0) {
     const int RT = R >= 16 ? R / 16 : 1;
     const int ntiles = RT * NT;
-    const int nsplit = ntiles >= WARPS ? 1 : WARPS / ntiles;
+    nsplit = ntiles >= WARPS ? 1 : WARPS / ntiles;
     const int KB = Ks / 16;
     for (int tl = warp % ntiles; tl < ntiles; tl += (ntiles >= WARPS ? WARPS : ntiles)) {
       const int rt = tl / NT, nt = tl - rt * NT;
       const int part_k = ntiles >= WARPS ? 0 : warp / ntiles;
       float h4[4] = {0.f, 0.f, 0.f, 0.f};
       const int mi = lane >> 3, ri = lane & 7;
+      const int mb = nt * 8 + g;  // batch row of this lane's B fragment
+      const __half* xrow = xraw + mb * XS + 2 * c;
       for (int kb = part_k; kb < KB; kb += nsplit) {
         uint32_t a[4];
         {
@@ -455,90 +452,349 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT)) w4a16_gemv_kernel(co
             a[3] = 0u;
           }
         }
-        uint32_t b[2];
-        {
-          const int l16 = lane & 15;
-          ldsm_x2(b, xraw + (nt * 8 + (l16 & 7)) * XS + kb * 16 + 8 * (l16 >> 3));
+        uint32_t b0 = 0u, b1 = 0u;
+        if (mb < M) {
+          b0 = *reinterpret_cast<const uint32_t*>(xrow + kb * 16);
+          b1 = *reinterpret_cast<const uint32_t*>(xrow + kb * 16 + 8);
         }
-        mma_16816(h4, a[0], a[1], a[2], a[3], b[0], b[1]);
+        mma_16816(h4, a[0], a[1], a[2], a[3], b0, b1);
       }
-      // h4: (rank row g, batch 2c/2c+1) and (rank row g+8, ...)
       if (nsplit == 1) {
         const int j0 = rt * 16 + g, m0 = nt * 8 + 2 * c;
-        hs[m0 * R + j0] = h4[0];
-        hs[(m0 + 1) * R + j0] = h4[1];
+        if (m0 < M) hs[m0 * R + j0] = h4[0];
+        if (m0 + 1 < M) hs[(m0 + 1) * R + j0] = h4[1];
         if (j0 + 8 < R) {
-          hs[m0 * R + j0 + 8] = h4[2];
-          hs[(m0 + 1) * R + j0 + 8] = h4[3];
+          if (m0 < M) hs[m0 * R + j0 + 8] = h4[2];
+          if (m0 + 1 < M) hs[(m0 + 1) * R + j0 + 8] = h4[3];
         }
-      } else {
-        float* rw = red + warp * 128;  // [16][8]
-        rw[g * 8 + 2 * c] = h4[0];
-        rw[g * 8 + 2 * c + 1] = h4[1];
-        rw[(g + 8) * 8 + 2 * c] = h4[2];
-        rw[(g + 8) * 8 + 2 * c + 1] = h4[3];
+      } else {  // tile-local rows 2c, 2c+1 (< MR = min(M, 8))
+        float* rw = red + warp * 16 * MR;  // [16][MR]
+        const int ml = 2 * c;
+        if (nt * 8 + ml < M) {
+          rw[g * MR + ml] = h4[0];
+          rw[(g + 8) * MR + ml] = h4[2];
+        }
+        if (nt * 8 + ml + 1 < M) {
+          rw[g * MR + ml + 1] = h4[1];
+          rw[(g + 8) * MR + ml + 1] = h4[3];
+        }
       }
     }
-    if (nsplit > 1) {
-      __syncthreads();
-      for (int it = tid; it < ntiles * 128; it += THREADS) {
-        const int tl = it >> 7, e = it & 127, jr = e >> 3, mc = e & 7;
+  }
+  __syncthreads();  // xs, xks, hs or the split-k partials ready; A consumed
+  if (R > 0) {
+    if (tid == 0) {  // LoRA B tile into the A slice's space, lands during the weight loop
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_expect_tx(bar_b, uint32_t(R * COLS) * 2);
+      tma_2d(smem_addr(Bs), &p.tb, n_tile0, 0, bar_b);
+    }
+    if (nsplit > 1) {  // warp q2 * ntiles + tl holds split q2 of tile tl
+      const int ntiles = (R >= 16 ? R / 16 : 1) * NT;
+      for (int it = tid; it < ntiles * 16 * MR; it += THREADS) {
+        const int tl = it / (16 * MR), e = it - tl * (16 * MR), jr = e / MR, ml = e - jr * MR;
         const int rt = tl / NT, nt = tl - rt * NT;
-        float v = 0.f;
-        for (int q2 = 0; q2 < nsplit; ++q2) v += red[(q2 * ntiles + tl) * 128 + e];
-        const int j = rt * 16 + jr;
-        if (j < R) hs[(nt * 8 + mc) * R + j] = v;
+        const int j = rt * 16 + jr, m = nt * 8 + ml;
+        if (j < R && m < M) {
+          float v = 0.f;
+          for (int q2 = 0; q2 < nsplit; ++q2) v += red[(q2 * ntiles + tl) * 16 * MR + e];
+          hs[m * R + j] = v;
+        }
+      }
+      __syncthreads();
+    }
+  }
+
+  // 4. main loop over this CTA's quantisation groups (pipeline stages);
+  //    acc[pp][nt][i] holds column lcol + 2 pp + (i >> 1), row nt*8 + 2c + (i & 1)
+  float acc[2][NT][4], cgr[2][NT][4];
+#pragma unroll
+  for (int pp = 0; pp < 2; ++pp)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[pp][nt][i] = 0.f;
+
+  int st = 0, use = 0;  // ring stage and wrap count
+  const unsigned char* wlane = ring + c * ROWB + lcol * 4;
+  for (int gi = 0; gi < ngrp; ++gi) {
+    mbar_wait(full0 + 8 * st, use & 1);
+    uint4 wq[KPG];
+#pragma unroll
+    for (int j = 0; j < KPG; ++j)
+      wq[j] = col_ok ? *reinterpret_cast<const uint4*>(wlane + st * STAGE + j * 4 * ROWB)
+                     : make_uint4(0u, 0u, 0u, 0u);
+    if (gi + nst < ngrp) {  // refill this stage with group gi + nst
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty0 + 8 * st);
+      if (tid == 0) {
+        mbar_wait(empty0 + 8 * st, use & 1);
+        mbar_expect_tx(full0 + 8 * st, STAGE_TX);
+        tma_2d_hint(ring_s + st * STAGE, &p.tw, wx, (ks0 + (gi + nst) * KPG) * 4, full0 + 8 * st,
+                    evict_first_policy());
+      }
+      __syncwarp();
+    }
+    const uint4* xg = xs + size_t(gi) * KPG * M * 4;
+#pragma unroll
+    for (int j = 0; j < KPG; ++j) {
+      const uint32_t wv[4] = {wq[j].x, wq[j].y, wq[j].z, wq[j].w};
+      uint32_t q[4][4];
+#pragma unroll
+      for (int jw = 0; jw < 4; ++jw) {
+        const uint32_t hi = wv[jw] >> 8;
+        q[jw][0] = lop3_and_or(wv[jw], 0x000F000Fu, 0x64006400u);  // (1024+q0, 1024+q4)
+        q[jw][1] = lop3_and_or(wv[jw], 0x00F000F0u, 0x64006400u);  // (1024+16q1, 1024+16q5)
+        q[jw][2] = lop3_and_or(hi, 0x000F000Fu, 0x64006400u);      // (1024+q2, 1024+q6)
+        q[jw][3] = lop3_and_or(hi, 0x00F000F0u, 0x64006400u);      // (1024+16q3, 1024+16q7)
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int mrow = nt * 8 + g;
+        const uint4 bx = mrow < M ? xg[(j * M + mrow) * 4 + c] : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int pp = 0; pp < 2; ++pp) {
+          if (j == 0)  // the group's first product starts from zero
+            mma_16816_zc(cgr[pp][nt], q[2 * pp][0], q[2 * pp + 1][0], q[2 * pp][1],
+                         q[2 * pp + 1][1], bx.x, bx.y);
+          else
+            mma_16816(cgr[pp][nt], q[2 * pp][0], q[2 * pp + 1][0], q[2 * pp][1], q[2 * pp + 1][1],
+                      bx.x, bx.y);
+          mma_16816(cgr[pp][nt], q[2 * pp][2], q[2 * pp + 1][2], q[2 * pp][3], q[2 * pp + 1][3],
+                    bx.z, bx.w);
+        }
+      }
+    }
+    {  // group correction: acc += s (C - Off) - (s z) Sx
+      const float4 c01 = *reinterpret_cast<const float4*>(sf + gi * COLS + lcol);      // s, sz of cols 0, 1
+      const float4 c23 = *reinterpret_cast<const float4*>(sf + gi * COLS + lcol + 2);  // cols 2, 3
+      const float sv[4] = {c01.x, c01.z, c23.x, c23.z}, zv[4] = {c01.y, c01.w, c23.y, c23.w};
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        // (Off, Sx) of rows nt*8 + 2c and + 1 (rows >= M hold garbage that
+        // only reaches discarded accumulators)
+        const float4 xv = *reinterpret_cast<const float4*>(xks + (gi * Mp + nt * 8 + 2 * c) * 2);
+#pragma unroll
+        for (int pp = 0; pp < 2; ++pp) {
+          const float s0 = sv[2 * pp], z0 = zv[2 * pp], s1 = sv[2 * pp + 1], z1 = zv[2 * pp + 1];
+          acc[pp][nt][0] = fmaf(-z0, xv.y, fmaf(s0, cgr[pp][nt][0] - xv.x, acc[pp][nt][0]));
+          acc[pp][nt][1] = fmaf(-z0, xv.w, fmaf(s0, cgr[pp][nt][1] - xv.z, acc[pp][nt][1]));
+          acc[pp][nt][2] = fmaf(-z1, xv.y, fmaf(s1, cgr[pp][nt][2] - xv.x, acc[pp][nt][2]));
+          acc[pp][nt][3] = fmaf(-z1, xv.w, fmaf(s1, cgr[pp][nt][3] - xv.z, acc[pp][nt][3]));
+        }
+      }
+    }
+    if (++st == nst) {
+      st = 0;
+      ++use;
+    }
+  }
+
+  // 5. this CTA's LoRA term (alpha/r) h_s B[:, cols] joins its partial sums
+  if (R > 0) {
+    mbar_wait(bar_b, 0);
+    if (col_ok) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const int m = nt * 8 + 2 * c + rr;
+          if (m < M) {
+            float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+            for (int j0 = 0; j0 < R; j0 += 8) {  // rank is a multiple of 8
+#pragma unroll
+              for (int j = j0; j < j0 + 8; ++j) {
+                const float h = hs[m * R + j];
+                const uint2 b = *reinterpret_cast<const uint2*>(Bs + j * COLS + lcol);
+                const float2 b01 = h2_to_f2(b.x), b23 = h2_to_f2(b.y);
+                l0 = fmaf(h, b01.x, l0);
+                l1 = fmaf(h, b01.y, l1);
+                l2 = fmaf(h, b23.x, l2);
+                l3 = fmaf(h, b23.y, l3);
+              }
+            }
+            acc[0][nt][rr] = fmaf(p.lora_scale, l0, acc[0][nt][rr]);
+            acc[0][nt][2 + rr] = fmaf(p.lora_scale, l1, acc[0][nt][2 + rr]);
+            acc[1][nt][rr] = fmaf(p.lora_scale, l2, acc[1][nt][rr]);
+            acc[1][nt][2 + rr] = fmaf(p.lora_scale, l3, acc[1][nt][2 + rr]);
+          }
+        }
       }
     }
   }
 
-  // 8. cluster reduction through distributed shared memory
-  cluster.sync();
-  if (R > 0) {
-    for (int it = tid; it < M * R; it += THREADS) {
+  // 6. send the partial of the columns owned by CTA j into j's receive area
+  //    [S][M][CPR] (rows nt*8 + 2c (+1), columns lcol + 2pp (+1)).
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  if (col_ok) {
+#pragma unroll
+    for (int pp = 0; pp < 2; ++pp) {
+      const int cl = lcol + 2 * pp;
+      const int owner = cl / CPR, cc = cl - owner * CPR;
+      const uint32_t rbase = map_rank(smem_addr(recv + size_t(s) * M * CPR + cc), owner);
+      const uint32_t rbar = map_rank(bar_rv, owner);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int m0 = nt * 8 + 2 * c;
+        if (m0 < M) st_async_f2(rbase + m0 * CPR * 4, acc[pp][nt][0], acc[pp][nt][2], rbar);
+        if (m0 + 1 < M)
+          st_async_f2(rbase + (m0 + 1) * CPR * 4, acc[pp][nt][1], acc[pp][nt][3], rbar);
+      }
+    }
+  }
+
+  // 7. this CTA's columns: wait for the S partials, sum in rank order, round
+  if (own_cols > 0) {
+    mbar_wait(bar_rv, 0);
+    for (int it = tid; it < M * own_cols; it += THREADS) {
+      const int m = it / own_cols, cc = it - m * own_cols;
       float v = 0.f;
-      for (int r2 = 0; r2 < S; ++r2) v += cluster.map_shared_rank(hs, r2)[it];
-      hsum[it] = v;
-    }
-    __syncthreads();
-  }
-  for (int it = tid; it < M * CPR; it += THREADS) {
-    const int m = it / CPR, cc = it - m * CPR;
-    const int cl = s * CPR + cc, n = n_tile0 + cl;
-    if (n < N) {
-      float vals[MAX_S];
-#pragma unroll
-      for (int r2 = 0; r2 < MAX_S; ++r2)
-        vals[r2] = r2 < S ? cluster.map_shared_rank(part, r2)[m * COLS + cl] : 0.f;
-      float base = 0.f;
-#pragma unroll
-      for (int r2 = 0; r2 < MAX_S; ++r2) base += vals[r2];
-      float lora = 0.f;
-      for (int jj = 0; jj < R; ++jj) lora = fmaf(hsum[m * R + jj], __half2float(Bs[jj * CPR + cc]), lora);
-      p.y[size_t(m) * N + n] = __float2half_rn(fmaf(p.lora_scale, lora, base));
+      for (int r2 = 0; r2 < S; ++r2) v += recv[(size_t(r2) * M + m) * CPR + cc];
+      p.y[size_t(m) * N + cb + cc] = __float2half_rn(v);
     }
   }
-  cluster.sync();  // peers may still be reading this CTA's shared memory
 }
 
 template <int NT, int KPG>
-static int launch(const Params& prm, const Plan& pl, cudaStream_t st) {
-  auto kern = w4a16_gemv_kernel<NT, KPG>;
+static int prepare(int dev) {
   static std::mutex mu;
-  static bool attr_done[64] = {};
+  static bool done[64] = {};
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev >= 0 && dev < 64 && done[dev]) return QX_OK;
+  auto kern = w4a16_gemv_kernel<NT, KPG>;
+  QX_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_LIMIT)),
+              "w4a16_gemv: set smem limit");
+  QX_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+              "w4a16_gemv: allow 16-CTA clusters");
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return QX_OK;
+}
+
+// Among the cluster sizes whose shared memory fits, pick the one that needs
+// the fewest waves of co-resident clusters (occupancy API), larger S on ties.
+template <int NT, int KPG>
+static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed, Plan* out) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, int, int, int>, Plan> cache;
   int dev = 0;
-  cudaGetDevice(&dev);
+  QX_CUDA_TRY(cudaGetDevice(&dev), "w4a16_gemv: cudaGetDevice");
+  const auto key = std::make_tuple(dev, M, K, N, rank, group, zeros_packed);
   {
     std::lock_guard<std::mutex> lk(mu);
-    const int ti = 0;
-    if (dev < 0 || dev >= 64 || !attr_done[dev + ti]) {
-      QX_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(SMEM_LIMIT)),
-                  "w4a16_gemv: set smem limit");
-      QX_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
-                  "w4a16_gemv: allow 16-CTA clusters");
-      if (dev >= 0 && dev < 64) attr_done[dev + ti] = true;
+    auto itc = cache.find(key);
+    if (itc != cache.end()) {
+      *out = itc->second;
+      return QX_OK;
     }
+  }
+  const int rc = prepare<NT, KPG>(dev);
+  if (rc != QX_OK) return rc;
+  const int tiles = (N + COLS - 1) / COLS, T = K / KSTEP, Gt = K / group;
+  Plan best{};
+  long best_waves = -1;
+  for (int S = 1; S <= MAX_S && S <= Gt; S *= 2) {
+    Plan pl{};
+    pl.NT = NT;
+    pl.tiles = tiles;
+    pl.T = T;
+    pl.S = S;
+    const int gmax = (Gt + S - 1) / S;
+    if (gmax > 256) continue;  // one tensor-map box covers a CTA's scale rows
+    pl.Ts_max = gmax * KPG;
+    pl.nst = std::min(gmax, MAX_NST);
+    pl.smem = layout(M, NT, KPG, pl.Ts_max, rank, S, pl.nst, zeros_packed).total;
+    if (pl.smem > SMEM_LIMIT) continue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(tiles, S, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = pl.smem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = S;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, w4a16_gemv_kernel<NT, KPG>, &cfg) != cudaSuccess ||
+        clusters <= 0) {
+      cudaGetLastError();
+      continue;
+    }
+    const long waves = (long(tiles) + clusters - 1) / clusters;
+    if (best_waves < 0 || waves <= best_waves) {
+      best = pl;
+      best_waves = waves;
+    }
+  }
+  if (best_waves < 0)
+    return fail(QX_ERR_UNSUPPORTED, "w4a16_gemv: no cluster size fits K=%d N=%d rank=%d", K, N, rank);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    cache[key] = best;
+  }
+  *out = best;
+  return QX_OK;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+// 2-D tiled tensor map, no swizzle, zero fill outside the tensor.
+static int encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t cols,
+                     uint64_t rows, uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows,
+                     const char* what) {
+  const auto enc = tmap_encoder();
+  if (!enc) return fail(QX_ERR_CUDA, "w4a16_gemv: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(QX_ERR_CUDA, "w4a16_gemv: tensor map for %s (CUresult %d)", what, int(r));
+  return QX_OK;
+}
+
+template <int NT, int KPG>
+static int run(Params prm, cudaStream_t st) {
+  Plan pl;
+  int rc = make_plan<NT, KPG>(prm.M, prm.K, prm.N, prm.rank, prm.group, prm.zeros_packed, &pl);
+  if (rc != QX_OK) return rc;
+  prm.T = pl.T;
+  prm.S = pl.S;
+  prm.Ts_max = pl.Ts_max;
+  prm.gmax = pl.Ts_max / KPG;
+  prm.nst = pl.nst;
+  // qweight as 64-bit elements [K/8][N/2]; one box = a group of packed rows x
+  // (256 + 8) columns, i.e. 1056 B rows
+  rc = encode_2d(&prm.tw, CU_TENSOR_MAP_DATA_TYPE_UINT64, prm.qw, uint64_t(prm.N) / 2,
+                 uint64_t(prm.K) / 8, uint64_t(prm.N) * 4, ROWB / 8, uint32_t(KPG) * 4, "qweight");
+  if (rc != QX_OK) return rc;
+  const uint64_t Gt = uint64_t(prm.K / prm.group);
+  rc = encode_2d(&prm.ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, prm.scales, uint64_t(prm.N), Gt,
+                 uint64_t(prm.N) * 2, COLS, uint32_t(prm.gmax), "scales");
+  if (rc != QX_OK) return rc;
+  if (!prm.zeros_packed)
+    rc = encode_2d(&prm.tz, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, prm.zeros, uint64_t(prm.N), Gt,
+                   uint64_t(prm.N) * 2, COLS, uint32_t(prm.gmax), "zeros");
+  if (rc != QX_OK) return rc;
+  if (prm.rank > 0) {
+    rc = encode_2d(&prm.tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, prm.B, uint64_t(prm.N),
+                   uint64_t(prm.rank), uint64_t(prm.N) * 2, COLS, uint32_t(prm.rank), "lora_B");
+    if (rc != QX_OK) return rc;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.tiles, pl.S, 1);
@@ -552,37 +808,49 @@ static int launch(const Params& prm, const Plan& pl, cudaStream_t st) {
   attrs[na].val.clusterDim.y = pl.S;
   attrs[na].val.clusterDim.z = 1;
   ++na;
-  if (g_pdl_enabled.load(std::memory_order_relaxed)) {
+  if (prm.pdl) {
     attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attrs[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  QX_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, prm), "w4a16_gemv: launch");
+  QX_CUDA_TRY(cudaLaunchKernelEx(&cfg, w4a16_gemv_kernel<NT, KPG>, prm), "w4a16_gemv: launch");
   return check_launch("w4a16_gemv");
 }
 
 template <int NT>
-static int dispatch_kpg(const Params& prm, const Plan& pl, int kpg, cudaStream_t st) {
+static int dispatch_kpg(const Params& prm, int kpg, cudaStream_t st) {
   switch (kpg) {
-    case 1: return launch<NT, 1>(prm, pl, st);
-    case 2: return launch<NT, 2>(prm, pl, st);
-    case 4: return launch<NT, 4>(prm, pl, st);
-    default: return launch<NT, 8>(prm, pl, st);
+    case 1: return run<NT, 1>(prm, st);
+    case 2: return run<NT, 2>(prm, st);
+    case 4: return run<NT, 4>(prm, st);
+    default: return run<NT, 8>(prm, st);
   }
 }
 
-static int dispatch(const Params& prm, const Plan& pl, int kpg, cudaStream_t st) {
-  if (pl.NT == 1) return dispatch_kpg<1>(prm, pl, kpg, st);
-  if (pl.NT == 2) return dispatch_kpg<2>(prm, pl, kpg, st);
-  return dispatch_kpg<4>(prm, pl, kpg, st);
+static int dispatch(const Params& prm, int kpg, cudaStream_t st) {
+  if (prm.M <= 8) return dispatch_kpg<1>(prm, kpg, st);
+  if (prm.M <= 16) return dispatch_kpg<2>(prm, kpg, st);
+  return dispatch_kpg<4>(prm, kpg, st);
 }
 
 }  // namespace gemv
 }  // namespace qx
 
 using namespace qx;
+
+extern "C" int qx_get_device_error(unsigned* code, int reset) {
+  QX_REQUIRE(code, "get_device_error: null output");
+  QX_CUDA_TRY(cudaMemcpyFromSymbol(code, g_device_error, sizeof(unsigned)),
+              "get_device_error: read");
+  if (reset) {
+    const unsigned zero = 0;
+    QX_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(unsigned)),
+                "get_device_error: reset");
+  }
+  return QX_OK;
+}
 
 extern "C" int qx_set_pdl(int enable) {
   g_pdl_enabled.store(enable ? 1 : 0);
@@ -612,14 +880,9 @@ extern "C" int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const v
   QX_REQUIRE(aligned(zeros, zeros_packed ? 4 : 16) && aligned(y, 2),
              "w4a16_gemv: misaligned zeros/y");
   QX_REQUIRE(zeros_packed == 0 || zeros_packed == 1, "w4a16_gemv: zeros_packed must be 0 or 1");
-  const int sms = device_sm_count();
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   for (int m0 = 0; m0 < M; m0 += gemv::MROWS) {
     const int mc = std::min(gemv::MROWS, M - m0);
-    const gemv::Plan pc = gemv::make_plan(mc, K, N, rank, group_size, sms);
-    if (pc.smem > gemv::SMEM_LIMIT)
-      return fail(QX_ERR_UNSUPPORTED, "w4a16_gemv: shape needs %zu bytes of shared memory",
-                  pc.smem);
     gemv::Params prm{};
     prm.x = static_cast<const __half*>(x) + size_t(m0) * K;
     prm.qw = reinterpret_cast<const uint32_t*>(qweight);
@@ -636,11 +899,8 @@ extern "C" int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const v
     prm.zeros_packed = zeros_packed;
     prm.zero_offset = zero_offset;
     prm.lora_scale = rank > 0 ? lora_scale : 0.f;
-    prm.T = pc.T;
-    prm.S = pc.S;
-    prm.Ts_max = pc.Ts_max;
-    prm.ng_max = pc.ng_max;
-    const int rc = gemv::dispatch(prm, pc, group_size / gemv::KSTEP, st);
+    prm.pdl = g_pdl_enabled.load(std::memory_order_relaxed);
+    const int rc = gemv::dispatch(prm, group_size / gemv::KSTEP, st);
     if (rc != QX_OK) return rc;
   }
   return QX_OK;

@@ -234,3 +234,13 @@ def test_accumulation_precision(C, xscale):
     ulp = np.spacing(np.abs(y64).astype(np.float16)).astype(np.float64)
     excess = np.abs(y - y64) - 0.5 * ulp
     assert excess.max() <= 1e-4 * np.abs(y64).max(), (excess.max(), np.abs(y64).max())
+
+
+def test_no_device_error_after_calls(C):
+    """The bounded waits of the weight pipeline never timed out during the GEMV tests."""
+    import ctypes
+    from qextract_infer_b200 import _lib
+    code = ctypes.c_uint(123)
+    torch.cuda.synchronize()
+    assert _lib.load().qx_get_device_error(ctypes.byref(code), 1) == 0, _lib.last_error()
+    assert code.value == 0
