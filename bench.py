@@ -326,7 +326,7 @@ def run_b200(args):
                          "nominal_frac_8tbs": achieved / 8000.0,
                          "traffic": profiled_traffic(),
                          "algorithmic_bytes_per_launch": BYTES_PER_CALL,
-                         "kernel": "qx::gemv::w4a16_gemv_kernel<1>"},
+                         "kernel": "qx::gemv::w4a16_gemv_kernel<1, 4>"},
             "e2e": None if not e_steps else {
                     "value": BYTES_PER_CALL * e_steps / (e_ms / 1e3) / 1e9 * world, "unit": "GB/s",
                     "us_per_call": e_ms * 1e3 / e_steps,
