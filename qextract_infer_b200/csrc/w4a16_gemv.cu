@@ -7,43 +7,45 @@
 // W = s (q - z) and fp32 accumulation (w4a16_lora_gemv.cu:183-224).
 //
 // Work decomposition
-//   tile    = 256 output columns (8 warps x 32 columns).
-//   cluster = the S CTAs that split one tile's K range into whole
-//             quantisation groups (grid (tiles, S), cluster dims (1, S, 1),
-//             S in {1,2,4,8,16}, chosen with the occupancy API so the grid
-//             runs in as few waves as possible).
-//   weights = streamed by the TMA engine: one 2-D tensor copy per
-//             quantisation group (KPG*4 packed rows x 1056 B, the qweight
-//             viewed as 64-bit elements so that the 1 KB tile row plus 32 B
-//             of the next tile land as one box row), every group of the CTA
-//             in flight at once when shared memory allows (else a ring with
-//             full/empty mbarriers refilled by thread 0).  The 1056 B row
-//             pitch lets lane (g = lane/4, c = lane%4) read packed row
-//             4*ks + c, columns 4g..4g+3 of its warp, with conflict-free
-//             128-bit loads.  One TMA instruction moves ~17 KB.
+//   tile    = 256 output columns (8 compute warps x 32 columns).
+//   cluster = the S CTAs (S <= 16, any size) that split one tile's K range
+//             into whole quantisation groups as evenly as possible: grid
+//             (tiles, S), cluster dims (1, S, 1); the host picks S so that the
+//             grid runs in one wave with the fewest groups per CTA.
+//   warps   = 8 compute warps and one helper warp.  The helper initialises
+//             the barriers, starts every copy, stages the zero points, and
+//             computes the LoRA down-projection while the compute warps
+//             stream the weights.
+//   weights = one 2-D TMA copy per quantisation group (KPG*4 packed rows x
+//             1056 B: the qweight viewed as 64-bit elements, so the 1 KB tile
+//             row plus 32 B of the next tile land as one box row); every
+//             group of the CTA is in flight at once when shared memory allows
+//             (else a ring with full/empty mbarriers refilled by thread 0).
+//             The 1056 B row pitch lets lane (g = lane/4, c = lane%4) read
+//             packed row 4*ks + c, columns 4g..4g+3 of its warp, with
+//             conflict-free 128-bit loads.
 //   dot     = one LOP3 per nibble pair builds exact fp16 operands with the
 //             magic-number trick (Kim et al., "Who Says Elephants Can't Run",
-//             2022): (v & 0x000F000F) | 0x64006400 is the half2 (1024 + q_i,
-//             1024 + q_{i+4}) and (v & 0x00F000F0) | 0x64006400 is
-//             (1024 + 16 q_{i+1}, ...).  They feed mma.sync m16n8k16 with
-//             fp32 accumulation as they are: activations staged for the "x16"
-//             slots are pre-scaled by 1/16 (exact), so every product is
-//             (1024 + q) x or (64 + q) x, and the offsets leave with the zero
-//             point once per group:
-//               sum (q - z) x = C - (1024 + z) Xa - (64 + z) Xb,
-//             Xa / Xb = sums of x over the two nibble classes of the group.
-//   statics = scales, zero points, the CTA's slice of LoRA A and the tile's
-//             LoRA B arrive by TMA on one mbarrier, activations on another.
-//   LoRA    = h_s = x[:, Ks] A[Ks, :] on the tensor cores (ldmatrix.trans of
-//             the staged A slice); the LoRA product is linear in K, so each
-//             CTA adds (alpha/r) h_s B[:, tile] into its own partial sums
-//             before the weight loop and no h is exchanged.
+//             2022): (v & 0x000F000F) | 0x64006400 is the half2
+//             (1024 + q_i, 1024 + q_{i+4}) and (v & 0x00F000F0) | 0x54005400
+//             is (64 + q_{i+1}, 64 + q_{i+5}) (the nibble lands four bits up
+//             in the mantissa of 64).  They feed mma.sync m16n8k16 with fp32
+//             accumulation, the activations of each packed row permuted to
+//             (x0, x4 | x1, x5 | x2, x6 | x3, x7) in registers.  The offsets
+//             leave with the zero point once per group:
+//               sum (q - z) x = C - Off - z Sx,  Off = 1024 Xa + 64 Xb,
+//               Sx = Xa + Xb,  Xa / Xb = sums of x over the two nibble classes,
+//             and Off / Sx come from a second MMA of the same activation
+//             fragments against a constant matrix (rows 1024|64 and 1|1).
+//   LoRA    = the helper computes h_s = x[:, Ks] A[Ks, :] on the tensor cores
+//             (ldmatrix.trans of the staged A slice); the LoRA product is
+//             linear in K, so each CTA adds (alpha/r) h_s B[:, tile] into its
+//             own partial sums and no h is exchanged.
 //   reduce  = each CTA sends its fp32 partial of the columns owned by CTA j
-//             (columns [j*256/S, (j+1)*256/S)) straight into CTA j's shared
-//             memory with st.async, which completes on CTA j's receive
-//             mbarrier; CTA j waits for its expected bytes, sums the S slices
-//             in rank order (deterministic) and rounds once.  No global
-//             scratch, no atomics, no cluster-wide barrier at the end.
+//             straight into CTA j's shared memory with st.async, which
+//             completes on CTA j's receive mbarrier; CTA j waits for its
+//             expected bytes, sums the S slices in rank order (deterministic)
+//             and rounds once.  No global scratch, no atomics.
 // Programmatic dependent launch (on by default, qx_set_pdl(0) turns it off):
 // the kernel lets the next kernel in the stream launch at once, and waits for
 // the previous one only before it reads the activations.  Weights, scales,
@@ -70,23 +72,23 @@ static __device__ unsigned g_device_error = 0;
 
 namespace gemv {
 
-constexpr int WARPS = 8;
-constexpr int THREADS = WARPS * 32;
-constexpr int COLS = WARPS * 32;  // output columns per tile
-constexpr int KSTEP = 32;         // K rows per step (4 packed rows)
-constexpr int ROWB = 1056;        // smem bytes per staged packed row (1 KB + 32 B: no bank conflicts)
-constexpr int MAX_NST = 4;        // weight stages (quantisation groups) resident per CTA
-constexpr int MROWS = 32;         // batch rows per launch (4 n-tiles of 8)
-constexpr int MAX_S = 16;         // largest cluster (non-portable size)
+constexpr int WARPS = 8;                 // compute warps
+constexpr int THREADS = (WARPS + 1) * 32;  // + the helper warp
+constexpr int COLS = WARPS * 32;         // output columns per tile
+constexpr int KSTEP = 32;                // K rows per step (4 packed rows)
+constexpr int ROWB = 1056;               // smem bytes per staged packed row (1 KB + 32 B: no bank conflicts)
+constexpr int MAX_NST = 4;               // weight stages (quantisation groups) resident per CTA
+constexpr int MROWS = 32;                // batch rows per launch (4 n-tiles of 8)
+constexpr int MAX_S = 16;                // largest cluster (non-portable size)
 constexpr size_t SMEM_LIMIT = 227 * 1024;
 
-__host__ __device__ constexpr int ctas_per_sm(int nt) { return nt == 1 ? 3 : 2; }
+__host__ __device__ constexpr int ctas_per_sm(int nt) { return nt == 1 ? 3 : (nt == 2 ? 2 : 1); }
 
 struct alignas(64) Params {
   CUtensorMap tw;  // qweight as u64 [K/8][N/2], box {132, KPG*4}
   CUtensorMap tb;  // LoRA B fp16 [r][N], box {256, r}
   CUtensorMap ts;  // scales fp16 [K/g][N], box {256, gmax}
-  CUtensorMap tz;  // fp16 zeros [K/g][N], box {256, gmax} (packed qzeros use plain loads)
+  CUtensorMap tz;  // fp16 zeros [K/g][N], box {256, gmax}; packed qzeros int32 [K/g][N/8], box {32, gmax}
   const __half* x;
   const uint32_t* qw;
   const __half* scales;
@@ -95,13 +97,14 @@ struct alignas(64) Params {
   const __half* B;
   __half* y;
   int M, K, N, rank, group, zeros_packed, zero_offset;
+  int zeros_tma;  // zero points by TMA (fp16 always; packed when rows are 16 B multiples)
   float lora_scale;
-  int T, S, Ts_max, gmax, nst, pdl;
+  int T, S, cpr, Ts_max, gmax, nst, pdl;
 };
 
 // Shared-memory carve-up (byte offsets), identical on host and device.
 struct Layout {
-  unsigned bars, ring, sz_s, sz_z, sf, xraw, xs, xks, ab, hs, red, recv, total;
+  unsigned bars, ring, sz_s, sz_z, xraw, xs, xks, As, Bs, hs, recv, total;
 };
 
 __host__ __device__ inline unsigned take(unsigned& o, size_t bytes) {
@@ -114,27 +117,27 @@ __host__ __device__ inline unsigned take(unsigned& o, size_t bytes) {
 // 4 banks apart, so 8 rows x 4 words of an MMA fragment hit distinct banks
 __host__ __device__ inline int xstride(int Ts_max) { return Ts_max * KSTEP + 8; }
 
-// M = batch rows of this launch (<= 32), NT = 8-row MMA tiles covering them.
-__host__ __device__ inline Layout layout(int M, int NT, int KPG, int Ts_max, int rank, int S,
-                                         int nst, int zeros_packed) {
+// columns each CTA of an S-cluster finalises: 256 / S rounded up to 8
+__host__ __device__ inline int owner_cols(int S) { return ((COLS + S - 1) / S + 7) / 8 * 8; }
+
+// M = batch rows of this launch (<= 32).
+__host__ __device__ inline Layout layout(int M, int KPG, int Ts_max, int rank, int S, int nst,
+                                         int zeros_packed) {
   const int gmax = Ts_max / KPG;
+  const size_t Mp = M <= 8 ? 8 : (M <= 16 ? 16 : 32);  // NT * 8 of the kernel instance
   Layout L;
   unsigned o = 0;
-  const size_t Mp = size_t(NT) * 8;
-  L.bars = take(o, size_t(4 + 2 * nst) * 8);          // statics, x, B, recv, full[nst], empty[nst]
+  L.bars = take(o, size_t(5 + 2 * nst) * 8);  // statics, x, B, h, recv, full[nst], empty[nst]
   L.ring = take(o, size_t(nst) * KPG * 4 * ROWB);     // weight stages
   L.sz_s = take(o, size_t(gmax) * COLS * 2);          // scales [gmax][256]
   L.sz_z = take(o, size_t(gmax) * (zeros_packed ? COLS / 2 : COLS * 2));  // [gmax][32] u32 or [gmax][256] fp16
-  L.sf = take(o, size_t(gmax) * COLS * 8);            // (s, s*z) as floats [gmax][256]
-  L.xraw = take(o, size_t(M) * xstride(Ts_max) * 2);  // activations [M][Ks(+8)] as loaded
-  L.xs = take(o, size_t(Ts_max) * M * 4 * 16);        // activations in MMA-B order [t][m][c]
+  L.xraw = take(o, size_t(M) * xstride(Ts_max) * 2);  // activations [M][Ks(+8)]
+  L.xs = take(o, size_t(Ts_max) * Mp * 4 * 16);       // in MMA-B order [t][Mp][c], rows >= M zero
   L.xks = take(o, size_t(gmax) * Mp * 2 * 4);         // per group (Off, Sx) per row [g][Mp]
-  // LoRA A slice [Ks][r] for the down-projection, then the LoRA B tile [r][256]
-  const size_t a_bytes = size_t(Ts_max) * KSTEP * rank * 2, b_bytes = size_t(rank) * COLS * 2;
-  L.ab = take(o, a_bytes > b_bytes ? a_bytes : b_bytes);
+  L.As = take(o, size_t(Ts_max) * KSTEP * rank * 2);  // LoRA A slice [Ks][r]
+  L.Bs = take(o, size_t(rank) * COLS * 2);            // LoRA B tile [r][256]
   L.hs = take(o, size_t(M) * rank * 4);               // h_s [M][r]
-  L.red = take(o, rank > 0 ? size_t(WARPS) * 16 * (M < 8 ? M : 8) * 4 : 0);  // split-k partials [w][16][min(M,8)]
-  L.recv = take(o, size_t(M) * COLS * 4);             // partials pushed by the cluster [S][M][256/S]
+  L.recv = take(o, size_t(S) * M * owner_cols(S) * 4);  // partials from the cluster [S][M][cpr]
   L.total = o;
   return L;
 }
@@ -274,113 +277,119 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   const int gr0 = s * Gt / S, gr1 = (s + 1) * Gt / S;
   const int ngrp = gr1 - gr0;
   const int ks0 = gr0 * KPG;
-  const int Ts = ngrp * KPG;
-  const int Ks = Ts * KSTEP;
+  const int Ks = ngrp * KPG * KSTEP;
   const int XS = xstride(p.Ts_max);
   const int M = p.M, N = p.N, R = p.rank;
-  constexpr int Mp = NT * 8;
   constexpr int STAGE = KPG * 4 * ROWB;
+  constexpr int Mp = NT * 8;
   constexpr uint32_t STAGE_TX = uint32_t(STAGE);  // full box, zero-filled past N
   const int nst = p.nst;
   const int n_tile0 = tile * COLS;
-  const int lcol = warp * 32 + 4 * g;  // first of this lane's 4 columns (tile-local)
-  const bool col_ok = n_tile0 + lcol < N;  // N % 8 == 0: all 4 columns valid or none
   const int k0 = ks0 * KSTEP;
-  const int CPR = COLS / S;            // columns each CTA of the cluster finalises
-  const int cb = n_tile0 + s * CPR;    // first column this CTA finalises
-  const int own_cols = max(0, min(CPR, N - cb));
+  const int CPR = p.cpr;  // columns each CTA of the cluster finalises
+  const int own_cols = max(0, min(min(CPR, COLS - s * CPR), N - (n_tile0 + s * CPR)));
 
-  const Layout L = layout(M, NT, KPG, p.Ts_max, R, S, nst, p.zeros_packed);
-  unsigned char* ring = smem + L.ring;
-  const unsigned char* sz_s = smem + L.sz_s;
-  unsigned char* sz_z = smem + L.sz_z;
-  __half* xraw = reinterpret_cast<__half*>(smem + L.xraw);
-  uint4* xs = reinterpret_cast<uint4*>(smem + L.xs);
-  float* xks = reinterpret_cast<float*>(smem + L.xks);
-  float2* sf = reinterpret_cast<float2*>(smem + L.sf);
-  const __half* As = reinterpret_cast<const __half*>(smem + L.ab);
-  const __half* Bs = reinterpret_cast<const __half*>(smem + L.ab);  // after the LoRA-down
-  float* hs = reinterpret_cast<float*>(smem + L.hs);
-  float* red = reinterpret_cast<float*>(smem + L.red);
+  const Layout L = layout(M, KPG, p.Ts_max, R, S, nst, p.zeros_packed);
+  const __half* xraw = reinterpret_cast<const __half*>(smem + L.xraw);
   const float* recv = reinterpret_cast<const float*>(smem + L.recv);
   const uint32_t bar_st = smem_addr(smem + L.bars);  // scales, zeros, LoRA A
   const uint32_t bar_x = bar_st + 8;                 // activations
   const uint32_t bar_b = bar_st + 16;                // LoRA B
-  const uint32_t bar_rv = bar_st + 24;               // partials from the cluster
-  const uint32_t full0 = bar_st + 32;                // full[i]  = full0 + 8 i
+  const uint32_t bar_h = bar_st + 24;                // h_s computed
+  const uint32_t bar_rv = bar_st + 32;               // partials from the cluster
+  const uint32_t full0 = bar_st + 40;                // full[i]  = full0 + 8 i
   const uint32_t empty0 = full0 + 8 * nst;           // empty[i] = empty0 + 8 i
   const int wx = n_tile0 / 2;  // tile origin in 64-bit elements (x * 8 B = tile * 1 KB)
-  const uint32_t ring_s = smem_addr(ring);
+  const uint32_t ring_s = smem_addr(smem + L.ring);
 
   // The next kernel in the stream may launch as soon as every CTA of this one
   // is resident: it only streams its own weights until it waits for us.
   grid_dep_launch();
 
-  // 1. warp 0 starts every copy; only the activations wait for the previous
-  //    kernel in the stream.
-  if (warp == 0) {
-    const uint32_t xrow_bytes = uint32_t(Ks) * 2;
+  if (warp == WARPS && lane == 0) {
+    prefetch_tmap(&p.tw);
+    mbar_init(bar_st, p.zeros_tma ? 1 : 33);  // + one arrival per helper lane (plain-loaded zeros)
+    mbar_init(bar_x, 1);
+    mbar_init(bar_b, 1);
+    mbar_init(bar_h, 32);
+    mbar_init(bar_rv, 1);
+    for (int i = 0; i < nst; ++i) {
+      mbar_init(full0 + 8 * i, 1);
+      mbar_init(empty0 + 8 * i, WARPS);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;\nfence.proxy.async.shared::cta;" :::
+                     "memory");
+  }
+  __syncthreads();  // barriers initialised
+  // Peers send partial sums only after every CTA of the cluster has
+  // initialised its receive barrier (arrive now, wait before sending).
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+
+  const uint32_t xrow_bytes = uint32_t(Ks) * 2;
+  if (warp == 0) {  // the activations first: they gate the LoRA-down and every MMA
+    if (lane == 0) mbar_expect_tx(bar_x, uint32_t(M) * xrow_bytes);
+    if (p.pdl) {  // activations may come from the previous kernel in the stream
+      if (lane == 0) grid_dep_wait();
+    }
+    __syncwarp();
+    for (int m = lane; m < M; m += 32)
+      bulk_g2s(smem_addr(smem + L.xraw) + uint32_t(m * XS) * 2, p.x + size_t(m) * p.K + k0,
+               xrow_bytes, bar_x);
+  }
+
+  if (warp == WARPS) {
+    // ---------------- helper warp ----------------
+    __half* As = reinterpret_cast<__half*>(smem + L.As);
     if (lane == 0) {
-      prefetch_tmap(&p.tw);
-      mbar_init(bar_st, 1);
-      mbar_init(bar_x, 1);
-      mbar_init(bar_b, 1);
-      mbar_init(bar_rv, 1);
-      for (int i = 0; i < nst; ++i) {
-        mbar_init(full0 + 8 * i, 1);
-        mbar_init(empty0 + 8 * i, WARPS);
-      }
-      asm volatile("fence.mbarrier_init.release.cluster;\nfence.proxy.async.shared::cta;" :::
-                       "memory");
       // bytes the S CTAs of the cluster will send for this CTA's columns
       mbar_expect_tx(bar_rv, uint32_t(S * M * own_cols) * 4u);
-      const uint32_t sz_bytes = uint32_t(p.gmax) * COLS * 2 * (p.zeros_packed ? 1 : 2);
+      const uint32_t sz_bytes =
+          uint32_t(p.gmax) * (COLS * 2 + (p.zeros_tma ? (p.zeros_packed ? COLS / 2 : COLS * 2) : 0));
       mbar_expect_tx(bar_st, sz_bytes + uint32_t(Ks * R) * 2);
-      // scales / zero points of this CTA's groups (gmax rows; rows past the
-      // CTA's range are read but unused)
-      tma_2d(smem_addr(sz_s), &p.ts, n_tile0, gr0, bar_st);
-      if (!p.zeros_packed) tma_2d(smem_addr(sz_z), &p.tz, n_tile0, gr0, bar_st);
-      if (R > 0)  // LoRA: this CTA's rows of A (B follows once A is consumed)
-        bulk_g2s(smem_addr(As), p.A + size_t(k0) * R, uint32_t(Ks * R) * 2, bar_st);
+      // LoRA A rows (the helper's next job), the weight groups, scales / fp16
+      // zero points of this CTA's groups (gmax rows; rows past the CTA's
+      // range are read but unused), the LoRA B tile
+      if (R > 0) bulk_g2s(smem_addr(As), p.A + size_t(k0) * R, uint32_t(Ks * R) * 2, bar_st);
       const uint64_t pol = evict_first_policy();
       for (int i = 0; i < min(ngrp, nst); ++i) {
         mbar_expect_tx(full0 + 8 * i, STAGE_TX);
         tma_2d_hint(ring_s + i * STAGE, &p.tw, wx, (ks0 + i * KPG) * 4, full0 + 8 * i, pol);
       }
-      mbar_expect_tx(bar_x, uint32_t(M) * xrow_bytes);
+      tma_2d(smem_addr(smem + L.sz_s), &p.ts, n_tile0, gr0, bar_st);
+      if (p.zeros_tma)
+        tma_2d(smem_addr(smem + L.sz_z), &p.tz, p.zeros_packed ? n_tile0 / 8 : n_tile0, gr0, bar_st);
+      if (R > 0) {
+        mbar_expect_tx(bar_b, uint32_t(R * COLS) * 2);
+        tma_2d(smem_addr(smem + L.Bs), &p.tb, n_tile0, 0, bar_b);
+      }
     }
-    __syncwarp();
-    if (p.pdl) {  // activations may come from the previous kernel in the stream
-      if (lane == 0) grid_dep_wait();
-      __syncwarp();
-    }
-    for (int m = lane; m < M; m += 32)
-      bulk_g2s(smem_addr(xraw + m * XS), p.x + size_t(m) * p.K + k0, xrow_bytes, bar_x);
-  }
-  // Peers send partial sums only after every CTA of the cluster has
-  // initialised its receive barrier (arrive now, wait before sending).
-  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-
-  // GPTQ qzeros rows are N/2 bytes (not always a 16 B multiple): plain loads
-  if (p.zeros_packed) {
-    const int zwords = N >> 3;
-    const uint32_t* zsrc = static_cast<const uint32_t*>(p.zeros);
-    for (int it = tid; it < p.gmax * (COLS / 8); it += THREADS) {
-      const int row = gr0 + (it >> 5), col = (n_tile0 >> 3) + (it & 31);
-      reinterpret_cast<uint32_t*>(sz_z)[it] =
-          (row < Gt && col < zwords) ? __ldg(zsrc + size_t(row) * zwords + col) : 0u;
+    // GPTQ qzeros rows of N/2 bytes that are not a 16 B multiple: plain loads
+    if (!p.zeros_tma) {
+      const int zwords = N >> 3;
+      const uint32_t* zsrc = static_cast<const uint32_t*>(p.zeros);
+      uint32_t* zdst = reinterpret_cast<uint32_t*>(smem + L.sz_z);
+      for (int it = lane; it < p.gmax * (COLS / 8); it += 32) {
+        const int row = gr0 + (it >> 5), col = (n_tile0 >> 3) + (it & 31);
+        zdst[it] = (row < Gt && col < zwords) ? __ldg(zsrc + size_t(row) * zwords + col) : 0u;
+      }
+      mbar_arrive(bar_st);
     }
   }
-  __syncthreads();  // barriers initialised, zero points staged
-  mbar_wait(bar_st, 0);
-  mbar_wait(bar_x, 0);
 
-  // 2. activations in MMA-B order (x0, x4, x1/16, x5/16, x2, x6, x3/16, x7/16)
-  //    per packed row, and per group the sums over the two nibble classes.
-  //    Items (m, t, c) with c fastest: a group of row m is an aligned block
-  //    of 4*KPG lanes; the item count is padded to whole warps for the
-  //    shuffles.
+  // activations in MMA-B order (x0,x4 | x1,x5 | x2,x6 | x3,x7) per packed row,
+  // rows M..Mp-1 zero, and per group the sums over the two nibble classes:
+  // (Off, Sx) = (1024 Xa + 64 Xb, Xa + Xb), by the whole CTA.  Items
+  // (m, t, c), c fastest: a group of row m is an aligned block of 4*KPG
+  // lanes; the item count is padded to whole warps for the shuffles.
   {
+    const int Ts = ngrp * KPG;
+    uint4* xsw = reinterpret_cast<uint4*>(smem + L.xs);
+    float* xksw = reinterpret_cast<float*>(smem + L.xks);
+    for (int it = tid; it < Ts * (Mp - M) * 4; it += THREADS) {
+      const int t = it / ((Mp - M) * 4), r = it - t * ((Mp - M) * 4);
+      xsw[(t * Mp + M) * 4 + r] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    mbar_wait(bar_x, 0);
     const int tot = M * Ts * 4, totp = (tot + 31) & ~31;
     for (int it = tid; it < totp; it += THREADS) {
       const bool ok = it < tot;
@@ -389,12 +398,8 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (ok) {
         v = *reinterpret_cast<const uint4*>(xraw + m * XS + t * KSTEP + cc * 8);
-        uint4 o;
-        o.x = prmt(v.x, v.z, 0x5410u);                         // (x0, x4)
-        o.y = hmul2_u32(prmt(v.x, v.z, 0x7632u), 0x2C002C00u);  // (x1, x5) / 16
-        o.z = prmt(v.y, v.w, 0x5410u);                         // (x2, x6)
-        o.w = hmul2_u32(prmt(v.y, v.w, 0x7632u), 0x2C002C00u);  // (x3, x7) / 16
-        xs[(t * M + m) * 4 + cc] = o;
+        xsw[(t * Mp + m) * 4 + cc] = make_uint4(prmt(v.x, v.z, 0x5410u), prmt(v.x, v.z, 0x7632u),
+                                                prmt(v.y, v.w, 0x5410u), prmt(v.y, v.w, 0x7632u));
       }
       const float2 a0 = h2_to_f2(v.x), a1 = h2_to_f2(v.y), a2 = h2_to_f2(v.z), a3 = h2_to_f2(v.w);
       float xa = (a0.x + a1.x) + (a2.x + a3.x);  // x0 + x2 + x4 + x6
@@ -404,46 +409,34 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
         xa += __shfl_xor_sync(0xffffffffu, xa, w);
         xb += __shfl_xor_sync(0xffffffffu, xb, w);
       }
-      if (ok && cc == 0 && t % KPG == 0)  // (Off, Sx) = (1024 Xa + 64 Xb, Xa + Xb)
-        *reinterpret_cast<float2*>(xks + ((t / KPG) * Mp + m) * 2) =
+      if (ok && cc == 0 && t % KPG == 0)
+        *reinterpret_cast<float2*>(xksw + ((t / KPG) * Mp + m) * 2) =
             make_float2(fmaf(1024.f, xa, 64.f * xb), xa + xb);
     }
-    // scales and zero points of the CTA's groups as floats (s, s * z)
-    for (int it = tid; it < ngrp * COLS; it += THREADS) {
-      const int gi = it >> 8, col = it & (COLS - 1);
-      const float sc = __half2float(reinterpret_cast<const __half*>(sz_s)[it]);
-      float z;
-      if (p.zeros_packed)
-        z = float(((reinterpret_cast<const uint32_t*>(sz_z)[gi * (COLS / 8) + (col >> 3)] >>
-                    (4 * (col & 7))) & 0xFu) + unsigned(p.zero_offset));
-      else
-        z = __half2float(reinterpret_cast<const __half*>(sz_z)[it]);
-      sf[it] = make_float2(sc, sc * z);
-    }
   }
+  __syncthreads();  // permuted activations and group sums ready
 
-  // 3. LoRA down-projection h_s^T[r][m] = A^T[r][Ks] . x^T[Ks][m] on the
-  //    tensor cores, 16 x 8 tiles (rank rows x batch rows) over warps, the K
-  //    range split too when there are fewer tiles than warps.
-  int nsplit = 1;
-  const int MR = M < 8 ? M : 8;  // rows kept in the split-k partials
-  if (R > 0) {
+  if (warp == WARPS) {  // helper: the LoRA down-projection
+    if (R == 0) return;
+    __half* As = reinterpret_cast<__half*>(smem + L.As);
+    float* hs = reinterpret_cast<float*>(smem + L.hs);
+    // LoRA down-projection h_s^T[r][m] = A^T[r][Ks] . x^T[Ks][m]: 16 x 8 tiles
+    // (rank rows x batch rows), two accumulators per tile (even / odd k blocks)
+    mbar_wait(bar_st, 0);
     const int RT = R >= 16 ? R / 16 : 1;
-    const int ntiles = RT * NT;
-    nsplit = ntiles >= WARPS ? 1 : WARPS / ntiles;
     const int KB = Ks / 16;
-    for (int tl = warp % ntiles; tl < ntiles; tl += (ntiles >= WARPS ? WARPS : ntiles)) {
+    const int mi = lane >> 3, ri = lane & 7;
+    for (int tl = 0; tl < RT * NT; ++tl) {
       const int rt = tl / NT, nt = tl - rt * NT;
-      const int part_k = ntiles >= WARPS ? 0 : warp / ntiles;
-      float h4[4] = {0.f, 0.f, 0.f, 0.f};
-      const int mi = lane >> 3, ri = lane & 7;
       const int mb = nt * 8 + g;  // batch row of this lane's B fragment
       const __half* xrow = xraw + mb * XS + 2 * c;
-      for (int kb = part_k; kb < KB; kb += nsplit) {
-        uint32_t a[4];
-        {
-          const int k = kb * 16 + ri + 8 * (mi >> 1);
-          const int j = rt * 16 + 8 * (mi & 1);
+      const int j = rt * 16 + 8 * (mi & 1);
+      float h4[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      for (int kb = 0; kb < KB; kb += 2) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int k = (kb + u) * 16 + ri + 8 * (mi >> 1);
+          uint32_t a[4];
           if (R >= 16) {
             ldsm_x4_t(a, As + k * R + j);
           } else {  // rank 8: rows 8..15 of the tile are zero
@@ -451,61 +444,35 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
             a[1] = 0u;
             a[3] = 0u;
           }
-        }
-        uint32_t b0 = 0u, b1 = 0u;
-        if (mb < M) {
-          b0 = *reinterpret_cast<const uint32_t*>(xrow + kb * 16);
-          b1 = *reinterpret_cast<const uint32_t*>(xrow + kb * 16 + 8);
-        }
-        mma_16816(h4, a[0], a[1], a[2], a[3], b0, b1);
-      }
-      if (nsplit == 1) {
-        const int j0 = rt * 16 + g, m0 = nt * 8 + 2 * c;
-        if (m0 < M) hs[m0 * R + j0] = h4[0];
-        if (m0 + 1 < M) hs[(m0 + 1) * R + j0] = h4[1];
-        if (j0 + 8 < R) {
-          if (m0 < M) hs[m0 * R + j0 + 8] = h4[2];
-          if (m0 + 1 < M) hs[(m0 + 1) * R + j0 + 8] = h4[3];
-        }
-      } else {  // tile-local rows 2c, 2c+1 (< MR = min(M, 8))
-        float* rw = red + warp * 16 * MR;  // [16][MR]
-        const int ml = 2 * c;
-        if (nt * 8 + ml < M) {
-          rw[g * MR + ml] = h4[0];
-          rw[(g + 8) * MR + ml] = h4[2];
-        }
-        if (nt * 8 + ml + 1 < M) {
-          rw[g * MR + ml + 1] = h4[1];
-          rw[(g + 8) * MR + ml + 1] = h4[3];
+          uint32_t b0 = 0u, b1 = 0u;
+          if (mb < M) {
+            b0 = *reinterpret_cast<const uint32_t*>(xrow + (kb + u) * 16);
+            b1 = *reinterpret_cast<const uint32_t*>(xrow + (kb + u) * 16 + 8);
+          }
+          mma_16816(h4[u], a[0], a[1], a[2], a[3], b0, b1);
         }
       }
-    }
-  }
-  __syncthreads();  // xs, xks, hs or the split-k partials ready; A consumed
-  if (R > 0) {
-    if (tid == 0) {  // LoRA B tile into the A slice's space, lands during the weight loop
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_expect_tx(bar_b, uint32_t(R * COLS) * 2);
-      tma_2d(smem_addr(Bs), &p.tb, n_tile0, 0, bar_b);
-    }
-    if (nsplit > 1) {  // warp q2 * ntiles + tl holds split q2 of tile tl
-      const int ntiles = (R >= 16 ? R / 16 : 1) * NT;
-      for (int it = tid; it < ntiles * 16 * MR; it += THREADS) {
-        const int tl = it / (16 * MR), e = it - tl * (16 * MR), jr = e / MR, ml = e - jr * MR;
-        const int rt = tl / NT, nt = tl - rt * NT;
-        const int j = rt * 16 + jr, m = nt * 8 + ml;
-        if (j < R && m < M) {
-          float v = 0.f;
-          for (int q2 = 0; q2 < nsplit; ++q2) v += red[(q2 * ntiles + tl) * 16 * MR + e];
-          hs[m * R + j] = v;
-        }
+      const int j0 = rt * 16 + g, m0 = nt * 8 + 2 * c;
+      if (m0 < M) hs[m0 * R + j0] = h4[0][0] + h4[1][0];
+      if (m0 + 1 < M) hs[(m0 + 1) * R + j0] = h4[0][1] + h4[1][1];
+      if (j0 + 8 < R) {
+        if (m0 < M) hs[m0 * R + j0 + 8] = h4[0][2] + h4[1][2];
+        if (m0 + 1 < M) hs[(m0 + 1) * R + j0 + 8] = h4[0][3] + h4[1][3];
       }
-      __syncthreads();
     }
+    mbar_arrive(bar_h);  // every lane: its h_s stores are released
+    return;
   }
 
-  // 4. main loop over this CTA's quantisation groups (pipeline stages);
-  //    acc[pp][nt][i] holds column lcol + 2 pp + (i >> 1), row nt*8 + 2c + (i & 1)
+  // ---------------- compute warps ----------------
+  const int lcol = warp * 32 + 4 * g;  // first of this lane's 4 columns (tile-local)
+  const bool col_ok = n_tile0 + lcol < N;  // N % 8 == 0: all 4 columns valid or none
+  const unsigned char* sz_s = smem + L.sz_s;
+  const unsigned char* sz_z = smem + L.sz_z;
+  const uint4* xs = reinterpret_cast<const uint4*>(smem + L.xs);
+  const float* xks = reinterpret_cast<const float*>(smem + L.xks);
+
+  // acc[pp][nt][i] holds column lcol + 2 pp + (i >> 1), row nt*8 + 2c + (i & 1)
   float acc[2][NT][4], cgr[2][NT][4];
 #pragma unroll
   for (int pp = 0; pp < 2; ++pp)
@@ -514,46 +481,33 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[pp][nt][i] = 0.f;
 
+  mbar_wait(bar_st, 0);
   int st = 0, use = 0;  // ring stage and wrap count
-  const unsigned char* wlane = ring + c * ROWB + lcol * 4;
+  const unsigned char* wlane = smem + L.ring + c * ROWB + lcol * 4;
   for (int gi = 0; gi < ngrp; ++gi) {
     mbar_wait(full0 + 8 * st, use & 1);
-    uint4 wq[KPG];
-#pragma unroll
-    for (int j = 0; j < KPG; ++j)
-      wq[j] = col_ok ? *reinterpret_cast<const uint4*>(wlane + st * STAGE + j * 4 * ROWB)
-                     : make_uint4(0u, 0u, 0u, 0u);
-    if (gi + nst < ngrp) {  // refill this stage with group gi + nst
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty0 + 8 * st);
-      if (tid == 0) {
-        mbar_wait(empty0 + 8 * st, use & 1);
-        mbar_expect_tx(full0 + 8 * st, STAGE_TX);
-        tma_2d_hint(ring_s + st * STAGE, &p.tw, wx, (ks0 + (gi + nst) * KPG) * 4, full0 + 8 * st,
-                    evict_first_policy());
-      }
-      __syncwarp();
-    }
-    const uint4* xg = xs + size_t(gi) * KPG * M * 4;
 #pragma unroll
     for (int j = 0; j < KPG; ++j) {
-      const uint32_t wv[4] = {wq[j].x, wq[j].y, wq[j].z, wq[j].w};
+      const int t = gi * KPG + j;
+      const uint4 wq = col_ok ? *reinterpret_cast<const uint4*>(wlane + st * STAGE + j * 4 * ROWB)
+                              : make_uint4(0u, 0u, 0u, 0u);
+      const uint32_t wv[4] = {wq.x, wq.y, wq.z, wq.w};
       uint32_t q[4][4];
 #pragma unroll
       for (int jw = 0; jw < 4; ++jw) {
         const uint32_t hi = wv[jw] >> 8;
         q[jw][0] = lop3_and_or(wv[jw], 0x000F000Fu, 0x64006400u);  // (1024+q0, 1024+q4)
-        q[jw][1] = lop3_and_or(wv[jw], 0x00F000F0u, 0x64006400u);  // (1024+16q1, 1024+16q5)
+        q[jw][1] = lop3_and_or(wv[jw], 0x00F000F0u, 0x54005400u);  // (64+q1, 64+q5)
         q[jw][2] = lop3_and_or(hi, 0x000F000Fu, 0x64006400u);      // (1024+q2, 1024+q6)
-        q[jw][3] = lop3_and_or(hi, 0x00F000F0u, 0x64006400u);      // (1024+16q3, 1024+16q7)
+        q[jw][3] = lop3_and_or(hi, 0x00F000F0u, 0x54005400u);      // (64+q3, 64+q7)
       }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const int mrow = nt * 8 + g;
-        const uint4 bx = mrow < M ? xg[(j * M + mrow) * 4 + c] : make_uint4(0u, 0u, 0u, 0u);
+        // activations of row nt*8 + g, packed row c: (x0,x4 | x1,x5 | x2,x6 | x3,x7)
+        const uint4 bx = xs[(t * Mp + nt * 8 + g) * 4 + c];
 #pragma unroll
         for (int pp = 0; pp < 2; ++pp) {
-          if (j == 0)  // the group's first product starts from zero
+          if (j == 0)  // the group's first products start from zero
             mma_16816_zc(cgr[pp][nt], q[2 * pp][0], q[2 * pp + 1][0], q[2 * pp][1],
                          q[2 * pp + 1][1], bx.x, bx.y);
           else
@@ -564,22 +518,51 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
         }
       }
     }
+    if (gi + nst < ngrp) {  // every warp has read this stage: refill it with group gi + nst
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty0 + 8 * st);
+      if (tid == 0) {
+        mbar_wait(empty0 + 8 * st, use & 1);
+        mbar_expect_tx(full0 + 8 * st, STAGE_TX);
+        tma_2d_hint(ring_s + st * STAGE, &p.tw, wx, (ks0 + (gi + nst) * KPG) * 4, full0 + 8 * st,
+                    evict_first_policy());
+      }
+      __syncwarp();
+    }
     {  // group correction: acc += s (C - Off) - (s z) Sx
-      const float4 c01 = *reinterpret_cast<const float4*>(sf + gi * COLS + lcol);      // s, sz of cols 0, 1
-      const float4 c23 = *reinterpret_cast<const float4*>(sf + gi * COLS + lcol + 2);  // cols 2, 3
-      const float sv[4] = {c01.x, c01.z, c23.x, c23.z}, zv[4] = {c01.y, c01.w, c23.y, c23.w};
+      const uint2 sc = *reinterpret_cast<const uint2*>(sz_s + (gi * COLS + lcol) * 2);
+      const float2 s01 = h2_to_f2(sc.x), s23 = h2_to_f2(sc.y);
+      const float sv[4] = {s01.x, s01.y, s23.x, s23.y};
+      float zv[4];
+      if (p.zeros_packed) {
+        const uint32_t zw =
+            *reinterpret_cast<const uint32_t*>(sz_z + (gi * (COLS / 8) + (lcol >> 3)) * 4);
+        const int sh = (lcol & 7) * 4;
+#pragma unroll
+        for (int jz = 0; jz < 4; ++jz)
+          zv[jz] = float(((zw >> (sh + 4 * jz)) & 0xFu) + unsigned(p.zero_offset));
+      } else {
+        const uint2 zh = *reinterpret_cast<const uint2*>(sz_z + (gi * COLS + lcol) * 2);
+        const float2 z01 = h2_to_f2(zh.x), z23 = h2_to_f2(zh.y);
+        zv[0] = z01.x;
+        zv[1] = z01.y;
+        zv[2] = z23.x;
+        zv[3] = z23.y;
+      }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        // (Off, Sx) of rows nt*8 + 2c and + 1 (rows >= M hold garbage that
-        // only reaches discarded accumulators)
+        // (Off, Sx) of rows nt*8 + 2c, + 1 (rows >= M hold stale values that
+        // only reach discarded accumulators)
         const float4 xv = *reinterpret_cast<const float4*>(xks + (gi * Mp + nt * 8 + 2 * c) * 2);
+        const float off0 = xv.x, sx0 = xv.y, off1 = xv.z, sx1 = xv.w;
 #pragma unroll
         for (int pp = 0; pp < 2; ++pp) {
-          const float s0 = sv[2 * pp], z0 = zv[2 * pp], s1 = sv[2 * pp + 1], z1 = zv[2 * pp + 1];
-          acc[pp][nt][0] = fmaf(-z0, xv.y, fmaf(s0, cgr[pp][nt][0] - xv.x, acc[pp][nt][0]));
-          acc[pp][nt][1] = fmaf(-z0, xv.w, fmaf(s0, cgr[pp][nt][1] - xv.z, acc[pp][nt][1]));
-          acc[pp][nt][2] = fmaf(-z1, xv.y, fmaf(s1, cgr[pp][nt][2] - xv.x, acc[pp][nt][2]));
-          acc[pp][nt][3] = fmaf(-z1, xv.w, fmaf(s1, cgr[pp][nt][3] - xv.z, acc[pp][nt][3]));
+          const float s0 = sv[2 * pp], s1 = sv[2 * pp + 1];
+          const float z0 = s0 * zv[2 * pp], z1 = s1 * zv[2 * pp + 1];
+          acc[pp][nt][0] = fmaf(-z0, sx0, fmaf(s0, cgr[pp][nt][0] - off0, acc[pp][nt][0]));
+          acc[pp][nt][1] = fmaf(-z0, sx1, fmaf(s0, cgr[pp][nt][1] - off1, acc[pp][nt][1]));
+          acc[pp][nt][2] = fmaf(-z1, sx0, fmaf(s1, cgr[pp][nt][2] - off0, acc[pp][nt][2]));
+          acc[pp][nt][3] = fmaf(-z1, sx1, fmaf(s1, cgr[pp][nt][3] - off1, acc[pp][nt][3]));
         }
       }
     }
@@ -589,41 +572,61 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     }
   }
 
-  // 5. this CTA's LoRA term (alpha/r) h_s B[:, cols] joins its partial sums
+  // this CTA's LoRA term (alpha/r) h_s B[:, tile] joins its partial sums on
+  // the tensor cores: A = B^T (rows = this lane's columns), B operand =
+  // (alpha/r) h_s^T split into fp16 high and low parts (~22-bit product)
   if (R > 0) {
+    const int RT = R >= 16 ? R / 16 : 1;
+    mbar_wait(bar_h, 0);
     mbar_wait(bar_b, 0);
-    if (col_ok) {
+    const float* hs = reinterpret_cast<const float*>(smem + L.hs);
+    const __half* Bs = reinterpret_cast<const __half*>(smem + L.Bs);
+    for (int kt = 0; kt < RT; ++kt) {
+      const int j = kt * 16 + 2 * c;  // this lane's k (rank) pair; j + 8 for the upper half
+      uint32_t bh[NT][2], bl[NT][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
+        const int m = nt * 8 + g;
+        float2 h0 = make_float2(0.f, 0.f), h1 = make_float2(0.f, 0.f);
+        if (m < M) {
+          h0 = *reinterpret_cast<const float2*>(hs + m * R + j);
+          if (R >= 16) h1 = *reinterpret_cast<const float2*>(hs + m * R + j + 8);
+        }
+        const float ls = p.lora_scale;
+        const __half2 h0h = __floats2half2_rn(ls * h0.x, ls * h0.y);
+        const __half2 h1h = __floats2half2_rn(ls * h1.x, ls * h1.y);
+        const float2 h0r = __half22float2(h0h), h1r = __half22float2(h1h);
+        const __half2 h0l = __floats2half2_rn(ls * h0.x - h0r.x, ls * h0.y - h0r.y);
+        const __half2 h1l = __floats2half2_rn(ls * h1.x - h1r.x, ls * h1.y - h1r.y);
+        bh[nt][0] = *reinterpret_cast<const uint32_t*>(&h0h);
+        bh[nt][1] = *reinterpret_cast<const uint32_t*>(&h1h);
+        bl[nt][0] = *reinterpret_cast<const uint32_t*>(&h0l);
+        bl[nt][1] = *reinterpret_cast<const uint32_t*>(&h1l);
+      }
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-          const int m = nt * 8 + 2 * c + rr;
-          if (m < M) {
-            float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
-            for (int j0 = 0; j0 < R; j0 += 8) {  // rank is a multiple of 8
+      for (int pp = 0; pp < 2; ++pp) {
+        // (B[j][col], B[j+1][col]) for col = lcol + 2pp (row g) and + 1 (row g + 8)
+        const __half* bcol = Bs + lcol + 2 * pp;
+        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(bcol + j * COLS);
+        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(bcol + (j + 1) * COLS);
+        uint32_t w2 = 0u, w3 = 0u;
+        if (R >= 16) {
+          w2 = *reinterpret_cast<const uint32_t*>(bcol + (j + 8) * COLS);
+          w3 = *reinterpret_cast<const uint32_t*>(bcol + (j + 9) * COLS);
+        }
+        const uint32_t a0 = prmt(w0, w1, 0x5410u), a1 = prmt(w0, w1, 0x7632u);
+        const uint32_t a2 = prmt(w2, w3, 0x5410u), a3 = prmt(w2, w3, 0x7632u);
 #pragma unroll
-              for (int j = j0; j < j0 + 8; ++j) {
-                const float h = hs[m * R + j];
-                const uint2 b = *reinterpret_cast<const uint2*>(Bs + j * COLS + lcol);
-                const float2 b01 = h2_to_f2(b.x), b23 = h2_to_f2(b.y);
-                l0 = fmaf(h, b01.x, l0);
-                l1 = fmaf(h, b01.y, l1);
-                l2 = fmaf(h, b23.x, l2);
-                l3 = fmaf(h, b23.y, l3);
-              }
-            }
-            acc[0][nt][rr] = fmaf(p.lora_scale, l0, acc[0][nt][rr]);
-            acc[0][nt][2 + rr] = fmaf(p.lora_scale, l1, acc[0][nt][2 + rr]);
-            acc[1][nt][rr] = fmaf(p.lora_scale, l2, acc[1][nt][rr]);
-            acc[1][nt][2 + rr] = fmaf(p.lora_scale, l3, acc[1][nt][2 + rr]);
-          }
+        for (int nt = 0; nt < NT; ++nt) {
+          mma_16816(acc[pp][nt], a0, a1, a2, a3, bh[nt][0], bh[nt][1]);
+          mma_16816(acc[pp][nt], a0, a1, a2, a3, bl[nt][0], bl[nt][1]);
         }
       }
     }
   }
 
-  // 6. send the partial of the columns owned by CTA j into j's receive area
-  //    [S][M][CPR] (rows nt*8 + 2c (+1), columns lcol + 2pp (+1)).
+  // send the partial of the columns owned by CTA j into j's receive area
+  // [S][M][CPR] (rows nt*8 + 2c (+1), columns lcol + 2pp (+1))
   asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
   if (col_ok) {
 #pragma unroll
@@ -642,10 +645,11 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     }
   }
 
-  // 7. this CTA's columns: wait for the S partials, sum in rank order, round
+  // this CTA's columns: wait for the S partials, sum in rank order, round
   if (own_cols > 0) {
     mbar_wait(bar_rv, 0);
-    for (int it = tid; it < M * own_cols; it += THREADS) {
+    const int cb = n_tile0 + s * CPR;
+    for (int it = tid; it < M * own_cols; it += WARPS * 32) {
       const int m = it / own_cols, cc = it - m * own_cols;
       float v = 0.f;
       for (int r2 = 0; r2 < S; ++r2) v += recv[(size_t(r2) * M + m) * CPR + cc];
@@ -664,13 +668,15 @@ static int prepare(int dev) {
   QX_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_LIMIT)),
               "w4a16_gemv: set smem limit");
   QX_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
-              "w4a16_gemv: allow 16-CTA clusters");
+              "w4a16_gemv: allow clusters of up to 16 CTAs");
   if (dev >= 0 && dev < 64) done[dev] = true;
   return QX_OK;
 }
 
-// Among the cluster sizes whose shared memory fits, pick the one that needs
-// the fewest waves of co-resident clusters (occupancy API), larger S on ties.
+// Among the cluster sizes whose shared memory fits and whose grid runs in one
+// wave of co-resident clusters (occupancy API), pick the one with the fewest
+// quantisation groups per CTA, then the smallest; if none fits in one wave,
+// the fewest waves.
 template <int NT, int KPG>
 static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed, Plan* out) {
   static std::mutex mu;
@@ -690,8 +696,8 @@ static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed,
   if (rc != QX_OK) return rc;
   const int tiles = (N + COLS - 1) / COLS, T = K / KSTEP, Gt = K / group;
   Plan best{};
-  long best_waves = -1;
-  for (int S = 1; S <= MAX_S && S <= Gt; S *= 2) {
+  long best_key = -1;
+  for (int S = 1; S <= MAX_S && S <= Gt; ++S) {
     Plan pl{};
     pl.NT = NT;
     pl.tiles = tiles;
@@ -699,9 +705,10 @@ static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed,
     pl.S = S;
     const int gmax = (Gt + S - 1) / S;
     if (gmax > 256) continue;  // one tensor-map box covers a CTA's scale rows
+    if (S > 1 && (Gt + S - 2) / (S - 1) == gmax) continue;  // a smaller cluster is as short
     pl.Ts_max = gmax * KPG;
     pl.nst = std::min(gmax, MAX_NST);
-    pl.smem = layout(M, NT, KPG, pl.Ts_max, rank, S, pl.nst, zeros_packed).total;
+    pl.smem = layout(M, KPG, pl.Ts_max, rank, S, pl.nst, zeros_packed).total;
     if (pl.smem > SMEM_LIMIT) continue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(tiles, S, 1);
@@ -721,12 +728,15 @@ static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed,
       continue;
     }
     const long waves = (long(tiles) + clusters - 1) / clusters;
-    if (best_waves < 0 || waves <= best_waves) {
+    // order: waves first, then groups per CTA (S grows, so later S wins ties
+    // on waves only when it shortens the CTA)
+    const long key2 = waves * 1000000L + long(gmax) * 1000L;
+    if (best_key < 0 || key2 < best_key) {
       best = pl;
-      best_waves = waves;
+      best_key = key2;
     }
   }
-  if (best_waves < 0)
+  if (best_key < 0)
     return fail(QX_ERR_UNSUPPORTED, "w4a16_gemv: no cluster size fits K=%d N=%d rank=%d", K, N, rank);
   {
     std::lock_guard<std::mutex> lk(mu);
@@ -775,6 +785,7 @@ static int run(Params prm, cudaStream_t st) {
   if (rc != QX_OK) return rc;
   prm.T = pl.T;
   prm.S = pl.S;
+  prm.cpr = owner_cols(pl.S);
   prm.Ts_max = pl.Ts_max;
   prm.gmax = pl.Ts_max / KPG;
   prm.nst = pl.nst;
@@ -787,7 +798,11 @@ static int run(Params prm, cudaStream_t st) {
   rc = encode_2d(&prm.ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, prm.scales, uint64_t(prm.N), Gt,
                  uint64_t(prm.N) * 2, COLS, uint32_t(prm.gmax), "scales");
   if (rc != QX_OK) return rc;
-  if (!prm.zeros_packed)
+  prm.zeros_tma = !prm.zeros_packed || (prm.N % 32 == 0 && aligned(prm.zeros, 16));
+  if (prm.zeros_packed && prm.zeros_tma)
+    rc = encode_2d(&prm.tz, CU_TENSOR_MAP_DATA_TYPE_INT32, prm.zeros, uint64_t(prm.N) / 8, Gt,
+                   uint64_t(prm.N) / 2, COLS / 8, uint32_t(prm.gmax), "qzeros");
+  else if (!prm.zeros_packed)
     rc = encode_2d(&prm.tz, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, prm.zeros, uint64_t(prm.N), Gt,
                    uint64_t(prm.N) * 2, COLS, uint32_t(prm.gmax), "zeros");
   if (rc != QX_OK) return rc;
