@@ -84,6 +84,11 @@ constexpr size_t SMEM_LIMIT = 227 * 1024;
 
 __host__ __device__ constexpr int ctas_per_sm(int nt) { return nt == 1 ? 3 : (nt == 2 ? 2 : 1); }
 
+// Shared-memory carve-up (byte offsets), identical on host and device.
+struct Layout {
+  unsigned bars, ring, sz_s, sz_z, sf, xraw, xs, xks, As, Bs, hs, recv, total;
+};
+
 struct alignas(64) Params {
   CUtensorMap tw;  // qweight as u64 [K/8][N/2], box {132, KPG*4}
   CUtensorMap tb;  // LoRA B fp16 [r][N], box {256, r}
@@ -100,12 +105,10 @@ struct alignas(64) Params {
   int zeros_tma;  // zero points by TMA (fp16 always; packed when rows are 16 B multiples)
   float lora_scale;
   int T, S, cpr, Ts_max, gmax, nst, pdl;
+  uint32_t s_magic, cpr_magic;  // ceil(2^32 / S) (S > 1), ceil(2^32 / cpr): exact floor division of small values
+  Layout lay;                   // shared-memory carve-up, computed on the host
 };
 
-// Shared-memory carve-up (byte offsets), identical on host and device.
-struct Layout {
-  unsigned bars, ring, sz_s, sz_z, xraw, xs, xks, As, Bs, hs, recv, total;
-};
 
 __host__ __device__ inline unsigned take(unsigned& o, size_t bytes) {
   const unsigned r = o;
@@ -127,10 +130,11 @@ __host__ __device__ inline Layout layout(int M, int KPG, int Ts_max, int rank, i
   const size_t Mp = M <= 8 ? 8 : (M <= 16 ? 16 : 32);  // NT * 8 of the kernel instance
   Layout L;
   unsigned o = 0;
-  L.bars = take(o, size_t(5 + 2 * nst) * 8);  // statics, x, B, h, recv, full[nst], empty[nst]
+  L.bars = take(o, size_t(4 + 2 * nst) * 8);  // statics, B, h, recv, full[nst], empty[nst]
   L.ring = take(o, size_t(nst) * KPG * 4 * ROWB);     // weight stages
   L.sz_s = take(o, size_t(gmax) * COLS * 2);          // scales [gmax][256]
   L.sz_z = take(o, size_t(gmax) * (zeros_packed ? COLS / 2 : COLS * 2));  // [gmax][32] u32 or [gmax][256] fp16
+  L.sf = take(o, size_t(gmax) * COLS * 8);            // (s, s*z) as floats [gmax][256]
   L.xraw = take(o, size_t(M) * xstride(Ts_max) * 2);  // activations [M][Ks(+8)]
   L.xs = take(o, size_t(Ts_max) * Mp * 4 * 16);       // in MMA-B order [t][Mp][c], rows >= M zero
   L.xks = take(o, size_t(gmax) * Mp * 2 * 4);         // per group (Off, Sx) per row [g][Mp]
@@ -274,7 +278,9 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   const int s = blockIdx.y;  // == rank in the (1, S, 1) cluster
   const int S = p.S;
   const int Gt = p.T / KPG;  // quantisation groups along K
-  const int gr0 = s * Gt / S, gr1 = (s + 1) * Gt / S;
+  // floor(s * Gt / S) and floor((s + 1) * Gt / S) (S == 1: one CTA takes all)
+  const int gr0 = S == 1 ? 0 : int(__umulhi(uint32_t(s * Gt), p.s_magic));
+  const int gr1 = S == 1 ? Gt : int(__umulhi(uint32_t((s + 1) * Gt), p.s_magic));
   const int ngrp = gr1 - gr0;
   const int ks0 = gr0 * KPG;
   const int Ks = ngrp * KPG * KSTEP;
@@ -289,15 +295,14 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   const int CPR = p.cpr;  // columns each CTA of the cluster finalises
   const int own_cols = max(0, min(min(CPR, COLS - s * CPR), N - (n_tile0 + s * CPR)));
 
-  const Layout L = layout(M, KPG, p.Ts_max, R, S, nst, p.zeros_packed);
-  const __half* xraw = reinterpret_cast<const __half*>(smem + L.xraw);
+  const Layout& L = p.lay;
+  __half* xraw = reinterpret_cast<__half*>(smem + L.xraw);
   const float* recv = reinterpret_cast<const float*>(smem + L.recv);
   const uint32_t bar_st = smem_addr(smem + L.bars);  // scales, zeros, LoRA A
-  const uint32_t bar_x = bar_st + 8;                 // activations
-  const uint32_t bar_b = bar_st + 16;                // LoRA B
-  const uint32_t bar_h = bar_st + 24;                // h_s computed
-  const uint32_t bar_rv = bar_st + 32;               // partials from the cluster
-  const uint32_t full0 = bar_st + 40;                // full[i]  = full0 + 8 i
+  const uint32_t bar_b = bar_st + 8;                 // LoRA B
+  const uint32_t bar_h = bar_st + 16;                // h_s computed
+  const uint32_t bar_rv = bar_st + 24;               // partials from the cluster
+  const uint32_t full0 = bar_st + 32;                // full[i]  = full0 + 8 i
   const uint32_t empty0 = full0 + 8 * nst;           // empty[i] = empty0 + 8 i
   const int wx = n_tile0 / 2;  // tile origin in 64-bit elements (x * 8 B = tile * 1 KB)
   const uint32_t ring_s = smem_addr(smem + L.ring);
@@ -309,7 +314,6 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   if (warp == WARPS && lane == 0) {
     prefetch_tmap(&p.tw);
     mbar_init(bar_st, p.zeros_tma ? 1 : 33);  // + one arrival per helper lane (plain-loaded zeros)
-    mbar_init(bar_x, 1);
     mbar_init(bar_b, 1);
     mbar_init(bar_h, 32);
     mbar_init(bar_rv, 1);
@@ -324,18 +328,6 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   // Peers send partial sums only after every CTA of the cluster has
   // initialised its receive barrier (arrive now, wait before sending).
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-
-  const uint32_t xrow_bytes = uint32_t(Ks) * 2;
-  if (warp == 0) {  // the activations first: they gate the LoRA-down and every MMA
-    if (lane == 0) mbar_expect_tx(bar_x, uint32_t(M) * xrow_bytes);
-    if (p.pdl) {  // activations may come from the previous kernel in the stream
-      if (lane == 0) grid_dep_wait();
-    }
-    __syncwarp();
-    for (int m = lane; m < M; m += 32)
-      bulk_g2s(smem_addr(smem + L.xraw) + uint32_t(m * XS) * 2, p.x + size_t(m) * p.K + k0,
-               xrow_bytes, bar_x);
-  }
 
   if (warp == WARPS) {
     // ---------------- helper warp ----------------
@@ -376,28 +368,31 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     }
   }
 
-  // activations in MMA-B order (x0,x4 | x1,x5 | x2,x6 | x3,x7) per packed row,
+  // activations (plain 128-bit loads) in MMA-B order (x0,x4 | x1,x5 | x2,x6 | x3,x7) per packed row,
   // rows M..Mp-1 zero, and per group the sums over the two nibble classes:
-  // (Off, Sx) = (1024 Xa + 64 Xb, Xa + Xb), by the whole CTA.  Items
-  // (m, t, c), c fastest: a group of row m is an aligned block of 4*KPG
-  // lanes; the item count is padded to whole warps for the shuffles.
+  // (Off, Sx) = (1024 Xa + 64 Xb, Xa + Xb), by the whole CTA.  A group of a
+  // row is an aligned block of 4*KPG lanes (whole warps join the shuffles).
   {
     const int Ts = ngrp * KPG;
     uint4* xsw = reinterpret_cast<uint4*>(smem + L.xs);
     float* xksw = reinterpret_cast<float*>(smem + L.xks);
-    for (int it = tid; it < Ts * (Mp - M) * 4; it += THREADS) {
-      const int t = it / ((Mp - M) * 4), r = it - t * ((Mp - M) * 4);
-      xsw[(t * Mp + M) * 4 + r] = make_uint4(0u, 0u, 0u, 0u);
+    // work in chunks of 32 items (8 k-steps, whole groups) of one row, spread over the warps
+    const int TB = (Ts + 7) >> 3;  // chunks per row
+    for (int id = warp; id < (Mp - M) * TB; id += WARPS + 1) {  // zero rows
+      const int mz = id / TB, it = (id - mz * TB) * 32 + lane;
+      if (it < Ts * 4) xsw[((it >> 2) * Mp + M + mz) * 4 + (it & 3)] = make_uint4(0u, 0u, 0u, 0u);
     }
-    mbar_wait(bar_x, 0);
-    const int tot = M * Ts * 4, totp = (tot + 31) & ~31;
-    for (int it = tid; it < totp; it += THREADS) {
-      const bool ok = it < tot;
-      const int mt = it >> 2, cc = it & 3;
-      const int m = ok ? mt / Ts : 0, t = ok ? mt - m * Ts : 0;
+    // the activations may come from the previous kernel in the stream: wait
+    // for it here, after every weight and static copy has been started
+    if (p.pdl) grid_dep_wait();
+    const __half* xg = p.x + k0;
+    for (int id = warp; id < M * TB; id += WARPS + 1) {
+      const int m = id / TB, it = (id - m * TB) * 32 + lane, t = it >> 2, cc = it & 3;
+      const bool ok = it < Ts * 4;  // Ts * 4 is a multiple of 4 * KPG: groups never straddle
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (ok) {
-        v = *reinterpret_cast<const uint4*>(xraw + m * XS + t * KSTEP + cc * 8);
+        v = *reinterpret_cast<const uint4*>(xg + size_t(m) * p.K + t * KSTEP + cc * 8);
+        *reinterpret_cast<uint4*>(xraw + m * XS + t * KSTEP + cc * 8) = v;  // natural order, LoRA-down
         xsw[(t * Mp + m) * 4 + cc] = make_uint4(prmt(v.x, v.z, 0x5410u), prmt(v.x, v.z, 0x7632u),
                                                 prmt(v.y, v.w, 0x5410u), prmt(v.y, v.w, 0x7632u));
       }
@@ -405,16 +400,33 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
       float xa = (a0.x + a1.x) + (a2.x + a3.x);  // x0 + x2 + x4 + x6
       float xb = (a0.y + a1.y) + (a2.y + a3.y);  // x1 + x3 + x5 + x7
 #pragma unroll
-      for (int w = 1; w < 4 * KPG; w <<= 1) {
+      for (int w = 1; w < 4 * KPG; w <<= 1) {  // the 4*KPG lanes of one group
         xa += __shfl_xor_sync(0xffffffffu, xa, w);
         xb += __shfl_xor_sync(0xffffffffu, xb, w);
       }
-      if (ok && cc == 0 && t % KPG == 0)
+      if (ok && (it & (4 * KPG - 1)) == 0)
         *reinterpret_cast<float2*>(xksw + ((t / KPG) * Mp + m) * 2) =
             make_float2(fmaf(1024.f, xa, 64.f * xb), xa + xb);
     }
   }
-  __syncthreads();  // permuted activations and group sums ready
+  // scales and zero points of the CTA's groups as floats (s, s * z)
+  mbar_wait(bar_st, 0);
+  {
+    float2* sfw = reinterpret_cast<float2*>(smem + L.sf);
+    const __half* szs = reinterpret_cast<const __half*>(smem + L.sz_s);
+    for (int it = tid; it < ngrp * COLS; it += THREADS) {
+      const int gi = it >> 8, col = it & (COLS - 1);
+      const float sc = __half2float(szs[it]);
+      float z;
+      if (p.zeros_packed)
+        z = float(((reinterpret_cast<const uint32_t*>(smem + L.sz_z)[gi * (COLS / 8) + (col >> 3)] >>
+                    (4 * (col & 7))) & 0xFu) + unsigned(p.zero_offset));
+      else
+        z = __half2float(reinterpret_cast<const __half*>(smem + L.sz_z)[it]);
+      sfw[it] = make_float2(sc, sc * z);
+    }
+  }
+  __syncthreads();  // permuted activations, group sums, scales ready
 
   if (warp == WARPS) {  // helper: the LoRA down-projection
     if (R == 0) return;
@@ -467,8 +479,6 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   // ---------------- compute warps ----------------
   const int lcol = warp * 32 + 4 * g;  // first of this lane's 4 columns (tile-local)
   const bool col_ok = n_tile0 + lcol < N;  // N % 8 == 0: all 4 columns valid or none
-  const unsigned char* sz_s = smem + L.sz_s;
-  const unsigned char* sz_z = smem + L.sz_z;
   const uint4* xs = reinterpret_cast<const uint4*>(smem + L.xs);
   const float* xks = reinterpret_cast<const float*>(smem + L.xks);
 
@@ -481,7 +491,6 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[pp][nt][i] = 0.f;
 
-  mbar_wait(bar_st, 0);
   int st = 0, use = 0;  // ring stage and wrap count
   const unsigned char* wlane = smem + L.ring + c * ROWB + lcol * 4;
   for (int gi = 0; gi < ngrp; ++gi) {
@@ -530,25 +539,10 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
       __syncwarp();
     }
     {  // group correction: acc += s (C - Off) - (s z) Sx
-      const uint2 sc = *reinterpret_cast<const uint2*>(sz_s + (gi * COLS + lcol) * 2);
-      const float2 s01 = h2_to_f2(sc.x), s23 = h2_to_f2(sc.y);
-      const float sv[4] = {s01.x, s01.y, s23.x, s23.y};
-      float zv[4];
-      if (p.zeros_packed) {
-        const uint32_t zw =
-            *reinterpret_cast<const uint32_t*>(sz_z + (gi * (COLS / 8) + (lcol >> 3)) * 4);
-        const int sh = (lcol & 7) * 4;
-#pragma unroll
-        for (int jz = 0; jz < 4; ++jz)
-          zv[jz] = float(((zw >> (sh + 4 * jz)) & 0xFu) + unsigned(p.zero_offset));
-      } else {
-        const uint2 zh = *reinterpret_cast<const uint2*>(sz_z + (gi * COLS + lcol) * 2);
-        const float2 z01 = h2_to_f2(zh.x), z23 = h2_to_f2(zh.y);
-        zv[0] = z01.x;
-        zv[1] = z01.y;
-        zv[2] = z23.x;
-        zv[3] = z23.y;
-      }
+      const float2* sf = reinterpret_cast<const float2*>(smem + L.sf) + gi * COLS + lcol;
+      const float4 c01 = *reinterpret_cast<const float4*>(sf);      // (s, sz) of cols 0, 1
+      const float4 c23 = *reinterpret_cast<const float4*>(sf + 2);  // cols 2, 3
+      const float sv[4] = {c01.x, c01.z, c23.x, c23.z}, zv[4] = {c01.y, c01.w, c23.y, c23.w};
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         // (Off, Sx) of rows nt*8 + 2c, + 1 (rows >= M hold stale values that
@@ -558,7 +552,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
 #pragma unroll
         for (int pp = 0; pp < 2; ++pp) {
           const float s0 = sv[2 * pp], s1 = sv[2 * pp + 1];
-          const float z0 = s0 * zv[2 * pp], z1 = s1 * zv[2 * pp + 1];
+          const float z0 = zv[2 * pp], z1 = zv[2 * pp + 1];
           acc[pp][nt][0] = fmaf(-z0, sx0, fmaf(s0, cgr[pp][nt][0] - off0, acc[pp][nt][0]));
           acc[pp][nt][1] = fmaf(-z0, sx1, fmaf(s0, cgr[pp][nt][1] - off1, acc[pp][nt][1]));
           acc[pp][nt][2] = fmaf(-z1, sx0, fmaf(s1, cgr[pp][nt][2] - off0, acc[pp][nt][2]));
@@ -632,7 +626,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
 #pragma unroll
     for (int pp = 0; pp < 2; ++pp) {
       const int cl = lcol + 2 * pp;
-      const int owner = cl / CPR, cc = cl - owner * CPR;
+      const int owner = __umulhi(uint32_t(cl), p.cpr_magic), cc = cl - owner * CPR;
       const uint32_t rbase = map_rank(smem_addr(recv + size_t(s) * M * CPR + cc), owner);
       const uint32_t rbar = map_rank(bar_rv, owner);
 #pragma unroll
@@ -649,11 +643,26 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   if (own_cols > 0) {
     mbar_wait(bar_rv, 0);
     const int cb = n_tile0 + s * CPR;
-    for (int it = tid; it < M * own_cols; it += WARPS * 32) {
-      const int m = it / own_cols, cc = it - m * own_cols;
-      float v = 0.f;
-      for (int r2 = 0; r2 < S; ++r2) v += recv[(size_t(r2) * M + m) * CPR + cc];
-      p.y[size_t(m) * N + cb + cc] = __float2half_rn(v);
+    if (M == 1) {
+      for (int cc = tid; cc < own_cols; cc += WARPS * 32) {
+        float v = 0.f;
+        for (int r2 = 0; r2 < S; ++r2) v += recv[r2 * CPR + cc];
+        p.y[cb + cc] = __float2half_rn(v);
+      }
+      return;
+    }
+    // the compute threads as (row, column) pairs: rpi rows per pass
+    const int rpi = own_cols >= WARPS * 32 ? 1 : (WARPS * 32) / own_cols;
+    const int mi = tid / own_cols, c0 = tid - mi * own_cols;
+    for (int m0 = 0; m0 < M; m0 += rpi) {
+      const int m = m0 + mi;
+      if (mi < rpi && m < M) {
+        for (int cc = c0; cc < own_cols; cc += WARPS * 32) {
+          float v = 0.f;
+          for (int r2 = 0; r2 < S; ++r2) v += recv[(size_t(r2) * M + m) * CPR + cc];
+          p.y[size_t(m) * N + cb + cc] = __float2half_rn(v);
+        }
+      }
     }
   }
 }
@@ -785,6 +794,9 @@ static int run(Params prm, cudaStream_t st) {
   if (rc != QX_OK) return rc;
   prm.T = pl.T;
   prm.S = pl.S;
+  prm.s_magic = pl.S > 1 ? uint32_t((0x100000000ull + pl.S - 1) / pl.S) : 0u;
+  prm.cpr_magic = uint32_t((0x100000000ull + owner_cols(pl.S) - 1) / owner_cols(pl.S));
+  prm.lay = layout(prm.M, KPG, pl.Ts_max, prm.rank, pl.S, pl.nst, prm.zeros_packed);
   prm.cpr = owner_cols(pl.S);
   prm.Ts_max = pl.Ts_max;
   prm.gmax = pl.Ts_max / KPG;
