@@ -89,6 +89,26 @@ int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const void* scales
 int qx_set_pdl(int enable);
 
 /* ------------------------------------------------------------------------
+ * W4A16-LoRA GEMM on the tcgen05 tensor cores (prefill, large M).
+ * Same math and operand formats as qx_w4a16_lora_gemv (the reference runs
+ * every M through w4a16_lora_gemv(), csrc/kernels/w4a16_lora_gemv.cu:268-323);
+ * new component: the reference has no tensor-core path.  Launches the LoRA
+ * down-projection (h = x . A, fp32, into the workspace) and the GEMM
+ * (128 x 256 output tiles, TMA-fed, int4 dequantised in shared memory,
+ * accumulator in TMEM, LoRA term added on the tensor cores).
+ * Constraints: N % 256 == 0, K % 64 == 0, group_size in {32, 64, 128, 256},
+ * rank in {0, 8, 16, 32, 64}; every tensor and the workspace 16-byte aligned.
+ * workspace: qx_w4a16_lora_gemm_sm100_workspace_size(M, rank) bytes (fp32 h);
+ * its contents need no initialisation.
+ * ---------------------------------------------------------------------- */
+size_t qx_w4a16_lora_gemm_sm100_workspace_size(int M, int rank);
+int qx_w4a16_lora_gemm_sm100(const void* x, const int32_t* qweight, const void* scales,
+                             const void* zeros, int zeros_packed, int zero_offset,
+                             const void* lora_A, const void* lora_B, void* y, int M, int K, int N,
+                             int rank, int group_size, float lora_scale, void* workspace,
+                             size_t workspace_bytes, qx_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Fused RMSNorm.  Replaces fused_rmsnorm() (csrc/kernels/rmsnorm.cu:162-210,
  * bound at csrc/binding.cpp:36-38).
  *   y[r, :] = fp16( (x[r, :] * rsqrt(mean(x[r, :]^2) + eps)) * w )

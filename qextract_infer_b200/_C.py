@@ -104,6 +104,10 @@ def _prepare_lora(lora_A, lora_B):
     return A, B, rp
 
 
+# rows from which w4a16(_lora)_gemv runs on the tensor-core GEMM instead of the decode GEMV
+GEMM_MIN_ROWS = 128
+
+
 def _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale, zero_offset):
     for t, n in ((input, "input"), (qweight, "qweight"), (scales, "scales"), (zeros, "zeros")):
         _check_input(t, n)
@@ -143,6 +147,17 @@ def _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale
     out = torch.empty(*lead, N, dtype=torch.float16, device=input.device)
     dev = input.device
     st = _stream(dev)
+    if M >= GEMM_MIN_ROWS and N % 256 == 0 and K % 64 == 0 and rank <= 64:
+        # prefill: the tcgen05 tensor-core GEMM
+        with torch.cuda.device(dev):
+            need = _LIB.qx_w4a16_lora_gemm_sm100_workspace_size(M, rank)
+            ws = _workspace.get(dev, st, need, "w4a16_gemm") if need else None
+            _lib.check(_LIB.qx_w4a16_lora_gemm_sm100(
+                input.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), packed,
+                int(zero_offset), _ptr(lora_A), _ptr(lora_B), out.data_ptr(), M, K, N, rank,
+                int(group_size), float(lora_scale), _ptr(ws), int(need), st.cuda_stream),
+                "w4a16_gemm")
+        return out
     with torch.cuda.device(dev):
         _lib.check(_LIB.qx_w4a16_lora_gemv(
             input.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), packed,

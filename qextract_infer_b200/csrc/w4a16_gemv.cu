@@ -867,6 +867,10 @@ static int dispatch(const Params& prm, int kpg, cudaStream_t st) {
 
 using namespace qx;
 
+namespace qx {
+int gemm_device_error(unsigned* code, int reset);  // w4a16_gemm.cu
+}
+
 extern "C" int qx_get_device_error(unsigned* code, int reset) {
   QX_REQUIRE(code, "get_device_error: null output");
   QX_CUDA_TRY(cudaMemcpyFromSymbol(code, g_device_error, sizeof(unsigned)),
@@ -876,6 +880,10 @@ extern "C" int qx_get_device_error(unsigned* code, int reset) {
     QX_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(unsigned)),
                 "get_device_error: reset");
   }
+  unsigned other = 0;
+  const int rc = qx::gemm_device_error(&other, reset);
+  if (rc != QX_OK) return rc;
+  *code |= other;
   return QX_OK;
 }
 
