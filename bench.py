@@ -439,6 +439,58 @@ def run_kernel_suite(args):
     return 0
 
 
+QWEN3_8B_PREFILL = [("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 4096),
+                    ("gate", 4096, 12288), ("up", 4096, 12288), ("down", 12288, 4096)]
+
+
+def measured_tflops():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    return 1590.0, 1400.0, "fallback"
+
+
+def run_prefill_suite(args):
+    """Prefill W4A16-LoRA GEMM at M=4096 over the 7 Qwen3-8B projection shapes
+    (GPTQ int4 g128, packed qzeros, LoRA r=64, alpha/r=2): one JSON line per
+    shape (tcgen05 path through the public API, us, TFLOP/s, fraction of the
+    measured dense fp16/bf16 peak) and one line for the whole set."""
+    import torch
+    from qextract_infer_b200 import _C
+    dev = torch.device("cuda", torch.cuda.current_device())
+    st = torch.cuda.Stream(dev)
+    peak, peak_sus, kind = measured_tflops()
+    Mr, R, G = 4096, 64, 128
+    gen = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn(Mr, 12288, generator=gen, device=dev).half()
+    total_flop, total_us = 0.0, 0.0
+    for name, K, N in QWEN3_8B_PREFILL:
+        qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), generator=gen, device=dev, dtype=torch.int32)
+        sc = (torch.rand(K // G, N, generator=gen, device=dev) * 0.015 + 0.005).half()
+        qz = torch.full((K // G, N // 8), 0x88888888 - 2 ** 32, dtype=torch.int32, device=dev)
+        A = (torch.randn(K, R, generator=gen, device=dev) * 0.02).half()
+        B = (torch.randn(R, N, generator=gen, device=dev) * 0.02).half()
+        xk = x[:, :K].contiguous()
+        steps = max(5, min(args.steps, 50))
+        us = _graph_time_us(torch, st, lambda i: _C.w4a16_lora_gemv(xk, qw, sc, qz, A, B, G, 2.0 * R), steps)
+        flop = 2.0 * Mr * K * N + 2.0 * Mr * R * (K + N)
+        tf = flop / us / 1e6
+        total_flop += flop
+        total_us += us
+        print(json.dumps({"metric": "prefill W4A16-LoRA GEMM TFLOP/s", "shape": name, "M": Mr, "K": K,
+                          "N": N, "rank": R, "us_per_call": us, "TFLOP/s": tf, "peak": peak,
+                          "tensor_frac": tf / peak, "peak_kind": kind,
+                          "kernels": ["lora_down_kernel", "w4a16_gemm_kernel"]}), flush=True)
+    tf = total_flop / total_us / 1e6
+    print(json.dumps({"metric": "prefill W4A16-LoRA GEMM TFLOP/s (7 Qwen3-8B shapes, M=4096)",
+                      "value": tf, "unit": "TFLOP/s", "us_total": total_us, "flop_total": total_flop,
+                      "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                                   "frac": tf / peak, "peak_kind": kind}}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -449,11 +501,15 @@ def main():
                     help="weight sets in the rotation (default: enough for > 2x L2)")
     ap.add_argument("--skip-e2e", action="store_true", help="omit the public-API timing")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline")
-    ap.add_argument("--workload", choices=["decode_gemv", "kernels"], default="decode_gemv",
-                    help="decode_gemv: the headline line; kernels: RMSNorm/SwiGLU/ring/attention lines")
+    ap.add_argument("--workload", choices=["decode_gemv", "kernels", "prefill_gemm"],
+                    default="decode_gemv",
+                    help="decode_gemv: the headline line; kernels: RMSNorm/SwiGLU/ring/attention lines; "
+                         "prefill_gemm: the tcgen05 GEMM over the Qwen3-8B shapes at M=4096")
     args = ap.parse_args()
     if args.workload == "kernels":
         return run_kernel_suite(args)
+    if args.workload == "prefill_gemm":
+        return run_prefill_suite(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)

@@ -98,7 +98,8 @@ int qx_set_pdl(int enable);
  * accumulator in TMEM, LoRA term added on the tensor cores).
  * Constraints: N % 256 == 0, K % 64 == 0, group_size in {32, 64, 128, 256},
  * rank in {0, 8, 16, 32, 64}; every tensor and the workspace 16-byte aligned.
- * workspace: qx_w4a16_lora_gemm_sm100_workspace_size(M, rank) bytes (fp32 h);
+ * workspace: qx_w4a16_lora_gemm_sm100_workspace_size(M, rank) bytes (the scaled
+ * LoRA down-projection as fp16 high and low parts);
  * its contents need no initialisation.
  * ---------------------------------------------------------------------- */
 size_t qx_w4a16_lora_gemm_sm100_workspace_size(int M, int rank);

@@ -6,7 +6,9 @@
 // with W = s (q - z) per quantisation group, fp32 accumulation.
 //
 // Two launches:
-//   lora_down_kernel   h[M, r] = x . A  (fp32, mma.sync; r <= 64, ~1.6 % of the FLOPs)
+//   lora_down_kernel   (alpha/r) h = (alpha/r) x . A in fp32 (mma.sync; r <= 64,
+//                      ~1.6 % of the FLOPs), stored as fp16 high and low parts
+//                      [M][64] (zero-padded ranks) for the GEMM's TMA
 //   w4a16_gemm_kernel  one CTA per 128 x 256 output tile:
 //     warp 0      TMA producer: x tile [128 x 64] (128B swizzle, K-major), the
 //                 int4 weight tile [8 packed rows x 256 columns], scales and
@@ -23,9 +25,10 @@
 //                 fp16(s (q - z)), as the reference dequantises
 //                 (tests/test_w4a16_gemv.py:68-90); then the epilogue
 //                 (tcgen05.ld 32x32b, fp32 -> fp16, 16-byte stores)
-//   The LoRA term enters the same accumulator first: A = (alpha/r) h split
-//   into fp16 high and low parts (two MMAs, ~22-bit product), B = B^T of the
-//   tile, both staged by warps 2-9 before the weight stream.
+//   The LoRA term enters the same accumulator first: A = the high and low
+//   parts of (alpha/r) h (two MMAs, ~22-bit product) and the LoRA B tile, both
+//   by TMA before the weight stream; warps 2-9 transpose the B tile into the
+//   K-major swizzled layout in shared memory.
 // Every wait is bounded (~200 ms, then QX_DEVERR_MBAR_TIMEOUT in the device
 // error word); no TMA multicast.
 #include <cuda.h>
@@ -56,7 +59,7 @@ constexpr int OFF_LH = OFF_BF + STAGES * BF_BYTES;  // LoRA h (hi | lo), 2 x 16 
 constexpr int OFF_WQ = OFF_LH + 2 * A_BYTES;
 constexpr int OFF_SZ = OFF_WQ + STAGES * WQ_BYTES;
 constexpr int OFF_BAR = OFF_SZ + STAGES * SZ_BYTES;
-constexpr int NBARS = 4 * STAGES + 2;  // full_a, empty_a, full_b, empty_b, tmem_full, spare
+constexpr int NBARS = 4 * STAGES + 2;  // full_a, empty_a, full_b, empty_b, tmem_full, lora
 constexpr int OFF_TMEM = OFF_BAR + NBARS * 8;
 constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;  // + alignment slack
 
@@ -65,11 +68,10 @@ struct alignas(64) GemmParams {
   CUtensorMap tw;  // qweight u64 [K/8][N/2], box {128, 8}
   CUtensorMap ts;  // scales fp16 [K/g][N], box {256, grows}
   CUtensorMap tz;  // zeros: packed u32 [K/g][N/8] box {32, grows}, or fp16 [K/g][N] box {256, grows}
-  const float* h;  // (x . A) fp32 [M][r]
-  const __half* B; // LoRA B fp16 [r][N]
+  CUtensorMap th;  // (alpha/r) h, fp16 high then low parts, [2M][64], box {64, 128}, 128B swizzle
+  CUtensorMap tb;  // LoRA B fp16 [r][N], box {256, kp}
   __half* y;
   int M, K, N, rank, group, zeros_packed, zero_offset, grows;
-  float lora_scale;
 };
 
 // Sticky device-side error word of this file's kernels (QX_DEVERR_* bits),
@@ -93,10 +95,10 @@ __device__ __forceinline__ void bar_expect(uint32_t b, uint32_t bytes) {
 __device__ __forceinline__ bool bar_try(uint32_t b, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{ .reg .pred P; mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 P, [%1], %2, %3; "
+      "{ .reg .pred P; mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 P, [%1], %2; "
       "selp.u32 %0, 1, 0, P; }"
       : "=r"(ok)
-      : "r"(b), "r"(parity), "r"(1000000u)
+      : "r"(b), "r"(parity)
       : "memory");
   return ok != 0;
 }
@@ -140,11 +142,12 @@ __device__ __forceinline__ uint64_t kmajor_sw128_desc(uint32_t saddr) {
 // kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N=256, M=128
 constexpr uint32_t IDESC = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
 
-__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t acc) {
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t acc,
+                                     uint32_t idesc = IDESC) {  // one thread issues
   asm volatile(
       "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(IDESC), "r"(acc)
+      "l"(da), "l"(db), "r"(idesc), "r"(acc)
       : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint32_t b) {
@@ -177,6 +180,8 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
   const uint32_t full_a = sb + OFF_BAR, empty_a = full_a + 8 * STAGES;
   const uint32_t full_b = empty_a + 8 * STAGES, empty_b = full_b + 8 * STAGES;
   const uint32_t tmem_full = empty_b + 8 * STAGES;
+  const uint32_t lora_full = tmem_full + 8;
+  const int kp = ((R + 15) / 16) * 16;  // LoRA K extent of the MMAs
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
 
   if (warp == 0 && lane == 0) {
@@ -187,6 +192,7 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
       bar_init(empty_b + 8 * i, 1);
     }
     bar_init(tmem_full, 1);
+    bar_init(lora_full, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\nfence.proxy.async.shared::cta;" ::: "memory");
   }
   if (warp == 1) {  // 256 TMEM columns: the 128 x 256 fp32 accumulator
@@ -206,6 +212,12 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
+      if (lora_items) {  // (alpha/r) h hi / lo tiles; the LoRA B tile [kp][256] (raw) into ring slot 1
+        bar_expect(lora_full, uint32_t(2 * A_BYTES + kp * BN * 2));
+        tma2d(sb + OFF_LH, &p.th, 0, m0, lora_full);
+        tma2d(sb + OFF_LH + A_BYTES, &p.th, 0, p.M + m0, lora_full);
+        tma2d(sb + OFF_BF + BF_BYTES, &p.tb, n0, 0, lora_full);
+      }
       for (int kb = 0; kb < KB; ++kb) {
         const int s = kb % STAGES;
         if (kb >= STAGES) bar_wait(empty_a + 8 * s, ((kb / STAGES) - 1) & 1);
@@ -222,11 +234,11 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       if (lora_items) {  // accumulator = (alpha/r) h B first (hi and lo parts)
-        bar_wait(full_b, 0);
+        bar_wait(lora_full, 0);
+        bar_wait(full_b, 0);  // the transposed B tile
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int ks = (R + 15) / 16;
         for (int part = 0; part < 2; ++part)
-          for (int k = 0; k < ks; ++k)
+          for (int k = 0; k < kp / 16; ++k)
             umma(tmem, kmajor_sw128_desc(sb + OFF_LH + part * A_BYTES + k * 32),
                  kmajor_sw128_desc(sb + OFF_BF + k * 32), (part | k) != 0);
         umma_commit(empty_b);
@@ -249,49 +261,22 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
   } else {
     // ------------------------------------------------------------ dequant warps
     const int dt = tid - 64;  // 0..255: the tile column this thread dequantises
-    const int n = n0 + dt;
-    if (lora_items) {
-      // B^T of the tile: row dt = column n, K = rank (zero-padded to a multiple of 16)
+    if (lora_items) {  // transpose the raw LoRA B tile (ring slot 1) into K-major ring slot 0
+      if (lane == 0) bar_wait(lora_full, 0);
+      __syncwarp();
+      bar_wait(lora_full, 0);
+      const __half* braw = reinterpret_cast<const __half*>(smem + OFF_BF + BF_BYTES);
       unsigned char* bf = smem + OFF_BF;
-      const int kp = ((R + 15) / 16) * 16;
       for (int ch = 0; ch < kp / 8; ++ch) {
         uint32_t w[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j = ch * 8 + 2 * e;
-          const __half lo = j < R ? p.B[size_t(j) * p.N + n] : __float2half(0.f);
-          const __half hi = j + 1 < R ? p.B[size_t(j + 1) * p.N + n] : __float2half(0.f);
-          w[e] = uint32_t(__half_as_ushort(lo)) | (uint32_t(__half_as_ushort(hi)) << 16);
-        }
-        *reinterpret_cast<uint4*>(bf + dt * 128 + ((ch ^ (dt & 7)) << 4)) =
-            make_uint4(w[0], w[1], w[2], w[3]);
-      }
-      // (alpha/r) h of the tile's rows, split into fp16 hi + lo: A operands [128 x kp]
-      const int row = dt >> 1, half = dt & 1;  // two threads per row
-      const int m = m0 + row;
-      unsigned char* lh = smem + OFF_LH;
-      for (int ch = half; ch < kp / 8; ch += 2) {
-        uint32_t hw[4], lw[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j = ch * 8 + 2 * e;
-          float v0 = 0.f, v1 = 0.f;
-          if (m < p.M) {
-            if (j < R) v0 = p.lora_scale * p.h[size_t(m) * R + j];
-            if (j + 1 < R) v1 = p.lora_scale * p.h[size_t(m) * R + j + 1];
-          }
-          const __half2 hh = __floats2half2_rn(v0, v1);
-          const float2 hr = __half22float2(hh);
-          const __half2 hl = __floats2half2_rn(v0 - hr.x, v1 - hr.y);
-          hw[e] = *reinterpret_cast<const uint32_t*>(&hh);
-          lw[e] = *reinterpret_cast<const uint32_t*>(&hl);
-        }
-        const int off = row * 128 + ((ch ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(lh + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4*>(lh + A_BYTES + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        for (int e = 0; e < 4; ++e)
+          w[e] = uint32_t(__half_as_ushort(braw[(ch * 8 + 2 * e) * BN + dt])) |
+                 (uint32_t(__half_as_ushort(braw[(ch * 8 + 2 * e + 1) * BN + dt])) << 16);
+        *reinterpret_cast<uint4*>(bf + dt * 128 + ((ch ^ (dt & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // every warp is done reading slot 1
       if (lane == 0) bar_arrive(full_b);
     }
     for (int kb = 0; kb < KB; ++kb) {
@@ -354,6 +339,8 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
       }
     }
     // ------------------------------------------------------------ epilogue
+    if (lane == 0) bar_wait(tmem_full, 0);
+    __syncwarp();
     bar_wait(tmem_full, 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const int q = warp & 3, chalf = (warp - 2) >> 2;  // TMEM lane quarter, column half
@@ -397,12 +384,15 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
   }
 }
 
-// h[M][r] = x[M][K] . A[K][r] in fp32: 64 rows per CTA (4 warps x 16 rows),
-// K in chunks of 64 staged in shared memory, mma.sync m16n8k16.
+// (alpha/r) h = (alpha/r) x[M][K] . A[K][r] in fp32: 64 rows per CTA (4 warps x
+// 16 rows), K in chunks of 64 staged in shared memory, mma.sync m16n8k16;
+// written as fp16 high parts hl[m][0..63] and low parts hl[M + m][0..63]
+// (ranks r..63 zero).
 constexpr int LD_ROWS = 64, LD_K = 64;
 __global__ void __launch_bounds__(128) lora_down_kernel(const __half* __restrict__ x,
                                                          const __half* __restrict__ A,
-                                                         float* __restrict__ h, int M, int K, int R) {
+                                                         __half* __restrict__ hl, int M, int K, int R,
+                                                         float scale) {
   __shared__ __align__(16) __half xs[LD_ROWS][LD_K + 8];
   __shared__ __align__(16) __half as[LD_K][MAX_RANK + 8];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -450,14 +440,19 @@ __global__ void __launch_bounds__(128) lora_down_kernel(const __half* __restrict
     }
     __syncthreads();
   }
+  auto put = [&](int row, int col, float v0, float v1) {
+    const __half2 hi = __floats2half2_rn(scale * v0, scale * v1);
+    const float2 hr = __half22float2(hi);
+    const __half2 lo = __floats2half2_rn(scale * v0 - hr.x, scale * v1 - hr.y);
+    *reinterpret_cast<__half2*>(hl + size_t(row) * MAX_RANK + col) = hi;
+    *reinterpret_cast<__half2*>(hl + (size_t(M) + row) * MAX_RANK + col) = lo;
+  };
 #pragma unroll
   for (int nt = 0; nt < MAX_RANK / 8; ++nt) {
-    if (nt < NT) {
-      const int row = r0 + warp * 16 + g, col = nt * 8 + 2 * c;
-      if (row < M) *reinterpret_cast<float2*>(h + size_t(row) * R + col) = make_float2(acc[nt][0], acc[nt][1]);
-      if (row + 8 < M)
-        *reinterpret_cast<float2*>(h + size_t(row + 8) * R + col) = make_float2(acc[nt][2], acc[nt][3]);
-    }
+    const bool v = nt < NT;
+    const int row = r0 + warp * 16 + g, col = nt * 8 + 2 * c;
+    if (row < M) put(row, col, v ? acc[nt][0] : 0.f, v ? acc[nt][1] : 0.f);
+    if (row + 8 < M) put(row + 8, col, v ? acc[nt][2] : 0.f, v ? acc[nt][3] : 0.f);
   }
 }
 
@@ -508,7 +503,8 @@ int gemm_device_error(unsigned* code, int reset) {
 using namespace qx;
 
 extern "C" size_t qx_w4a16_lora_gemm_sm100_workspace_size(int M, int rank) {
-  return rank > 0 ? (size_t(M) * size_t(rank) * 4 + 255) / 256 * 256 : 0;
+  // (alpha/r) h as fp16 high and low parts, [2M][64]
+  return rank > 0 ? size_t(2) * size_t(M) * gemm::MAX_RANK * 2 : 0;
 }
 
 extern "C" int qx_w4a16_lora_gemm_sm100(const void* x, const int32_t* qweight, const void* scales,
@@ -556,8 +552,16 @@ extern "C" int qx_w4a16_lora_gemm_sm100(const void* x, const int32_t* qweight, c
                   uint32_t(grows), CU_TENSOR_MAP_SWIZZLE_NONE, "zeros");
   }
   if (rc != QX_OK) return rc;
-  prm.h = static_cast<const float*>(workspace);
-  prm.B = static_cast<const __half*>(lora_B);
+  if (rank > 0) {
+    const int kp = ((rank + 15) / 16) * 16;
+    rc = encode(&prm.th, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, workspace, uint64_t(MAX_RANK),
+                uint64_t(2) * uint64_t(M), uint64_t(MAX_RANK) * 2, MAX_RANK, BM,
+                CU_TENSOR_MAP_SWIZZLE_128B, "lora h");
+    if (rc == QX_OK)
+      rc = encode(&prm.tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lora_B, uint64_t(N), uint64_t(rank),
+                  uint64_t(N) * 2, BN, uint32_t(kp), CU_TENSOR_MAP_SWIZZLE_NONE, "lora_B");
+    if (rc != QX_OK) return rc;
+  }
   prm.y = static_cast<__half*>(y);
   prm.M = M;
   prm.K = K;
@@ -567,7 +571,6 @@ extern "C" int qx_w4a16_lora_gemm_sm100(const void* x, const int32_t* qweight, c
   prm.zeros_packed = zeros_packed;
   prm.zero_offset = zero_offset;
   prm.grows = grows;
-  prm.lora_scale = lora_scale;
 
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
@@ -580,7 +583,7 @@ extern "C" int qx_w4a16_lora_gemm_sm100(const void* x, const int32_t* qweight, c
   if (rank > 0) {
     lora_down_kernel<<<(M + LD_ROWS - 1) / LD_ROWS, 128, 0, st>>>(
         static_cast<const __half*>(x), static_cast<const __half*>(lora_A),
-        static_cast<float*>(workspace), M, K, rank);
+        static_cast<__half*>(workspace), M, K, rank, lora_scale);
     QX_CUDA_TRY(cudaGetLastError(), "w4a16_gemm: lora_down launch");
   }
   dim3 grid(N / BN, (M + BM - 1) / BM);
