@@ -1,0 +1,257 @@
+"""Tensor-parallel Qwen3-architecture decoder on this library's operators.
+
+The model the reference patches (``qextract/patch.py:10-70``: HF Qwen3 with
+GPTQ int4 linears and PEFT LoRA adapters) written directly against the
+operators, sharded over ``torch.distributed`` ranks (one process per GPU,
+NCCL):
+
+* column-parallel q / k / v / gate / up: each rank holds N / tp output columns
+  (their scales, qzeros and LoRA B columns; LoRA A replicated);
+* row-parallel o / down: each rank holds K / tp input rows (LoRA A rows split,
+  LoRA B replicated), so the partial products and the LoRA partials meet in
+  one all-reduce after o and one after down;
+* q heads 32 / tp and KV heads 8 / tp per rank, each rank with its own
+  StreamingLLM ring (sink + window) for its KV heads;
+* embeddings replicated, the fp16 lm_head split over the vocabulary, greedy
+  sampling by an all-gather of the per-rank (max, argmax).
+
+Per decode step and layer: RMSNorm -> W4A16-LoRA GEMV q/k/v -> per-head
+RMSNorm of q and k (Qwen3) -> RoPE (theta 1e6, keys stored post-RoPE at their
+absolute positions) -> ring append -> GQA decode attention over sink + window
+(including the new token) -> o GEMV -> all-reduce -> residual -> RMSNorm ->
+gate / up GEMV -> SwiGLU -> down GEMV -> all-reduce -> residual.  Prefill
+chunks run the same operators with the tensor-core GEMM for the projections;
+their attention (each query over the sinks, the previous window and the causal
+part of its chunk) uses torch's scaled_dot_product_attention.
+
+Weights are synthetic: every full tensor comes from a generator seeded by
+(seed, layer, projection) on the device and each rank keeps its shard, so the
+model is the same for every tensor-parallel size.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from . import _C
+
+
+@dataclass
+class DecoderConfig:
+    num_layers: int = 36
+    hidden: int = 4096
+    intermediate: int = 12288
+    num_q_heads: int = 32
+    num_kv_heads: int = 8
+    head_dim: int = 128
+    vocab: int = 151936
+    rope_theta: float = 1e6
+    rms_eps: float = 1e-6
+    lora_rank: int = 16
+    lora_alpha: float = 32.0  # alpha / r = 2
+    group_size: int = 128
+    sink: int = 4
+    window: int = 4092
+    init_std: float = 0.02  # embeddings, norms, lm_head ~ N(0, std)
+
+
+class ShardedQuantLinear:
+    """One rank's shard of a GPTQ int4 (group-wise, packed qzeros all 8) + LoRA
+    linear; ``split`` is "col" (N), "row" (K) or None (replicated)."""
+
+    def __init__(self, K: int, N: int, cfg: DecoderConfig, seed: int, device, rank: int, world: int,
+                 split: str | None):
+        G, r = cfg.group_size, cfg.lora_rank
+        g = torch.Generator(device=device).manual_seed(seed)
+        qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), generator=g, device=device,
+                           dtype=torch.int32)
+        sc = (torch.rand(K // G, N, generator=g, device=device) * 0.015 + 0.005).half()
+        A = (torch.randn(K, r, generator=g, device=device) * 0.02).half()
+        B = (torch.randn(r, N, generator=g, device=device) * 0.02).half()
+        qz = torch.full((K // G, N // 8), 0x88888888 - 2 ** 32, dtype=torch.int32, device=device)
+        if split == "col" and world > 1:
+            n = N // world
+            c0, c1 = rank * n, (rank + 1) * n
+            qw, sc, qz, B = qw[:, c0:c1], sc[:, c0:c1], qz[:, c0 // 8:c1 // 8], B[:, c0:c1]
+            N = n
+        elif split == "row" and world > 1:
+            k = K // world
+            k0, k1 = rank * k, (rank + 1) * k
+            qw, sc, qz, A = qw[k0 // 8:k1 // 8], sc[k0 // G:k1 // G], qz[k0 // G:k1 // G], A[k0:k1]
+            K = k
+        self.K, self.N = K, N
+        self.qweight, self.scales, self.qzeros = qw.contiguous(), sc.contiguous(), qz.contiguous()
+        self.lora_A, self.lora_B = A.contiguous(), B.contiguous()
+        self.group, self.alpha = G, cfg.lora_alpha
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        return _C.w4a16_lora_gemv(x, self.qweight, self.scales, self.qzeros, self.lora_A,
+                                  self.lora_B, self.group, self.alpha)
+
+
+class TPDecoder:
+    def __init__(self, cfg: DecoderConfig, batch: int, device, seed: int = 4,
+                 group: dist.ProcessGroup | None = None):
+        self.cfg, self.batch, self.device = cfg, batch, torch.device(device)
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        w, r = self.world, self.rank
+        if cfg.num_q_heads % w or cfg.num_kv_heads % w or cfg.intermediate % w or cfg.vocab % w:
+            raise ValueError(f"tensor-parallel size {w} does not divide the heads / sizes")
+        self.hq, self.hkv = cfg.num_q_heads // w, cfg.num_kv_heads // w
+        D, H = cfg.head_dim, cfg.hidden
+        dev = self.device
+        gen = torch.Generator(device=dev)
+
+        def normal(shape, s):
+            gen.manual_seed(s)
+            return (torch.randn(*shape, generator=gen, device=dev) * cfg.init_std).half()
+
+        self.embed = normal((cfg.vocab, H), seed * 1000003 + 1)
+        vs = cfg.vocab // w
+        self.lm_head = normal((H, cfg.vocab), seed * 1000003 + 2)[:, r * vs:(r + 1) * vs].contiguous()
+        self.final_norm = normal((H,), seed * 1000003 + 3)
+        self.layers = []
+        for li in range(cfg.num_layers):
+            base = seed * 1000003 + 100 + li * 16
+            L = dict(
+                in_norm=normal((H,), base), post_norm=normal((H,), base + 1),
+                q_norm=normal((D,), base + 2), k_norm=normal((D,), base + 3),
+                q=ShardedQuantLinear(H, cfg.num_q_heads * D, cfg, base + 4, dev, r, w, "col"),
+                k=ShardedQuantLinear(H, cfg.num_kv_heads * D, cfg, base + 5, dev, r, w, "col"),
+                v=ShardedQuantLinear(H, cfg.num_kv_heads * D, cfg, base + 6, dev, r, w, "col"),
+                o=ShardedQuantLinear(cfg.num_q_heads * D, H, cfg, base + 7, dev, r, w, "row"),
+                gate=ShardedQuantLinear(H, cfg.intermediate, cfg, base + 8, dev, r, w, "col"),
+                up=ShardedQuantLinear(H, cfg.intermediate, cfg, base + 9, dev, r, w, "col"),
+                down=ShardedQuantLinear(cfg.intermediate, H, cfg, base + 10, dev, r, w, "row"),
+            )
+            self.layers.append(L)
+        self.cache = _C.RingBufferKVCache(cfg.num_layers, self.hkv, D, cfg.sink, cfg.window,
+                                          batch=batch, device=dev)
+        self.max_pos = 1 << 16
+        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D))
+        ang = torch.arange(self.max_pos, device=dev, dtype=torch.float32)[:, None] * inv[None, :]
+        self.cos = torch.cat([ang.cos(), ang.cos()], dim=-1)  # [pos, D]
+        self.sin = torch.cat([ang.sin(), ang.sin()], dim=-1)
+
+    # ------------------------------------------------------------------ pieces
+    def _allreduce(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world > 1:
+            dist.all_reduce(t, group=self.group)
+        return t
+
+    def _rope(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        """x [..., T, heads, D] fp16; cos/sin [T, D] fp32 -> rotated fp16 (HF rotate_half)."""
+        xf = x.float()
+        half = x.size(-1) // 2
+        rot = torch.cat([-xf[..., half:], xf[..., :half]], dim=-1)
+        return (xf * cos[:, None, :] + rot * sin[:, None, :]).half()
+
+    def _head_norm(self, t: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        return _C.fused_rmsnorm(t.contiguous(), w, self.cfg.rms_eps)
+
+    def _mlp(self, L, h: torch.Tensor) -> torch.Tensor:
+        a = _C.fused_swiglu(L["gate"](h), L["up"](h))
+        return self._allreduce(L["down"](a))
+
+    # ------------------------------------------------------------------ decode
+    def decode_step(self, tokens: torch.Tensor, return_hidden: bool = False):
+        """One greedy step for the batch: ``tokens`` int64 [B] (device) -> next
+        tokens int64 [B] (and the final hidden state [B, H] if asked).  The
+        position is the cache's token count."""
+        cfg, B, D = self.cfg, self.batch, self.cfg.head_dim
+        pos = self.cache.get_total_written()
+        cos, sin = self.cos[pos:pos + 1], self.sin[pos:pos + 1]
+        x = self.embed.index_select(0, tokens)  # [B, H]
+        for li, L in enumerate(self.layers):
+            h = _C.fused_rmsnorm(x, L["in_norm"], cfg.rms_eps)
+            q = self._head_norm(L["q"](h).view(B, self.hq, D), L["q_norm"])
+            k = self._head_norm(L["k"](h).view(B, self.hkv, D), L["k_norm"])
+            v = L["v"](h).view(B, 1, self.hkv, D)
+            q = self._rope(q.view(B, 1, self.hq, D), cos, sin).view(B, self.hq, D)
+            k = self._rope(k.view(B, 1, self.hkv, D), cos, sin)
+            self.cache.append(k, v, li)
+            att = _C.decode_attention(q, self.cache.k[li], self.cache.v[li], pos + 1, cfg.sink,
+                                      cfg.window)
+            x = x + self._allreduce(L["o"](att.view(B, self.hq * D)))
+            h = _C.fused_rmsnorm(x, L["post_norm"], cfg.rms_eps)
+            x = x + self._mlp(L, h)
+        nxt = self._greedy(x)
+        return (nxt, x) if return_hidden else nxt
+
+    def _greedy_logits(self, x: torch.Tensor) -> torch.Tensor:
+        """this rank's vocabulary slice of the logits [B, V / tp] (fp16, cuBLAS)"""
+        h = _C.fused_rmsnorm(x, self.final_norm, self.cfg.rms_eps)
+        return h @ self.lm_head
+
+    def _greedy(self, x: torch.Tensor) -> torch.Tensor:
+        logits = self._greedy_logits(x)
+        val, idx = logits.float().max(dim=-1)
+        idx = idx + self.rank * self.lm_head.size(1)
+        if self.world > 1:
+            vals = [torch.empty_like(val) for _ in range(self.world)]
+            idxs = [torch.empty_like(idx) for _ in range(self.world)]
+            dist.all_gather(vals, val, group=self.group)
+            dist.all_gather(idxs, idx, group=self.group)
+            v, i = torch.stack(vals), torch.stack(idxs)  # [world, B]
+            best = v.argmax(dim=0)
+            idx = i.gather(0, best[None, :])[0]
+        return idx
+
+    # ----------------------------------------------------------------- prefill
+    def _cache_positions(self, c: int) -> torch.Tensor:
+        """absolute positions of the cache's valid slots in logical order"""
+        S, W = self.cfg.sink, self.cfg.window
+        sinks = list(range(min(c, S)))
+        n_ring = min(max(c - S, 0), W)
+        return torch.tensor(sinks + list(range(c - n_ring, c)), device=self.device)
+
+    def prefill(self, tokens: torch.Tensor, chunk: int = 2048, return_hidden: bool = False):
+        """``tokens`` int64 [B, T] (device); returns the greedy next tokens [B]
+        (and the last position's hidden state [B, H] if asked)."""
+        cfg, B, D = self.cfg, self.batch, self.cfg.head_dim
+        T = tokens.size(1)
+        x_last = None
+        for t0 in range(0, T, chunk):
+            tc = tokens[:, t0:t0 + chunk]
+            n = tc.size(1)
+            c = self.cache.get_total_written()
+            cos, sin = self.cos[c:c + n], self.sin[c:c + n]
+            qpos = torch.arange(c, c + n, device=self.device)
+            kpos = torch.cat([self._cache_positions(c), qpos])
+            # causal, and within the sinks or the last `window` positions
+            mask = (kpos[None, :] <= qpos[:, None]) & (
+                (kpos[None, :] < cfg.sink) | (kpos[None, :] > qpos[:, None] - cfg.window))
+            x = self.embed.index_select(0, tc.reshape(-1)).view(B * n, cfg.hidden)
+            for li, L in enumerate(self.layers):
+                h = _C.fused_rmsnorm(x, L["in_norm"], cfg.rms_eps)
+                q = self._head_norm(L["q"](h).view(B * n * self.hq, D), L["q_norm"])
+                k = self._head_norm(L["k"](h).view(B * n * self.hkv, D), L["k_norm"])
+                v = L["v"](h).view(B, n, self.hkv, D)
+                q = self._rope(q.view(B, n, self.hq, D), cos, sin)
+                k = self._rope(k.view(B, n, self.hkv, D), cos, sin)
+                if c > 0:
+                    kc, vc = self.cache.get_kv(li)
+                    if B == 1:
+                        kc, vc = kc[None], vc[None]
+                    kk, vv = torch.cat([kc, k], dim=1), torch.cat([vc, v], dim=1)
+                else:
+                    kk, vv = k, v
+                rep = self.hq // self.hkv
+                att = torch.nn.functional.scaled_dot_product_attention(
+                    q.transpose(1, 2), kk.transpose(1, 2).repeat_interleave(rep, dim=1),
+                    vv.transpose(1, 2).repeat_interleave(rep, dim=1), attn_mask=mask,
+                    scale=1.0 / math.sqrt(D))  # [B, hq, n, D]
+                self.cache.append(k, v, li)
+                att = att.transpose(1, 2).reshape(B * n, self.hq * D).contiguous()
+                x = x + self._allreduce(L["o"](att))
+                h = _C.fused_rmsnorm(x, L["post_norm"], cfg.rms_eps)
+                x = x + self._mlp(L, h)
+            x_last = x.view(B, n, cfg.hidden)[:, -1].contiguous()
+        nxt = self._greedy(x_last)
+        return (nxt, x_last) if return_hidden else nxt
