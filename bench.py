@@ -491,6 +491,113 @@ def run_prefill_suite(args):
     return 0
 
 
+def run_decode_tp(args):
+    """Qwen3-8B-architecture decode (random init, GPTQ int4 g128 + LoRA r16
+    linears, fp16 norms/embeddings/lm_head, ring of 4 sink + 4092 window),
+    tensor-parallel over the torchrun ranks: an 8192-token prompt prefilled in
+    2048-token chunks, then 64 greedy decode steps replayed from per-step CUDA
+    graphs (NCCL all-reduces inside).  One JSON line per batch size; value =
+    decoded tokens per second over the whole job, time = max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from qextract_infer_b200.tp_decoder import DecoderConfig, TPDecoder
+
+    world, rank, local = dist_setup()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=__import__("datetime").timedelta(seconds=300))
+    dev = torch.device("cuda", local if world > 1 else torch.cuda.current_device())
+    torch.cuda.set_device(dev)
+    cfg = DecoderConfig()
+    prompt_len, decode_steps, chunk = args.prompt, args.decode, 2048
+    batches = [int(b) for b in args.batches.split(",")]
+    hbm = measured_peaks()[0]
+    for B in batches:
+        dec = TPDecoder(cfg, batch=B, device=dev, seed=4)
+        prompt = torch.randint(0, cfg.vocab, (B, prompt_len), generator=torch.Generator().manual_seed(4))
+        prompt = prompt.to(dev)
+        torch.cuda.synchronize(dev)
+        t0 = time.time()
+        nxt = dec.prefill(prompt, chunk=chunk)
+        torch.cuda.synchronize(dev)
+        prefill_s = time.time() - t0
+        count0 = dec.cache.get_total_written()
+        k0, v0 = dec.cache.k.clone(), dec.cache.v.clone()
+        tok = torch.empty_like(nxt)
+        st = torch.cuda.Stream(dev)
+
+        def restore():
+            dec.cache.k.copy_(k0)
+            dec.cache.v.copy_(v0)
+            dec.cache._write_count = count0
+            tok.copy_(nxt)
+
+        with torch.cuda.stream(st):
+            restore()
+            tok.copy_(dec.decode_step(tok))  # eager step: plans, workspaces, lazy state
+            restore()
+        st.synchronize()
+        graphs, pool = [], torch.cuda.graph_pool_handle()
+        for _ in range(decode_steps):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool, stream=st):
+                tok.copy_(dec.decode_step(tok))
+            graphs.append(g)
+        for rep in range(2):  # rep 0 uploads the graphs; rep 1 is timed
+            with torch.cuda.stream(st):
+                restore()
+            st.synchronize()
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(st):
+                e0.record(st)
+                for g in graphs:
+                    g.replay()
+                e1.record(st)
+            e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t[0])
+        step_ms = ms / decode_steps
+        # bytes one decode step reads per rank: int4 weights + scales/qzeros + LoRA, lm_head
+        # shard, and the ring (all layers, this rank's KV heads, every sequence)
+        wbytes = 0
+        for L in dec.layers:
+            for k in ("q", "k", "v", "o", "gate", "up", "down"):
+                lin = L[k]
+                wbytes += sum(t.numel() * t.element_size() for t in
+                              (lin.qweight, lin.scales, lin.qzeros, lin.lora_A, lin.lora_B))
+        wbytes += dec.lm_head.numel() * 2
+        kvbytes = 2 * cfg.num_layers * B * (cfg.sink + cfg.window) * dec.hkv * cfg.head_dim * 2
+        per_rank_gbs = (wbytes + kvbytes) / (step_ms / 1e3) / 1e9
+        line = {"metric": "Qwen3-8B decode tok/s", "value": B * decode_steps / (ms / 1e3),
+                "unit": "tok/s", "n_gpus": world, "steps": decode_steps, "warmup": 1,
+                "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "fp16 activations, int4 weights, fp32 accumulate",
+                "data": "synthetic (random-init Qwen3-8B architecture, uniform random prompt tokens)",
+                "config": {"workload": "Qwen3-8B decoder, TP decode", "batch": B,
+                           "prompt": prompt_len, "decode_tokens": decode_steps,
+                           "parallelism": f"tp{world}", "prefill_chunk": chunk,
+                           "graphs": "one CUDA graph per decode step"},
+                "prefill_s": prefill_s, "prefill_tok_s": B * prompt_len / prefill_s,
+                "roofline": {"bound": "hbm", "achieved": per_rank_gbs, "peak": hbm, "unit": "GB/s",
+                             "frac": per_rank_gbs / hbm, "bytes_per_step_per_rank": wbytes + kvbytes}}
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        del graphs, g
+        del dec, k0, v0
+        torch.cuda.empty_cache()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -501,7 +608,10 @@ def main():
                     help="weight sets in the rotation (default: enough for > 2x L2)")
     ap.add_argument("--skip-e2e", action="store_true", help="omit the public-API timing")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline")
-    ap.add_argument("--workload", choices=["decode_gemv", "kernels", "prefill_gemm"],
+    ap.add_argument("--batches", default="1,32", help="decode_tp: batch sizes")
+    ap.add_argument("--prompt", type=int, default=8192, help="decode_tp: prompt tokens")
+    ap.add_argument("--decode", type=int, default=64, help="decode_tp: greedy decode tokens")
+    ap.add_argument("--workload", choices=["decode_gemv", "kernels", "prefill_gemm", "decode_tp"],
                     default="decode_gemv",
                     help="decode_gemv: the headline line; kernels: RMSNorm/SwiGLU/ring/attention lines; "
                          "prefill_gemm: the tcgen05 GEMM over the Qwen3-8B shapes at M=4096")
@@ -510,6 +620,8 @@ def main():
         return run_kernel_suite(args)
     if args.workload == "prefill_gemm":
         return run_prefill_suite(args)
+    if args.workload == "decode_tp":
+        return run_decode_tp(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)

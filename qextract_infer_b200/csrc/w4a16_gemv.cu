@@ -697,6 +697,9 @@ static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed,
     std::lock_guard<std::mutex> lk(mu);
     auto itc = cache.find(key);
     if (itc != cache.end()) {
+      if (itc->second.tiles == 0)  // remembered: no cluster size fits
+        return fail(QX_ERR_UNSUPPORTED, "w4a16_gemv: no cluster size fits M=%d K=%d N=%d rank=%d", M, K,
+                    N, rank);
       *out = itc->second;
       return QX_OK;
     }
@@ -745,8 +748,12 @@ static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed,
       best_key = key2;
     }
   }
-  if (best_key < 0)
-    return fail(QX_ERR_UNSUPPORTED, "w4a16_gemv: no cluster size fits K=%d N=%d rank=%d", K, N, rank);
+  if (best_key < 0) {
+    std::lock_guard<std::mutex> lk(mu);
+    cache[key] = Plan{};
+    return fail(QX_ERR_UNSUPPORTED, "w4a16_gemv: no cluster size fits M=%d K=%d N=%d rank=%d", M, K, N,
+                rank);
+  }
   {
     std::lock_guard<std::mutex> lk(mu);
     cache[key] = best;
@@ -916,8 +923,11 @@ extern "C" int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const v
              "w4a16_gemv: misaligned zeros/y");
   QX_REQUIRE(zeros_packed == 0 || zeros_packed == 1, "w4a16_gemv: zeros_packed must be 0 or 1");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  for (int m0 = 0; m0 < M; m0 += gemv::MROWS) {
-    const int mc = std::min(gemv::MROWS, M - m0);
+  // up to 32 rows per launch; fewer when the activations of 32 rows and the
+  // kernel's weight stages do not fit in shared memory together
+  int mrows = gemv::MROWS;
+  for (int m0 = 0; m0 < M;) {
+    const int mc = std::min(mrows, M - m0);
     gemv::Params prm{};
     prm.x = static_cast<const __half*>(x) + size_t(m0) * K;
     prm.qw = reinterpret_cast<const uint32_t*>(qweight);
@@ -936,7 +946,12 @@ extern "C" int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const v
     prm.lora_scale = rank > 0 ? lora_scale : 0.f;
     prm.pdl = g_pdl_enabled.load(std::memory_order_relaxed);
     const int rc = gemv::dispatch(prm, group_size / gemv::KSTEP, st);
+    if (rc == QX_ERR_UNSUPPORTED && mc > 8) {
+      mrows = mc > 16 ? 16 : 8;
+      continue;
+    }
     if (rc != QX_OK) return rc;
+    m0 += mc;
   }
   return QX_OK;
 }

@@ -244,3 +244,15 @@ def test_no_device_error_after_calls(C):
     torch.cuda.synchronize()
     assert _lib.load().qx_get_device_error(ctypes.byref(code), 1) == 0, _lib.last_error()
     assert code.value == 0
+
+
+def test_batch_rows_long_k_fall_back_to_fewer_rows(C):
+    """32 rows at K=12288 (Qwen3-8B down_proj): the launch splits the rows when
+    their activations and the weight stages do not fit in shared memory."""
+    d = make_gemv_inputs(32, 12288, 256, 16, seed=31)
+    t = _dev(d)
+    y = C.w4a16_lora_gemv(t["x"], t["qweight"], t["scales"], t["zeros"], t["lora_A"], t["lora_B"],
+                          128, 32.0)
+    ref = w4a16_lora_gemv_ref(d["x"], d["qweight"], d["scales"], d["zeros"], d["lora_A"],
+                              d["lora_B"], 128, 32.0)
+    assert_close(to_np(y), ref, RTOL, ATOL, "M=32 K=12288")
