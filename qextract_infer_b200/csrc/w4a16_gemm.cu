@@ -30,7 +30,7 @@
 //   by TMA before the weight stream; warps 2-9 transpose the B tile into the
 //   K-major swizzled layout in shared memory.
 // Every wait is bounded (~200 ms, then QX_DEVERR_MBAR_TIMEOUT in the device
-// error word); no TMA multicast.
+// error word); every copy targets this CTA only.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 

@@ -221,7 +221,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   }
   return true;
 }
-// 1-D bulk copies global -> shared (no multicast), completion counted on `bar`
+// 1-D bulk copies global -> this CTA's shared memory, completion counted on `bar`
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
                                          uint32_t bar) {
   asm volatile(
@@ -230,7 +230,7 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
 }
-// 2-D tensor copy global -> shared (no multicast); coordinates in elements,
+// 2-D tensor copy global -> this CTA's shared memory; coordinates in elements,
 // x innermost (x * element size is a multiple of 16 B at every call site)
 __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
                                        uint32_t bar) {

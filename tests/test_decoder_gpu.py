@@ -46,3 +46,21 @@ def test_prefill_and_decode_match_reference():
         xr = ref.token(cur_in)
         _close(hid, xr, f"decode step {step} hidden")
         _close(dec._greedy_logits(hid), ref.logits(xr), f"decode step {step} logits")
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="tensor parallelism needs two GPUs")
+def test_tensor_parallel_two_ranks_match_reference():
+    """TP = 2 over NCCL (torchrun, one process per GPU): column/row-parallel
+    linears, the all-reduces and the vocab-split greedy against the unsharded
+    reference on each rank."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", "29531",
+           os.path.join(root, "tests", "tp_decoder_check.py")]
+    r = subprocess.run(cmd, cwd=root, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert r.stdout.count("ok=True") == 2, r.stdout[-2000:]
