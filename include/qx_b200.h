@@ -110,6 +110,35 @@ int qx_w4a16_lora_gemm_sm100(const void* x, const int32_t* qweight, const void* 
                              size_t workspace_bytes, qx_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Fused kernels of the tensor-parallel decode step (new components; the
+ * reference's patched Qwen3 layer, qextract/patch_qwen.py, runs each as
+ * separate torch ops).  Rounding points equal the unfused sequence.
+ *
+ * qx_add_rmsnorm: x <- fp16(x + delta) in place (the residual add), then
+ *   y = fp16((x * rsqrt(mean(x^2) + eps)) * w) as qx_fused_rmsnorm.
+ *   x, delta, y fp16 [rows, hidden]; w fp16 [hidden]; hidden % 8 == 0,
+ *   hidden <= 8192; 16-byte aligned.
+ * qx_qk_norm_rope_append: qkv fp16 [batch, q_heads + 2 kv_heads, head_dim]
+ *   (the fused q|k|v projection of one decode position); q and k heads are
+ *   RMSNorm'd over head_dim with q_norm_w / k_norm_w (fp16 result) and
+ *   rotated (rotate-half RoPE; cos_row / sin_row fp32 [head_dim] of the
+ *   position); q heads go to q_out fp16 [batch, q_heads, head_dim], k and v
+ *   heads to slot (pos < sink ? pos : sink + (pos - sink) % window) of the
+ *   ring caches k_cache / v_cache fp16 [batch, sink + window, kv_heads,
+ *   head_dim].  head_dim in {64, 128, 256}.
+ * qx_swiglu_packed: gate_up fp16 [rows, 2 inter] (gate columns, then up);
+ *   y fp16 [rows, inter] = fp16(silu(gate) * up) as qx_fused_swiglu;
+ *   inter % 8 == 0, 16-byte aligned.
+ * ---------------------------------------------------------------------- */
+int qx_add_rmsnorm(void* x, const void* delta, const void* weight, void* y, int64_t rows, int hidden,
+                   float eps, qx_stream_t stream);
+int qx_qk_norm_rope_append(const void* qkv, int batch, int q_heads, int kv_heads, int head_dim,
+                           const void* q_norm_w, const void* k_norm_w, float eps,
+                           const float* cos_row, const float* sin_row, void* q_out, void* k_cache,
+                           void* v_cache, int sink, int window, int64_t pos, qx_stream_t stream);
+int qx_swiglu_packed(const void* gate_up, void* y, int64_t rows, int inter, qx_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Fused RMSNorm.  Replaces fused_rmsnorm() (csrc/kernels/rmsnorm.cu:162-210,
  * bound at csrc/binding.cpp:36-38).
  *   y[r, :] = fp16( (x[r, :] * rsqrt(mean(x[r, :]^2) + eps)) * w )

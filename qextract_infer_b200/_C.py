@@ -87,6 +87,69 @@ def fused_swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     return out
 
 
+# ------------------------------------------------------ fused decode step --
+def add_rmsnorm(x: torch.Tensor, delta: torch.Tensor, weight: torch.Tensor,
+                eps: float = 1e-6) -> torch.Tensor:
+    """Residual add and RMSNorm in one pass: ``x += delta`` (in place, fp16
+    rounding) and returns ``fused_rmsnorm(x, weight, eps)`` (new component:
+    the reference's patched layer runs the add and the norm separately)."""
+    for t, n in ((x, "x"), (delta, "delta"), (weight, "weight")):
+        _check_input(t, n)
+        _check_fp16(t, n)
+    if x.shape != delta.shape or weight.dim() != 1 or weight.numel() != x.size(-1):
+        raise RuntimeError("add_rmsnorm: x and delta must match, weight must be [hidden]")
+    out = torch.empty_like(x)
+    st = _stream(x.device)
+    _lib.check(_LIB.qx_add_rmsnorm(x.data_ptr(), delta.data_ptr(), weight.data_ptr(), out.data_ptr(),
+                                   x.numel() // x.size(-1), x.size(-1), float(eps), st.cuda_stream),
+               "add_rmsnorm")
+    return out
+
+
+def qk_norm_rope_append(qkv: torch.Tensor, q_heads: int, kv_heads: int, q_norm: torch.Tensor,
+                        k_norm: torch.Tensor, eps: float, cos_row: torch.Tensor,
+                        sin_row: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                        sink: int, window: int, pos: int) -> torch.Tensor:
+    """One decode position: ``qkv`` fp16 ``[B, (q_heads + 2 kv_heads) * D]``;
+    returns q ``[B, q_heads, D]`` (head-normed, rotated) and writes the
+    head-normed, rotated k and the v heads into ring slot ``pos`` of
+    ``k_cache`` / ``v_cache`` ``[B, sink + window, kv_heads, D]``."""
+    for t, n in ((qkv, "qkv"), (q_norm, "q_norm"), (k_norm, "k_norm"), (k_cache, "k_cache"),
+                 (v_cache, "v_cache")):
+        _check_input(t, n)
+        _check_fp16(t, n)
+    D = q_norm.numel()
+    B = qkv.size(0)
+    if qkv.numel() != B * (q_heads + 2 * kv_heads) * D or k_norm.numel() != D:
+        raise RuntimeError("qk_norm_rope_append: qkv must be [B, (q_heads + 2 kv_heads) * head_dim]")
+    if tuple(k_cache.shape) != (B, sink + window, kv_heads, D) or v_cache.shape != k_cache.shape:
+        raise RuntimeError("qk_norm_rope_append: cache must be [B, sink + window, kv_heads, head_dim]")
+    for t, n in ((cos_row, "cos_row"), (sin_row, "sin_row")):
+        _check_input(t, n)
+        if t.dtype != torch.float32 or t.numel() != D:
+            raise RuntimeError(f"{n} must be float32 [{D}]")
+    q = torch.empty(B, q_heads, D, dtype=torch.float16, device=qkv.device)
+    st = _stream(qkv.device)
+    _lib.check(_LIB.qx_qk_norm_rope_append(
+        qkv.data_ptr(), B, q_heads, kv_heads, D, q_norm.data_ptr(), k_norm.data_ptr(), float(eps),
+        cos_row.data_ptr(), sin_row.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+        int(sink), int(window), int(pos), st.cuda_stream), "qk_norm_rope_append")
+    return q
+
+
+def swiglu_packed(gate_up: torch.Tensor) -> torch.Tensor:
+    """``gate_up`` fp16 ``[..., 2 I]`` (gate columns then up) ->
+    ``fp16(silu(gate) * up)`` ``[..., I]`` (the formula of ``fused_swiglu``)."""
+    _check_input(gate_up, "gate_up")
+    _check_fp16(gate_up, "gate_up")
+    inter = gate_up.size(-1) // 2
+    out = torch.empty(*gate_up.shape[:-1], inter, dtype=torch.float16, device=gate_up.device)
+    st = _stream(gate_up.device)
+    _lib.check(_LIB.qx_swiglu_packed(gate_up.data_ptr(), out.data_ptr(), gate_up.numel() // (2 * inter),
+                                     inter, st.cuda_stream), "swiglu_packed")
+    return out
+
+
 # ------------------------------------------------------------------- GEMV --
 def _prepare_lora(lora_A, lora_B):
     """Pad rank up to a supported value with zero rows/columns (exact: the
@@ -108,7 +171,10 @@ def _prepare_lora(lora_A, lora_B):
 GEMM_MIN_ROWS = 128
 
 
-def _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale, zero_offset):
+def _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale, zero_offset,
+           path: str | None = None):
+    """``path`` (tests and benchmarks): "gemm" forces the tensor-core GEMM;
+    None routes by shape (GEMM for >= GEMM_MIN_ROWS rows, else the GEMV)."""
     for t, n in ((input, "input"), (qweight, "qweight"), (scales, "scales"), (zeros, "zeros")):
         _check_input(t, n)
     _check_fp16(input, "input")
@@ -147,7 +213,8 @@ def _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale
     out = torch.empty(*lead, N, dtype=torch.float16, device=input.device)
     dev = input.device
     st = _stream(dev)
-    if M >= GEMM_MIN_ROWS and N % 256 == 0 and K % 64 == 0 and rank <= 64:
+    if path == "gemm" or (path is None and M >= GEMM_MIN_ROWS and N % 256 == 0 and K % 64 == 0
+                          and rank <= 64):
         # prefill: the tcgen05 tensor-core GEMM
         with torch.cuda.device(dev):
             need = _LIB.qx_w4a16_lora_gemm_sm100_workspace_size(M, rank)
@@ -275,6 +342,11 @@ class RingBufferKVCache:
             self.window_size, self._write_count, st.cuda_stream), "ring_append")
         if layer_idx == self.num_layers - 1:
             self._write_count += T
+
+    def advance(self, tokens: int) -> None:
+        """Count ``tokens`` positions that a fused decode kernel
+        (``qk_norm_rope_append``) wrote into every layer."""
+        self._write_count += int(tokens)
 
     def get_kv(self, layer_idx: int):
         """(K, V) in logical order: ``[valid, H, D]`` for batch 1, else

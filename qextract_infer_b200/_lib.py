@@ -34,6 +34,12 @@ SIGNATURES = {
     "qx_get_device_error": (c_int, [c_void_p, c_int]),
     "qx_fused_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_void_p]),
     "qx_fused_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "qx_add_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float,
+                               c_void_p]),
+    "qx_qk_norm_rope_append": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                                       c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_int, c_int, c_int64, c_void_p]),
+    "qx_swiglu_packed": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_void_p]),
     "qx_ring_append": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                c_int, c_int, c_int64, c_void_p]),
     "qx_ring_slot_indices": (c_int64, [c_void_p, c_int, c_int, c_int64, c_void_p]),

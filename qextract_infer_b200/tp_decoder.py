@@ -15,14 +15,18 @@ NCCL):
 * embeddings replicated, the fp16 lm_head split over the vocabulary, greedy
   sampling by an all-gather of the per-rank (max, argmax).
 
-Per decode step and layer: RMSNorm -> W4A16-LoRA GEMV q/k/v -> per-head
-RMSNorm of q and k (Qwen3) -> RoPE (theta 1e6, keys stored post-RoPE at their
-absolute positions) -> ring append -> GQA decode attention over sink + window
-(including the new token) -> o GEMV -> all-reduce -> residual -> RMSNorm ->
-gate / up GEMV -> SwiGLU -> down GEMV -> all-reduce -> residual.  Prefill
-chunks run the same operators with the tensor-core GEMM for the projections;
-their attention (each query over the sinks, the previous window and the causal
-part of its chunk) uses torch's scaled_dot_product_attention.
+The projections that read the same input are fused: q|k|v and gate|up are
+each one W4A16-LoRA call (weights side by side, LoRA A side by side, LoRA B
+block-diagonal, rank zero-padded to a supported size: the same math).  Per
+decode step and layer (9 launches + 2 all-reduces): qkv GEMV -> per-head
+RMSNorm of q and k (Qwen3), RoPE (theta 1e6, keys stored post-RoPE at their
+absolute positions) and the ring append in one kernel -> GQA decode attention
+over sink + window (including the new token) -> o GEMV -> all-reduce ->
+residual add + RMSNorm in one kernel -> gate|up GEMV -> SwiGLU -> down GEMV ->
+all-reduce -> residual add + the next RMSNorm in one kernel.  Prefill chunks
+run the same projections with the tensor-core GEMM; their attention (each
+query over the sinks, the previous window and the causal part of its chunk)
+uses torch's scaled_dot_product_attention.
 
 Weights are synthetic: every full tensor comes from a generator seeded by
 (seed, layer, projection) on the device and each rank keeps its shard, so the
@@ -34,6 +38,7 @@ from __future__ import annotations
 import math
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -86,11 +91,53 @@ class ShardedQuantLinear:
         self.K, self.N = K, N
         self.qweight, self.scales, self.qzeros = qw.contiguous(), sc.contiguous(), qz.contiguous()
         self.lora_A, self.lora_B = A.contiguous(), B.contiguous()
-        self.group, self.alpha = G, cfg.lora_alpha
+        self.group = G
+        self.lora_scale = float(np.float32(cfg.lora_alpha) / np.float32(r))  # alpha / r in fp32
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        return _C.w4a16_lora_gemv(x, self.qweight, self.scales, self.qzeros, self.lora_A,
-                                  self.lora_B, self.group, self.alpha)
+        return _C._w4a16(x, self.qweight, self.scales, self.qzeros, self.lora_A, self.lora_B,
+                         self.group, self.lora_scale, 0)
+
+
+class FusedQuantLinear:
+    """Column-parallel linears that read the same input, as one W4A16-LoRA
+    call: qweight / scales / qzeros side by side along N, LoRA A side by side
+    and LoRA B block-diagonal, the rank zero-padded to ``rank`` (the padding
+    contributes 0, so every part's output equals its own linear's).  The parts
+    share alpha / r."""
+
+    def __init__(self, parts: list, rank: int):
+        dev = parts[0].qweight.device
+        self.K = parts[0].K
+        self.splits = [p.N for p in parts]
+        self.N = sum(self.splits)
+        self.qweight = torch.cat([p.qweight for p in parts], 1).contiguous()
+        self.scales = torch.cat([p.scales for p in parts], 1).contiguous()
+        self.qzeros = torch.cat([p.qzeros for p in parts], 1).contiguous()
+        rs = [p.lora_A.size(1) for p in parts]
+        if sum(rs) > rank or len({p.lora_scale for p in parts}) != 1:
+            raise ValueError("fused parts need one alpha / r and a total rank <= rank")
+        A = torch.zeros(self.K, rank, dtype=torch.float16, device=dev)
+        B = torch.zeros(rank, self.N, dtype=torch.float16, device=dev)
+        r0 = n0 = 0
+        for p, r in zip(parts, rs):
+            A[:, r0:r0 + r] = p.lora_A
+            B[r0:r0 + r, n0:n0 + p.N] = p.lora_B
+            r0, n0 = r0 + r, n0 + p.N
+        self.lora_A, self.lora_B = A, B
+        self.group, self.lora_scale = parts[0].group, parts[0].lora_scale
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        return _C._w4a16(x, self.qweight, self.scales, self.qzeros, self.lora_A, self.lora_B,
+                         self.group, self.lora_scale, 0)
+
+
+def _padded_rank(r: int) -> int:
+    """smallest LoRA rank the kernels take that holds r"""
+    for s in (8, 16, 32, 64, 128):
+        if s >= r:
+            return s
+    raise ValueError(f"fused LoRA rank {r} > 128")
 
 
 class TPDecoder:
@@ -119,17 +166,20 @@ class TPDecoder:
         self.layers = []
         for li in range(cfg.num_layers):
             base = seed * 1000003 + 100 + li * 16
+            q = ShardedQuantLinear(H, cfg.num_q_heads * D, cfg, base + 4, dev, r, w, "col")
+            k = ShardedQuantLinear(H, cfg.num_kv_heads * D, cfg, base + 5, dev, r, w, "col")
+            v = ShardedQuantLinear(H, cfg.num_kv_heads * D, cfg, base + 6, dev, r, w, "col")
+            gate = ShardedQuantLinear(H, cfg.intermediate, cfg, base + 8, dev, r, w, "col")
+            up = ShardedQuantLinear(H, cfg.intermediate, cfg, base + 9, dev, r, w, "col")
             L = dict(
                 in_norm=normal((H,), base), post_norm=normal((H,), base + 1),
                 q_norm=normal((D,), base + 2), k_norm=normal((D,), base + 3),
-                q=ShardedQuantLinear(H, cfg.num_q_heads * D, cfg, base + 4, dev, r, w, "col"),
-                k=ShardedQuantLinear(H, cfg.num_kv_heads * D, cfg, base + 5, dev, r, w, "col"),
-                v=ShardedQuantLinear(H, cfg.num_kv_heads * D, cfg, base + 6, dev, r, w, "col"),
+                qkv=FusedQuantLinear([q, k, v], _padded_rank(3 * cfg.lora_rank)),
                 o=ShardedQuantLinear(cfg.num_q_heads * D, H, cfg, base + 7, dev, r, w, "row"),
-                gate=ShardedQuantLinear(H, cfg.intermediate, cfg, base + 8, dev, r, w, "col"),
-                up=ShardedQuantLinear(H, cfg.intermediate, cfg, base + 9, dev, r, w, "col"),
+                gate_up=FusedQuantLinear([gate, up], _padded_rank(2 * cfg.lora_rank)),
                 down=ShardedQuantLinear(cfg.intermediate, H, cfg, base + 10, dev, r, w, "row"),
             )
+            del q, k, v, gate, up
             self.layers.append(L)
         self.cache = _C.RingBufferKVCache(cfg.num_layers, self.hkv, D, cfg.sink, cfg.window,
                                           batch=batch, device=dev)
@@ -156,8 +206,7 @@ class TPDecoder:
         return _C.fused_rmsnorm(t.contiguous(), w, self.cfg.rms_eps)
 
     def _mlp(self, L, h: torch.Tensor) -> torch.Tensor:
-        a = _C.fused_swiglu(L["gate"](h), L["up"](h))
-        return self._allreduce(L["down"](a))
+        return self._allreduce(L["down"](_C.swiglu_packed(L["gate_up"](h))))
 
     # ------------------------------------------------------------------ decode
     def decode_step(self, tokens: torch.Tensor, return_hidden: bool = False):
@@ -165,23 +214,25 @@ class TPDecoder:
         tokens int64 [B] (and the final hidden state [B, H] if asked).  The
         position is the cache's token count."""
         cfg, B, D = self.cfg, self.batch, self.cfg.head_dim
+        eps = cfg.rms_eps
         pos = self.cache.get_total_written()
-        cos, sin = self.cos[pos:pos + 1], self.sin[pos:pos + 1]
-        x = self.embed.index_select(0, tokens)  # [B, H]
+        cos, sin = self.cos[pos], self.sin[pos]
+        x = self.embed.index_select(0, tokens)  # [B, H], updated in place below
+        h = _C.fused_rmsnorm(x, self.layers[0]["in_norm"], eps)
+        n = len(self.layers)
         for li, L in enumerate(self.layers):
-            h = _C.fused_rmsnorm(x, L["in_norm"], cfg.rms_eps)
-            q = self._head_norm(L["q"](h).view(B, self.hq, D), L["q_norm"])
-            k = self._head_norm(L["k"](h).view(B, self.hkv, D), L["k_norm"])
-            v = L["v"](h).view(B, 1, self.hkv, D)
-            q = self._rope(q.view(B, 1, self.hq, D), cos, sin).view(B, self.hq, D)
-            k = self._rope(k.view(B, 1, self.hkv, D), cos, sin)
-            self.cache.append(k, v, li)
+            q = _C.qk_norm_rope_append(L["qkv"](h), self.hq, self.hkv, L["q_norm"], L["k_norm"], eps,
+                                       cos, sin, self.cache.k[li], self.cache.v[li], cfg.sink,
+                                       cfg.window, pos)
             att = _C.decode_attention(q, self.cache.k[li], self.cache.v[li], pos + 1, cfg.sink,
                                       cfg.window)
-            x = x + self._allreduce(L["o"](att.view(B, self.hq * D)))
-            h = _C.fused_rmsnorm(x, L["post_norm"], cfg.rms_eps)
-            x = x + self._mlp(L, h)
-        nxt = self._greedy(x)
+            o = self._allreduce(L["o"](att.view(B, self.hq * D)))
+            h = _C.add_rmsnorm(x, o, L["post_norm"], eps)  # x += o
+            dn = self._mlp(L, h)
+            nxt_w = self.layers[li + 1]["in_norm"] if li + 1 < n else self.final_norm
+            h = _C.add_rmsnorm(x, dn, nxt_w, eps)  # x += down; the next RMSNorm
+        self.cache.advance(1)
+        nxt = self._greedy_normed(h)
         return (nxt, x) if return_hidden else nxt
 
     def _greedy_logits(self, x: torch.Tensor) -> torch.Tensor:
@@ -190,7 +241,11 @@ class TPDecoder:
         return h @ self.lm_head
 
     def _greedy(self, x: torch.Tensor) -> torch.Tensor:
-        logits = self._greedy_logits(x)
+        return self._greedy_normed(_C.fused_rmsnorm(x, self.final_norm, self.cfg.rms_eps))
+
+    def _greedy_normed(self, h: torch.Tensor) -> torch.Tensor:
+        """greedy tokens from the final-normed hidden state"""
+        logits = h @ self.lm_head
         val, idx = logits.float().max(dim=-1)
         idx = idx + self.rank * self.lm_head.size(1)
         if self.world > 1:
@@ -230,9 +285,10 @@ class TPDecoder:
             x = self.embed.index_select(0, tc.reshape(-1)).view(B * n, cfg.hidden)
             for li, L in enumerate(self.layers):
                 h = _C.fused_rmsnorm(x, L["in_norm"], cfg.rms_eps)
-                q = self._head_norm(L["q"](h).view(B * n * self.hq, D), L["q_norm"])
-                k = self._head_norm(L["k"](h).view(B * n * self.hkv, D), L["k_norm"])
-                v = L["v"](h).view(B, n, self.hkv, D)
+                qp, kp, vp = L["qkv"](h).split(L["qkv"].splits, dim=-1)
+                q = self._head_norm(qp.reshape(B * n * self.hq, D), L["q_norm"])
+                k = self._head_norm(kp.reshape(B * n * self.hkv, D), L["k_norm"])
+                v = vp.reshape(B, n, self.hkv, D).contiguous()
                 q = self._rope(q.view(B, n, self.hq, D), cos, sin)
                 k = self._rope(k.view(B, n, self.hkv, D), cos, sin)
                 if c > 0:

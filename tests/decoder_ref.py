@@ -1,6 +1,8 @@
 """fp32 torch restatement of the tensor-parallel decoder's math (TP = 1) for the
 decoder tests: dequantised weights from the oracle, explicit sink + window
-attention over the full key history, no library kernels."""
+attention over the full key history, no library kernels.  The fused q|k|v and
+gate|up linears are evaluated as one product and split (their LoRA B is
+block-diagonal, so each part equals its own linear)."""
 
 from __future__ import annotations
 
@@ -17,8 +19,7 @@ def _dense(lin, device):
                         lin.group)
     A = lin.lora_A.float().to(device)
     B = lin.lora_B.float().to(device)
-    r = A.size(1)
-    return torch.from_numpy(np.asarray(W, dtype=np.float32)).to(device), A, B, float(lin.alpha) / r
+    return torch.from_numpy(np.asarray(W, dtype=np.float32)).to(device), A, B, float(lin.lora_scale)
 
 
 class RefDecoder:
@@ -29,8 +30,9 @@ class RefDecoder:
         self.layers = []
         for L in dec.layers:
             R = {k: f(L[k]) for k in ("in_norm", "post_norm", "q_norm", "k_norm")}
-            for k in ("q", "k", "v", "o", "gate", "up", "down"):
+            for k in ("qkv", "o", "gate_up", "down"):
                 R[k] = _dense(L[k], self.dev)
+            R["qkv_splits"], R["gate_up_splits"] = L["qkv"].splits, L["gate_up"].splits
             self.layers.append(R)
         self.cos, self.sin = dec.cos, dec.sin
         self.hq, self.hkv = dec.hq, dec.hkv
@@ -59,9 +61,10 @@ class RefDecoder:
         B, D = x.size(0), cfg.head_dim
         for li, L in enumerate(self.layers):
             h = self._rms(x, L["in_norm"])
-            q = self._rms(self._lin(h, L["q"]).view(B, self.hq, D), L["q_norm"])
-            k = self._rms(self._lin(h, L["k"]).view(B, self.hkv, D), L["k_norm"])
-            v = self._lin(h, L["v"]).view(B, self.hkv, D)
+            q_, k_, v_ = self._lin(h, L["qkv"]).split(L["qkv_splits"], dim=-1)
+            q = self._rms(q_.reshape(B, self.hq, D), L["q_norm"])
+            k = self._rms(k_.reshape(B, self.hkv, D), L["k_norm"])
+            v = v_.reshape(B, self.hkv, D)
             q, k = self._rope(q, p), self._rope(k, p)
             self.kh[li].append((p, k, v))
             keep = [(kp, kk, vv) for kp, kk, vv in self.kh[li]
@@ -75,7 +78,7 @@ class RefDecoder:
             a = torch.einsum("bhl,blhd->bhd", sc.softmax(-1), V).reshape(B, self.hq * D)
             x = x + self._lin(a, L["o"])
             h = self._rms(x, L["post_norm"])
-            g, u = self._lin(h, L["gate"]), self._lin(h, L["up"])
+            g, u = self._lin(h, L["gate_up"]).split(L["gate_up_splits"], dim=-1)
             x = x + self._lin(g * torch.sigmoid(g) * u, L["down"])
         self.count += 1
         return x

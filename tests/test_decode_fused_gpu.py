@@ -1,0 +1,74 @@
+"""Fused decode-step kernels against the unfused operator sequence they
+replace: residual add + RMSNorm and packed SwiGLU bit-exact; q/k head norm +
+RoPE + ring append against the head-norm kernel followed by the fp32 torch
+rotation (within one fp16 ulp: the two sum-of-squares reductions run in
+different orders)."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def C():
+    assert torch.cuda.is_available(), "GPU test run without a GPU"
+    from qextract_infer_b200 import _C
+    return _C
+
+
+def _g(seed):
+    return torch.Generator(device="cuda").manual_seed(seed)
+
+
+@pytest.mark.parametrize("rows,H", [(1, 4096), (3, 2560), (32, 4096), (2, 512), (5, 8192), (4, 200)])
+def test_add_rmsnorm_bit_exact(C, rows, H):
+    x = torch.randn(rows, H, generator=_g(rows + H), device="cuda").half()
+    d = torch.randn(rows, H, generator=_g(rows * H), device="cuda").half()
+    w = (1 + 0.1 * torch.randn(H, generator=_g(7), device="cuda")).half()
+    x_ref = (x.float() + d.float()).half()  # torch's fp16 add
+    y_ref = C.fused_rmsnorm(x_ref, w, 1e-6)
+    xx = x.clone()
+    y = C.add_rmsnorm(xx, d, w, 1e-6)
+    assert torch.equal(xx.view(torch.int16), x_ref.view(torch.int16))
+    assert torch.equal(y.view(torch.int16), y_ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("rows,inter", [(1, 12288), (32, 3072), (3, 8), (7, 1536)])
+def test_swiglu_packed_bit_exact(C, rows, inter):
+    gu = torch.randn(rows, 2 * inter, generator=_g(rows + inter), device="cuda").half()
+    ref = C.fused_swiglu(gu[:, :inter].contiguous(), gu[:, inter:].contiguous())
+    out = C.swiglu_packed(gu)
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
+def _rope_ref(x, cos, sin):
+    xf = x.float()
+    half = x.size(-1) // 2
+    rot = torch.cat([-xf[..., half:], xf[..., :half]], dim=-1)
+    return (xf * cos + rot * sin).half()
+
+
+@pytest.mark.parametrize("B,hq,hkv,D,pos", [(1, 32, 8, 128, 5), (32, 4, 1, 128, 8191), (3, 8, 2, 64, 2),
+                                            (2, 4, 2, 256, 4100)])
+def test_qk_norm_rope_append(C, B, hq, hkv, D, pos):
+    sink, window = 4, 60
+    qkv = torch.randn(B, (hq + 2 * hkv) * D, generator=_g(B + hq + D), device="cuda").half()
+    qn = (1 + 0.1 * torch.randn(D, generator=_g(1), device="cuda")).half()
+    kn = (1 + 0.1 * torch.randn(D, generator=_g(2), device="cuda")).half()
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, device="cuda", dtype=torch.float32) / D))
+    ang = pos * inv
+    cos, sin = torch.cat([ang.cos(), ang.cos()]), torch.cat([ang.sin(), ang.sin()])
+    kc = torch.zeros(B, sink + window, hkv, D, dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    q = C.qk_norm_rope_append(qkv, hq, hkv, qn, kn, 1e-6, cos, sin, kc, vc, sink, window, pos)
+    qp, kp, vp = qkv.split([hq * D, hkv * D, hkv * D], dim=-1)
+    q_ref = _rope_ref(C.fused_rmsnorm(qp.reshape(B * hq, D).contiguous(), qn, 1e-6).view(B, hq, D), cos, sin)
+    k_ref = _rope_ref(C.fused_rmsnorm(kp.reshape(B * hkv, D).contiguous(), kn, 1e-6).view(B, hkv, D), cos, sin)
+    slot = pos if pos < sink else sink + (pos - sink) % window
+    torch.testing.assert_close(q.float(), q_ref.float(), rtol=2e-3, atol=2e-3)
+    torch.testing.assert_close(kc[:, slot].float(), k_ref.float(), rtol=2e-3, atol=2e-3)
+    assert torch.equal(vc[:, slot], vp.reshape(B, hkv, D))
+    others = torch.ones(sink + window, dtype=torch.bool)
+    others[slot] = False
+    assert not kc[:, others].any() and not vc[:, others].any()

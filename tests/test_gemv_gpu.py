@@ -132,7 +132,8 @@ def test_input_shapes(C):
     y1 = C.w4a16_lora_gemv(t["x"][0], t["qweight"], t["scales"], t["zeros"], t["lora_A"],
                            t["lora_B"])
     assert tuple(y1.shape) == (128,)
-    np.testing.assert_array_equal(to_np(y1).view(np.uint16), to_np(y.reshape(6, 128)[0]).view(np.uint16))
+    # same row through a batched call (another kernel for larger batches): tolerance, not bits
+    assert_close(to_np(y1), to_np(y.reshape(6, 128)[0]), RTOL, ATOL, "row 0 alone vs in a batch")
     empty = C.w4a16_gemv(t["x"][:0], t["qweight"], t["scales"], t["zeros"])
     assert tuple(empty.shape) == (0, 128)
 
