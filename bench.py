@@ -566,12 +566,7 @@ def run_decode_tp(args):
         step_ms = ms / decode_steps
         # bytes one decode step reads per rank: int4 weights + scales/qzeros + LoRA, lm_head
         # shard, and the ring (all layers, this rank's KV heads, every sequence)
-        wbytes = 0
-        for L in dec.layers:
-            for k in ("q", "k", "v", "o", "gate", "up", "down"):
-                lin = L[k]
-                wbytes += sum(t.numel() * t.element_size() for t in
-                              (lin.qweight, lin.scales, lin.qzeros, lin.lora_A, lin.lora_B))
+        wbytes = sum(L[k].weight_bytes() for L in dec.layers for k in ("qkv", "o", "gate_up", "down"))
         wbytes += dec.lm_head.numel() * 2
         kvbytes = 2 * cfg.num_layers * B * (cfg.sink + cfg.window) * dec.hkv * cfg.head_dim * 2
         per_rank_gbs = (wbytes + kvbytes) / (step_ms / 1e3) / 1e9

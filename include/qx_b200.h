@@ -65,7 +65,7 @@ const char* qx_version(void);
  *   lora_scale  = lora_alpha / rank   (the reference computes it at w4a16_lora_gemv.cu:221)
  *   y        fp16  [M, N]
  * Constraints: K % 32 == 0, group_size % 32 == 0, K % group_size == 0,
- * N % 8 == 0, rank in {0, 8, 16, 32, 64, 128}; x, qweight, scales, lora_A,
+ * N % 8 == 0, rank in {0, 8, 16, 32, 48, 64, 128}; x, qweight, scales, lora_A,
  * lora_B (and fp16 zeros) 16-byte aligned.
  * Any M >= 1 (rows are processed 32 at a time).
  * No workspace: each group of CTAs that splits K forms a thread-block cluster
@@ -97,7 +97,7 @@ int qx_set_pdl(int enable);
  * (128 x 256 output tiles, TMA-fed, int4 dequantised in shared memory,
  * accumulator in TMEM, LoRA term added on the tensor cores).
  * Constraints: N % 256 == 0, K % 64 == 0, group_size in {32, 64, 128, 256},
- * rank in {0, 8, 16, 32, 64}; every tensor and the workspace 16-byte aligned.
+ * rank in {0, 8, 16, 32, 48, 64}; every tensor and the workspace 16-byte aligned.
  * workspace: qx_w4a16_lora_gemm_sm100_workspace_size(M, rank) bytes (the scaled
  * LoRA down-projection as fp16 high and low parts);
  * its contents need no initialisation.

@@ -29,7 +29,7 @@ __all__ = ["fused_rmsnorm", "fused_swiglu", "w4a16_gemv", "w4a16_lora_gemv",
            "RingBufferKVCache", "decode_attention", "ring_slot_indices"]
 
 _LIB = _lib.load()  # fail at import time if the native library is absent
-_SUPPORTED_RANKS = (8, 16, 32, 64, 128)
+_SUPPORTED_RANKS = (8, 16, 32, 48, 64, 128)
 
 
 def _check_input(t: torch.Tensor, name: str):

@@ -519,8 +519,8 @@ extern "C" int qx_w4a16_lora_gemm_sm100(const void* x, const int32_t* qweight, c
   QX_REQUIRE((group_size == 32 || group_size == 64 || group_size == 128 || group_size == 256) &&
                  K % group_size == 0,
              "w4a16_gemm: group_size=%d must be 32, 64, 128 or 256 and divide K=%d", group_size, K);
-  QX_REQUIRE(rank == 0 || rank == 8 || rank == 16 || rank == 32 || rank == 64,
-             "w4a16_gemm: LoRA rank %d unsupported (0, 8, 16, 32 or 64)", rank);
+  QX_REQUIRE(rank == 0 || rank == 8 || rank == 16 || rank == 32 || rank == 48 || rank == 64,
+             "w4a16_gemm: LoRA rank %d unsupported (0, 8, 16, 32, 48 or 64)", rank);
   QX_REQUIRE(x && qweight && scales && zeros && y, "w4a16_gemm: null tensor pointer");
   QX_REQUIRE(rank == 0 || (lora_A && lora_B), "w4a16_gemm: rank=%d but lora_A/lora_B missing", rank);
   QX_REQUIRE(aligned(x, 16) && aligned(qweight, 16) && aligned(scales, 16) && aligned(zeros, 16) &&

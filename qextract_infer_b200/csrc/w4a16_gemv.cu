@@ -37,8 +37,10 @@
 //               Sx = Xa + Xb,  Xa / Xb = sums of x over the two nibble classes,
 //             and Off / Sx come from a second MMA of the same activation
 //             fragments against a constant matrix (rows 1024|64 and 1|1).
-//   LoRA    = the helper computes h_s = x[:, Ks] A[Ks, :] on the tensor cores
-//             (ldmatrix.trans of the staged A slice); the LoRA product is
+//   LoRA    = h_s = x[:, Ks] A[Ks, :] on the tensor cores (ldmatrix.trans
+//             of the staged A slice): by the helper while the compute warps
+//             stream the weights for up to 8 rows and ranks below 32, else by
+//             the compute warps (tiles split over the 8 warps); the LoRA product is
 //             linear in K, so each CTA adds (alpha/r) h_s B[:, tile] into its
 //             own partial sums and no h is exchanged.
 //   reduce  = each CTA sends its fp32 partial of the columns owned by CTA j
@@ -123,6 +125,18 @@ __host__ __device__ inline int xstride(int Ts_max) { return Ts_max * KSTEP + 8; 
 // columns each CTA of an S-cluster finalises: 256 / S rounded up to 8
 __host__ __device__ inline int owner_cols(int S) { return ((COLS + S - 1) / S + 7) / 8 * 8; }
 
+// LoRA down-projection on the compute warps for batches above 8 rows or
+// ranks of 32 and more, as (16-row block, 8-rank block) tiles split into k
+// parts so that each warp has an item; else the helper warp computes it while
+// the compute warps stream the weights.
+__host__ __device__ inline bool lora_on_warps(int M, int rank) { return rank > 0 && (M > 8 || rank >= 32); }
+__host__ __device__ inline int lora_tiles(int M, int rank) { return ((M + 15) / 16) * (rank / 8); }
+__host__ __device__ inline int lora_kparts(int M, int rank) {
+  if (!lora_on_warps(M, rank)) return 1;
+  const int t = lora_tiles(M, rank);
+  return t >= WARPS ? 1 : WARPS / t;
+}
+
 // M = batch rows of this launch (<= 32).
 __host__ __device__ inline Layout layout(int M, int KPG, int Ts_max, int rank, int S, int nst,
                                          int zeros_packed) {
@@ -140,7 +154,7 @@ __host__ __device__ inline Layout layout(int M, int KPG, int Ts_max, int rank, i
   L.xks = take(o, size_t(gmax) * Mp * 2 * 4);         // per group (Off, Sx) per row [g][Mp]
   L.As = take(o, size_t(Ts_max) * KSTEP * rank * 2);  // LoRA A slice [Ks][r]
   L.Bs = take(o, size_t(rank) * COLS * 2);            // LoRA B tile [r][256]
-  L.hs = take(o, size_t(M) * rank * 4);               // h_s [M][r]
+  L.hs = take(o, size_t(lora_kparts(M, rank)) * M * rank * 4);  // h_s [parts][M][r]
   L.recv = take(o, size_t(S) * M * owner_cols(S) * 4);  // partials from the cluster [S][M][cpr]
   L.total = o;
   return L;
@@ -157,6 +171,12 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
   const unsigned a = static_cast<unsigned>(__cvta_generic_to_shared(p));
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t (&r)[2], const void* p) {
+  const unsigned a = static_cast<unsigned>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1])
                : "r"(a));
 }
 __device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void* p) {
@@ -428,8 +448,9 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   }
   __syncthreads();  // permuted activations, group sums, scales ready
 
-  if (warp == WARPS) {  // helper: the LoRA down-projection
-    if (R == 0) return;
+  const bool lora_warps = lora_on_warps(M, R);
+  if (warp == WARPS) {  // helper: the LoRA down-projection of small batches and ranks
+    if (R == 0 || lora_warps) return;
     __half* As = reinterpret_cast<__half*>(smem + L.As);
     float* hs = reinterpret_cast<float*>(smem + L.hs);
     // LoRA down-projection h_s^T[r][m] = A^T[r][Ks] . x^T[Ks][m]: 16 x 8 tiles
@@ -477,6 +498,36 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   }
 
   // ---------------- compute warps ----------------
+  const int KP = lora_kparts(M, R);  // h_s partial sums (1: the helper's complete h_s)
+  if (lora_warps) {
+    // LoRA down-projection h_s = x[:, Ks] A[Ks, :] on the compute warps:
+    // C[16 rows][8 ranks] tiles (mma.sync), each split into KP interleaved k
+    // parts (k16 blocks), item w = (tile, part) on warp w % 8; partial sums to
+    // hs[part][row][rank], summed in part order where the LoRA term is applied
+    const __half* As = reinterpret_cast<const __half*>(smem + L.As);
+    float* hp = reinterpret_cast<float*>(smem + L.hs);
+    const int RT8 = R >> 3, ntl = lora_tiles(M, R), KB = Ks >> 4;
+    for (int w = warp; w < ntl * KP; w += WARPS) {
+      const int tl = w % ntl, kp = w / ntl;
+      const int mt = tl / RT8, rt = tl - mt * RT8;
+      const int m0 = mt * 16 + g, m1 = m0 + 8;
+      const __half* x0 = xraw + (m0 < M ? m0 : 0) * XS + 2 * c;
+      const __half* x1 = xraw + (m1 < M ? m1 : 0) * XS + 2 * c;
+      float h[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int kb = kp; kb < KB; kb += KP) {
+        const uint32_t a0 = m0 < M ? *reinterpret_cast<const uint32_t*>(x0 + kb * 16) : 0u;
+        const uint32_t a2 = m0 < M ? *reinterpret_cast<const uint32_t*>(x0 + kb * 16 + 8) : 0u;
+        const uint32_t a1 = m1 < M ? *reinterpret_cast<const uint32_t*>(x1 + kb * 16) : 0u;
+        const uint32_t a3 = m1 < M ? *reinterpret_cast<const uint32_t*>(x1 + kb * 16 + 8) : 0u;
+        uint32_t bf[2];
+        ldsm_x2_t(bf, As + (kb * 16 + (lane & 15)) * R + rt * 8);
+        mma_16816(h, a0, a1, a2, a3, bf[0], bf[1]);
+      }
+      float* dst = hp + size_t(kp) * M * R + rt * 8 + 2 * c;
+      if (m0 < M) *reinterpret_cast<float2*>(dst + m0 * R) = make_float2(h[0], h[1]);
+      if (m1 < M) *reinterpret_cast<float2*>(dst + m1 * R) = make_float2(h[2], h[3]);
+    }
+  }
   const int lcol = warp * 32 + 4 * g;  // first of this lane's 4 columns (tile-local)
   const bool col_ok = n_tile0 + lcol < N;  // N % 8 == 0: all 4 columns valid or none
   const uint4* xs = reinterpret_cast<const uint4*>(smem + L.xs);
@@ -571,7 +622,10 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   // (alpha/r) h_s^T split into fp16 high and low parts (~22-bit product)
   if (R > 0) {
     const int RT = R >= 16 ? R / 16 : 1;
-    mbar_wait(bar_h, 0);
+    if (lora_warps)
+      asm volatile("bar.sync 1, %0;" ::"n"(WARPS * 32) : "memory");  // every warp's h_s partials
+    else
+      mbar_wait(bar_h, 0);
     mbar_wait(bar_b, 0);
     const float* hs = reinterpret_cast<const float*>(smem + L.hs);
     const __half* Bs = reinterpret_cast<const __half*>(smem + L.Bs);
@@ -583,8 +637,17 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
         const int m = nt * 8 + g;
         float2 h0 = make_float2(0.f, 0.f), h1 = make_float2(0.f, 0.f);
         if (m < M) {
-          h0 = *reinterpret_cast<const float2*>(hs + m * R + j);
-          if (R >= 16) h1 = *reinterpret_cast<const float2*>(hs + m * R + j + 8);
+          for (int kp = 0; kp < KP; ++kp) {  // partial sums in part order
+            const float* hk = hs + (size_t(kp) * M + m) * R + j;
+            const float2 u = *reinterpret_cast<const float2*>(hk);
+            h0.x += u.x;
+            h0.y += u.y;
+            if (R >= 16) {
+              const float2 u8 = *reinterpret_cast<const float2*>(hk + 8);
+              h1.x += u8.x;
+              h1.y += u8.y;
+            }
+          }
         }
         const float ls = p.lora_scale;
         const __half2 h0h = __floats2half2_rn(ls * h0.x, ls * h0.y);
@@ -911,8 +974,9 @@ extern "C" int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const v
                  K % group_size == 0,
              "w4a16_gemv: group_size=%d must be 32, 64, 128 or 256 and divide K=%d", group_size, K);
   QX_REQUIRE(N % 8 == 0, "w4a16_gemv: N=%d must be a multiple of 8", N);
-  QX_REQUIRE(rank == 0 || rank == 8 || rank == 16 || rank == 32 || rank == 64 || rank == 128,
-             "w4a16_gemv: LoRA rank %d unsupported (0, 8, 16, 32, 64 or 128)", rank);
+  QX_REQUIRE(rank == 0 || rank == 8 || rank == 16 || rank == 32 || rank == 48 || rank == 64 ||
+                 rank == 128,
+             "w4a16_gemv: LoRA rank %d unsupported (0, 8, 16, 32, 48, 64 or 128)", rank);
   QX_REQUIRE(x && qweight && scales && zeros && y, "w4a16_gemv: null tensor pointer");
   QX_REQUIRE(rank == 0 || (lora_A && lora_B), "w4a16_gemv: rank=%d but lora_A/lora_B missing",
              rank);

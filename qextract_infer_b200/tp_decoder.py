@@ -98,6 +98,11 @@ class ShardedQuantLinear:
         return _C._w4a16(x, self.qweight, self.scales, self.qzeros, self.lora_A, self.lora_B,
                          self.group, self.lora_scale, 0)
 
+    def weight_bytes(self) -> int:
+        """bytes of the operands one call reads (int4 weights, scales, qzeros, LoRA A and B)"""
+        return sum(t.numel() * t.element_size()
+                   for t in (self.qweight, self.scales, self.qzeros, self.lora_A, self.lora_B))
+
 
 class FusedQuantLinear:
     """Column-parallel linears that read the same input, as one W4A16-LoRA
@@ -126,6 +131,12 @@ class FusedQuantLinear:
             r0, n0 = r0 + r, n0 + p.N
         self.lora_A, self.lora_B = A, B
         self.group, self.lora_scale = parts[0].group, parts[0].lora_scale
+        self._bytes = sum(p.weight_bytes() for p in parts)  # the parts' own operands (no padding)
+
+    def weight_bytes(self) -> int:
+        """algorithmic bytes of one call: the parts' operands (the zero padding of
+        the fused LoRA factors is not counted)"""
+        return self._bytes
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         return _C._w4a16(x, self.qweight, self.scales, self.qzeros, self.lora_A, self.lora_B,
@@ -134,7 +145,7 @@ class FusedQuantLinear:
 
 def _padded_rank(r: int) -> int:
     """smallest LoRA rank the kernels take that holds r"""
-    for s in (8, 16, 32, 64, 128):
+    for s in (8, 16, 32, 48, 64, 128):
         if s >= r:
             return s
     raise ValueError(f"fused LoRA rank {r} > 128")

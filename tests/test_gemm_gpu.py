@@ -55,7 +55,7 @@ def _run(C, d, group, alpha, rank, zero_offset=0):
 
 @pytest.mark.parametrize("M,K,N,rank,group", [
     (128, 256, 256, 16, 128), (300, 512, 512, 64, 128), (256, 1024, 768, 0, 128),
-    (256, 512, 256, 8, 64), (192, 512, 512, 32, 32), (129, 256, 256, 16, 256),
+    (256, 512, 256, 8, 64), (192, 512, 512, 32, 32), (129, 256, 256, 16, 256), (256, 512, 768, 48, 128),
 ])
 def test_against_oracle(C, M, K, N, rank, group):
     d = _inputs(M, K, N, rank, group, seed=M + K + N, random_zeros=True)
