@@ -585,6 +585,7 @@ def run_decode_tp(args):
         if rank == 0:
             print(json.dumps(line), flush=True)
         del graphs, g
+        dec.close()
         del dec, k0, v0
         torch.cuda.empty_cache()
     if world > 1:

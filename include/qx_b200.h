@@ -43,6 +43,8 @@ const char* qx_last_error(void);
  * GPU (the kernel then finishes with undefined output).  New component: the
  * reference has no device-side error reporting. */
 #define QX_DEVERR_MBAR_TIMEOUT 1u
+/* a peer rank's flag did not arrive within ~2 s (qx_nvlink_ar_add_rmsnorm) */
+#define QX_DEVERR_PEER_TIMEOUT 2u
 /* Reads (and with reset != 0 clears) the sticky error bits of the current
  * device; synchronises with the device. */
 int qx_get_device_error(unsigned* code, int reset);
@@ -137,6 +139,29 @@ int qx_qk_norm_rope_append(const void* qkv, int batch, int q_heads, int kv_heads
                            const float* cos_row, const float* sin_row, void* q_out, void* k_cache,
                            void* v_cache, int sink, int window, int64_t pos, qx_stream_t stream);
 int qx_swiglu_packed(const void* gate_up, void* y, int64_t rows, int inter, qx_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * One-shot all-reduce over NVLink peer memory fused with the residual add and
+ * RMSNorm after the row-parallel projections of the tensor-parallel decode
+ * step (new component; NCCL's all-reduce is the baseline it replaces):
+ *   x[r] <- fp16(x[r] + fp16(sum over ranks of partial[r]))  (in place)
+ *   y[r]  = fp16((x[r] * rsqrt(mean(x[r]^2) + eps)) * w)
+ * Every rank computes identical bits (rank-ordered fp32 sum).
+ * Setup, on every rank of one node (one GPU per rank): qx_nvlink_ar_create
+ * allocates this rank's shared buffer (2 x max_rows x hidden fp16 + flags; the
+ * only allocation in the library) and writes its IPC handle
+ * (qx_nvlink_ar_handle_bytes() bytes) to handle_out; exchange the handles
+ * (all-gather, rank order) and call qx_nvlink_ar_open with all of them; then
+ * a barrier before the first call.  Calls: every rank makes the same sequence
+ * of calls; calls on one rank must not overlap (stream order).  A peer that
+ * does not arrive within ~2 s sets QX_DEVERR_PEER_TIMEOUT.
+ * ---------------------------------------------------------------------- */
+size_t qx_nvlink_ar_handle_bytes(void);
+int qx_nvlink_ar_create(int world, int rank, int max_rows, int hidden, void** ctx, void* handle_out);
+int qx_nvlink_ar_open(void* ctx, const void* handles);
+int qx_nvlink_ar_add_rmsnorm(void* ctx, const void* partial, void* x, const void* weight, void* y,
+                             int rows, float eps, qx_stream_t stream);
+int qx_nvlink_ar_destroy(void* ctx);
 
 /* ------------------------------------------------------------------------
  * Fused RMSNorm.  Replaces fused_rmsnorm() (csrc/kernels/rmsnorm.cu:162-210,

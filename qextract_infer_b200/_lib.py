@@ -40,6 +40,12 @@ SIGNATURES = {
                                        c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                        c_int, c_int, c_int64, c_void_p]),
     "qx_swiglu_packed": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_void_p]),
+    "qx_nvlink_ar_handle_bytes": (c_size_t, []),
+    "qx_nvlink_ar_create": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "qx_nvlink_ar_open": (c_int, [c_void_p, c_void_p]),
+    "qx_nvlink_ar_add_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                         c_float, c_void_p]),
+    "qx_nvlink_ar_destroy": (c_int, [c_void_p]),
     "qx_ring_append": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                c_int, c_int, c_int64, c_void_p]),
     "qx_ring_slot_indices": (c_int64, [c_void_p, c_int, c_int, c_int64, c_void_p]),

@@ -939,6 +939,7 @@ using namespace qx;
 
 namespace qx {
 int gemm_device_error(unsigned* code, int reset);  // w4a16_gemm.cu
+int nvar_device_error(unsigned* code, int reset);  // nvlink_allreduce.cu
 }
 
 extern "C" int qx_get_device_error(unsigned* code, int reset) {
@@ -951,7 +952,10 @@ extern "C" int qx_get_device_error(unsigned* code, int reset) {
                 "get_device_error: reset");
   }
   unsigned other = 0;
-  const int rc = qx::gemm_device_error(&other, reset);
+  int rc = qx::gemm_device_error(&other, reset);
+  if (rc != QX_OK) return rc;
+  *code |= other;
+  rc = qx::nvar_device_error(&other, reset);
   if (rc != QX_OK) return rc;
   *code |= other;
   return QX_OK;

@@ -18,12 +18,14 @@ NCCL):
 The projections that read the same input are fused: q|k|v and gate|up are
 each one W4A16-LoRA call (weights side by side, LoRA A side by side, LoRA B
 block-diagonal, rank zero-padded to a supported size: the same math).  Per
-decode step and layer (9 launches + 2 all-reduces): qkv GEMV -> per-head
-RMSNorm of q and k (Qwen3), RoPE (theta 1e6, keys stored post-RoPE at their
-absolute positions) and the ring append in one kernel -> GQA decode attention
-over sink + window (including the new token) -> o GEMV -> all-reduce ->
-residual add + RMSNorm in one kernel -> gate|up GEMV -> SwiGLU -> down GEMV ->
-all-reduce -> residual add + the next RMSNorm in one kernel.  Prefill chunks
+decode step and layer (9 launches): qkv GEMV -> per-head RMSNorm of q and k
+(Qwen3), RoPE (theta 1e6, keys stored post-RoPE at their absolute positions)
+and the ring append in one kernel -> GQA decode attention over sink + window
+(including the new token) -> o GEMV -> all-reduce + residual add + RMSNorm in
+one kernel -> gate|up GEMV -> SwiGLU -> down GEMV -> all-reduce + residual add
++ the next RMSNorm in one kernel.  With more than one rank the all-reduce is a
+one-shot exchange over NVLink peer memory inside that kernel
+(``nvlink_allreduce.py``); prefill chunks all-reduce with NCCL.  Prefill chunks
 run the same projections with the tensor-core GEMM; their attention (each
 query over the sinks, the previous window and the causal part of its chunk)
 uses torch's scaled_dot_product_attention.
@@ -153,7 +155,7 @@ def _padded_rank(r: int) -> int:
 
 class TPDecoder:
     def __init__(self, cfg: DecoderConfig, batch: int, device, seed: int = 4,
-                 group: dist.ProcessGroup | None = None):
+                 group: dist.ProcessGroup | None = None, nvlink_allreduce: bool = True):
         self.cfg, self.batch, self.device = cfg, batch, torch.device(device)
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -199,12 +201,30 @@ class TPDecoder:
         ang = torch.arange(self.max_pos, device=dev, dtype=torch.float32)[:, None] * inv[None, :]
         self.cos = torch.cat([ang.cos(), ang.cos()], dim=-1)  # [pos, D]
         self.sin = torch.cat([ang.sin(), ang.sin()], dim=-1)
+        # decode steps (batch rows) all-reduce through NVLink peer memory fused with the
+        # residual add and RMSNorm; prefill chunks use NCCL
+        self.ar = None
+        if self.world > 1 and nvlink_allreduce:
+            from .nvlink_allreduce import NVLinkAllReduce
+            self.ar = NVLinkAllReduce(group if group is not None else dist.group.WORLD, batch, H, dev)
+
+    def close(self) -> None:
+        """release the NVLink all-reduce buffers (collective: call on every rank)"""
+        if self.ar is not None:
+            self.ar.close()
+            self.ar = None
 
     # ------------------------------------------------------------------ pieces
     def _allreduce(self, t: torch.Tensor) -> torch.Tensor:
         if self.world > 1:
             dist.all_reduce(t, group=self.group)
         return t
+
+    def _reduce_add_norm(self, partial: torch.Tensor, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """x += all_reduce(partial) in place; returns rmsnorm(x) * w"""
+        if self.ar is not None:
+            return self.ar.add_rmsnorm(partial, x, w, self.cfg.rms_eps)
+        return _C.add_rmsnorm(x, self._allreduce(partial), w, self.cfg.rms_eps)
 
     def _rope(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
         """x [..., T, heads, D] fp16; cos/sin [T, D] fp32 -> rotated fp16 (HF rotate_half)."""
@@ -237,11 +257,10 @@ class TPDecoder:
                                        cfg.window, pos)
             att = _C.decode_attention(q, self.cache.k[li], self.cache.v[li], pos + 1, cfg.sink,
                                       cfg.window)
-            o = self._allreduce(L["o"](att.view(B, self.hq * D)))
-            h = _C.add_rmsnorm(x, o, L["post_norm"], eps)  # x += o
-            dn = self._mlp(L, h)
+            h = self._reduce_add_norm(L["o"](att.view(B, self.hq * D)), x, L["post_norm"])  # x += o
+            dn = L["down"](_C.swiglu_packed(L["gate_up"](h)))
             nxt_w = self.layers[li + 1]["in_norm"] if li + 1 < n else self.final_norm
-            h = _C.add_rmsnorm(x, dn, nxt_w, eps)  # x += down; the next RMSNorm
+            h = self._reduce_add_norm(dn, x, nxt_w)  # x += down; the next RMSNorm
         self.cache.advance(1)
         nxt = self._greedy_normed(h)
         return (nxt, x) if return_hidden else nxt

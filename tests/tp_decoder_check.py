@@ -48,8 +48,15 @@ def main():
         ok &= e <= 1e-2 * xr.abs().max().item() + 1e-2
         err = max(err, e)
     print(f"rank {dist.get_rank()} world {world}: max err {err:.4g} ok={ok}", flush=True)
+    import ctypes
+    from qextract_infer_b200 import _lib
+    code = ctypes.c_uint(0)
+    assert _lib.load().qx_get_device_error(ctypes.byref(code), 1) == 0
+    ok &= code.value == 0  # no bounded wait gave up
     t = torch.tensor([0 if ok else 1], device=dev)
     dist.all_reduce(t)
+    dec.close()
+    full.close()
     dist.barrier()
     dist.destroy_process_group()
     sys.exit(int(t.item() != 0))
