@@ -384,43 +384,69 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
   }
 }
 
-// (alpha/r) h = (alpha/r) x[M][K] . A[K][r] in fp32: 64 rows per CTA (4 warps x
-// 16 rows), K in chunks of 64 staged in shared memory, mma.sync m16n8k16;
-// written as fp16 high parts hl[m][0..63] and low parts hl[M + m][0..63]
-// (ranks r..63 zero).
-constexpr int LD_ROWS = 64, LD_K = 64;
-__global__ void __launch_bounds__(128) lora_down_kernel(const __half* __restrict__ x,
-                                                         const __half* __restrict__ A,
-                                                         __half* __restrict__ hl, int M, int K, int R,
-                                                         float scale) {
-  __shared__ __align__(16) __half xs[LD_ROWS][LD_K + 8];
-  __shared__ __align__(16) __half as[LD_K][MAX_RANK + 8];
+// (alpha/r) h = (alpha/r) x[M][K] . A[K][r] in fp32, split over K so that the
+// grid covers the GPU: CTA (128-row block, K slice) runs 8 warps of mma.sync
+// m16n8k16 (16 rows each, one accumulator per 8 ranks) over 32-wide k steps
+// whose x and A tiles are double-buffered by cp.async; fp32 partials go to
+// part[split][M][64].  A second kernel sums the splits in order and writes the
+// scaled result as fp16 high parts hl[m][0..63] and low parts hl[M + m][0..63]
+// (ranks r..63 zero), the tiles the GEMM's LoRA MMAs read.
+constexpr int LS_ROWS = 128, LS_K = 32, LS_THREADS = 256;
+
+__host__ __device__ inline int lora_splits(int M) {  // K splits: about two CTAs per SM of 148
+  const int rb = (M + LS_ROWS - 1) / LS_ROWS;
+  const int ks = (2 * 148 + rb - 1) / rb;
+  return ks < 1 ? 1 : (ks > 64 ? 64 : ks);
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(LS_THREADS) lora_down_split_kernel(const __half* __restrict__ x,
+                                                                     const __half* __restrict__ A,
+                                                                     float* __restrict__ part, int M,
+                                                                     int K, int R, int kchunk) {
+  __shared__ __align__(128) __half xs[2][LS_ROWS][LS_K + 8];
+  __shared__ __align__(128) __half as[2][LS_K][MAX_RANK + 8];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int r0 = blockIdx.x * LD_ROWS;
-  const int NT = (R + 7) / 8;  // n-tiles of 8 ranks
+  const int r0 = blockIdx.x * LS_ROWS;
+  const int k0 = blockIdx.y * kchunk, k1 = min(K, k0 + kchunk);
+  const int nsteps = (k1 - k0) / LS_K;
+  const int NT = R / 8;
   float acc[MAX_RANK / 8][4];
 #pragma unroll
   for (int i = 0; i < MAX_RANK / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-  for (int k0 = 0; k0 < K; k0 += LD_K) {
-    for (int it = tid; it < LD_ROWS * (LD_K / 8); it += 128) {
-      const int rr = it / (LD_K / 8), ch = it % (LD_K / 8);
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (r0 + rr < M) v = *reinterpret_cast<const uint4*>(x + size_t(r0 + rr) * K + k0 + ch * 8);
-      *reinterpret_cast<uint4*>(&xs[rr][ch * 8]) = v;
+  auto load = [&](int step, int buf) {
+    const int kb = k0 + step * LS_K;
+    for (int it = tid; it < LS_ROWS * (LS_K / 8); it += LS_THREADS) {
+      const int rr = it >> 2, ch = it & 3, row = r0 + rr;  // rows past M are zero-filled
+      cp_async16(&xs[buf][rr][ch * 8], x + size_t(row < M ? row : 0) * K + kb + ch * 8, row < M ? 16 : 0);
     }
-    for (int it = tid; it < LD_K * (R / 8); it += 128) {
-      const int kk = it / (R / 8), ch = it % (R / 8);
-      *reinterpret_cast<uint4*>(&as[kk][ch * 8]) =
-          *reinterpret_cast<const uint4*>(A + size_t(k0 + kk) * R + ch * 8);
+    for (int it = tid; it < LS_K * NT; it += LS_THREADS) {
+      const int kk = it / NT, ch = it - kk * NT;
+      cp_async16(&as[buf][kk][ch * 8], A + size_t(kb + kk) * R + ch * 8, 16);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (nsteps > 0) load(0, 0);
+  for (int st = 0; st < nsteps; ++st) {
+    if (st + 1 < nsteps) {
+      load(st + 1, (st + 1) & 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
+    const int b = st & 1;
 #pragma unroll
-    for (int kk = 0; kk < LD_K; kk += 16) {
+    for (int kk = 0; kk < LS_K; kk += 16) {
       uint32_t a[4];
       {
-        const int row = warp * 16 + (lane & 15), col = kk + 8 * (lane >> 4);
-        const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(&xs[row][col]));
+        const unsigned sa = smem_u32(&xs[b][warp * 16 + (lane & 15)][kk + 8 * (lane >> 4)]);
         asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
                      : "r"(sa));
@@ -428,32 +454,48 @@ __global__ void __launch_bounds__(128) lora_down_kernel(const __half* __restrict
 #pragma unroll
       for (int nt = 0; nt < MAX_RANK / 8; ++nt) {
         if (nt < NT) {
-          uint32_t b[2];
-          const int krow = kk + (lane & 15);
-          const unsigned sb2 = static_cast<unsigned>(__cvta_generic_to_shared(&as[krow][nt * 8]));
+          uint32_t bb[2];
+          const unsigned sb2 = smem_u32(&as[b][kk + (lane & 15)][nt * 8]);
           asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
-                       : "=r"(b[0]), "=r"(b[1])
+                       : "=r"(bb[0]), "=r"(bb[1])
                        : "r"(sb2));
-          mma_16816(acc[nt], a[0], a[1], a[2], a[3], b[0], b[1]);
+          mma_16816(acc[nt], a[0], a[1], a[2], a[3], bb[0], bb[1]);
         }
       }
     }
-    __syncthreads();
+    __syncthreads();  // the next load overwrites this buffer
   }
-  auto put = [&](int row, int col, float v0, float v1) {
-    const __half2 hi = __floats2half2_rn(scale * v0, scale * v1);
-    const float2 hr = __half22float2(hi);
-    const __half2 lo = __floats2half2_rn(scale * v0 - hr.x, scale * v1 - hr.y);
-    *reinterpret_cast<__half2*>(hl + size_t(row) * MAX_RANK + col) = hi;
-    *reinterpret_cast<__half2*>(hl + (size_t(M) + row) * MAX_RANK + col) = lo;
-  };
+  float* dst = part + size_t(blockIdx.y) * M * MAX_RANK;
 #pragma unroll
   for (int nt = 0; nt < MAX_RANK / 8; ++nt) {
     const bool v = nt < NT;
     const int row = r0 + warp * 16 + g, col = nt * 8 + 2 * c;
-    if (row < M) put(row, col, v ? acc[nt][0] : 0.f, v ? acc[nt][1] : 0.f);
-    if (row + 8 < M) put(row + 8, col, v ? acc[nt][2] : 0.f, v ? acc[nt][3] : 0.f);
+    if (row < M)
+      *reinterpret_cast<float2*>(dst + size_t(row) * MAX_RANK + col) =
+          make_float2(v ? acc[nt][0] : 0.f, v ? acc[nt][1] : 0.f);
+    if (row + 8 < M)
+      *reinterpret_cast<float2*>(dst + size_t(row + 8) * MAX_RANK + col) =
+          make_float2(v ? acc[nt][2] : 0.f, v ? acc[nt][3] : 0.f);
   }
+}
+
+__global__ void __launch_bounds__(256) lora_down_finalize_kernel(const float* __restrict__ part,
+                                                                 __half* __restrict__ hl, int M,
+                                                                 int splits, float scale) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // (row, column pair)
+  if (i >= M * (MAX_RANK / 2)) return;
+  const int row = i / (MAX_RANK / 2), col = (i - row * (MAX_RANK / 2)) * 2;
+  float v0 = 0.f, v1 = 0.f;
+  for (int sp = 0; sp < splits; ++sp) {  // in split order: deterministic
+    const float2 pv = *reinterpret_cast<const float2*>(part + (size_t(sp) * M + row) * MAX_RANK + col);
+    v0 += pv.x;
+    v1 += pv.y;
+  }
+  const __half2 hi = __floats2half2_rn(scale * v0, scale * v1);
+  const float2 hr = __half22float2(hi);
+  const __half2 lo = __floats2half2_rn(scale * v0 - hr.x, scale * v1 - hr.y);
+  *reinterpret_cast<__half2*>(hl + size_t(row) * MAX_RANK + col) = hi;
+  *reinterpret_cast<__half2*>(hl + (size_t(M) + row) * MAX_RANK + col) = lo;
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 encoder() {
@@ -503,8 +545,11 @@ int gemm_device_error(unsigned* code, int reset) {
 using namespace qx;
 
 extern "C" size_t qx_w4a16_lora_gemm_sm100_workspace_size(int M, int rank) {
-  // (alpha/r) h as fp16 high and low parts, [2M][64]
-  return rank > 0 ? size_t(2) * size_t(M) * gemm::MAX_RANK * 2 : 0;
+  // (alpha/r) h as fp16 high and low parts [2M][64], then the fp32 partial sums
+  // of the K splits [splits][M][64]
+  if (rank <= 0 || M <= 0) return 0;
+  return size_t(2) * size_t(M) * gemm::MAX_RANK * 2 +
+         size_t(gemm::lora_splits(M)) * size_t(M) * gemm::MAX_RANK * 4;
 }
 
 extern "C" int qx_w4a16_lora_gemm_sm100(const void* x, const int32_t* qweight, const void* scales,
@@ -581,10 +626,18 @@ extern "C" int qx_w4a16_lora_gemm_sm100(const void* x, const int32_t* qweight, c
   QX_CUDA_TRY(attr_err, "w4a16_gemm: set smem limit");
 
   if (rank > 0) {
-    lora_down_kernel<<<(M + LD_ROWS - 1) / LD_ROWS, 128, 0, st>>>(
-        static_cast<const __half*>(x), static_cast<const __half*>(lora_A),
-        static_cast<__half*>(workspace), M, K, rank, lora_scale);
+    // K slices of whole 32-wide steps, at most lora_splits(M) of them (the workspace size)
+    const int ks_max = lora_splits(M);
+    const int kchunk = ((K + ks_max - 1) / ks_max + LS_K - 1) / LS_K * LS_K;
+    const int splits = (K + kchunk - 1) / kchunk;
+    __half* hl = static_cast<__half*>(workspace);
+    float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + size_t(2) * M * MAX_RANK * 2);
+    lora_down_split_kernel<<<dim3((M + LS_ROWS - 1) / LS_ROWS, splits), LS_THREADS, 0, st>>>(
+        static_cast<const __half*>(x), static_cast<const __half*>(lora_A), part, M, K, rank, kchunk);
     QX_CUDA_TRY(cudaGetLastError(), "w4a16_gemm: lora_down launch");
+    lora_down_finalize_kernel<<<(M * (MAX_RANK / 2) + 255) / 256, 256, 0, st>>>(part, hl, M, splits,
+                                                                             lora_scale);
+    QX_CUDA_TRY(cudaGetLastError(), "w4a16_gemm: lora_down finalize launch");
   }
   dim3 grid(N / BN, (M + BM - 1) / BM);
   w4a16_gemm_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(prm);
