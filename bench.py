@@ -55,6 +55,17 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def gemv_kernel_name():
+    """The kernel qx_w4a16_lora_gemv runs for the decode shape (its own routing)."""
+    import ctypes
+    from qextract_infer_b200 import _lib
+    k = ctypes.c_int(0)
+    _lib.check(_lib.load().qx_w4a16_gemv_route(M, K, N, RANK, GROUP, 1, ctypes.byref(k)),
+               "w4a16_gemv_route")
+    return ("qx::gres::w4a16_gemv_res_kernel<4, 1>" if k.value == 1
+            else "qx::gemv::w4a16_gemv_kernel<1, 4>")
+
+
 def profiled_traffic():
     """dram bytes per launch of the GEMV kernel from the committed ncu summary."""
     p = os.path.join(ROOT, "profiles", "w4a16_gemv_decode.md")
@@ -327,7 +338,7 @@ def run_b200(args):
                          "nominal_frac_8tbs": achieved / 8000.0,
                          "traffic": profiled_traffic(),
                          "algorithmic_bytes_per_launch": BYTES_PER_CALL,
-                         "kernel": "qx::gemv::w4a16_gemv_kernel<1, 4>"},
+                         "kernel": gemv_kernel_name()},
             "e2e": None if not e_steps else {
                     "value": BYTES_PER_CALL * e_steps / (e_ms / 1e3) / 1e9 * world, "unit": "GB/s",
                     "us_per_call": e_ms * 1e3 / e_steps,
