@@ -20,6 +20,9 @@ library is missing or the inputs are not CUDA tensors: there is no CPU path.
 
 from __future__ import annotations
 
+import functools
+import math
+
 import numpy as np
 import torch
 
@@ -47,6 +50,21 @@ def _check_fp16(t: torch.Tensor, name: str):
 
 def _stream(device: torch.device):
     return torch.cuda.current_stream(device)
+
+
+_raw_stream_of = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _raw_stream(device: torch.device) -> int:
+    """cudaStream_t of the current torch stream of ``device`` (no Stream object)."""
+    if _raw_stream_of is not None:
+        return _raw_stream_of(device.index)
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+@functools.lru_cache(maxsize=256)
+def _lora_scale(lora_alpha: float, r: int) -> float:
+    return float(np.float32(lora_alpha) / np.float32(r))  # fp32 division, as w4a16_lora_gemv.cu:221
 
 
 def _ptr(t):
@@ -209,13 +227,13 @@ def _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale
             raise RuntimeError(f"lora_A must be [{K}, r] and lora_B [r, {N}]")
         lora_A, lora_B, rank = _prepare_lora(lora_A, lora_B)
     lead = input.shape[:-1]
-    M = int(np.prod(lead)) if len(lead) else 1
-    out = torch.empty(*lead, N, dtype=torch.float16, device=input.device)
+    M = math.prod(lead)
     dev = input.device
-    st = _stream(dev)
+    out = torch.empty(*lead, N, dtype=torch.float16, device=dev)
     if path == "gemm" or (path is None and M >= GEMM_MIN_ROWS and N % 256 == 0 and K % 64 == 0
                           and rank <= 64):
         # prefill: the tcgen05 tensor-core GEMM
+        st = _stream(dev)
         with torch.cuda.device(dev):
             need = _LIB.qx_w4a16_lora_gemm_sm100_workspace_size(M, rank)
             ws = _workspace.get(dev, st, need, "w4a16_gemm") if need else None
@@ -225,11 +243,14 @@ def _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale
                 int(group_size), float(lora_scale), _ptr(ws), int(need), st.cuda_stream),
                 "w4a16_gemm")
         return out
-    with torch.cuda.device(dev):
-        _lib.check(_LIB.qx_w4a16_lora_gemv(
-            input.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), packed,
+    args = (input.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), packed,
             int(zero_offset), _ptr(lora_A), _ptr(lora_B), out.data_ptr(), M, K, N, rank,
-            int(group_size), float(lora_scale), st.cuda_stream), "w4a16_gemv")
+            int(group_size), float(lora_scale))
+    if dev.index == torch.cuda.current_device():  # the decode hot path: no device switch
+        _lib.check(_LIB.qx_w4a16_lora_gemv(*args, _raw_stream(dev)), "w4a16_gemv")
+    else:
+        with torch.cuda.device(dev):
+            _lib.check(_LIB.qx_w4a16_lora_gemv(*args, _raw_stream(dev)), "w4a16_gemv")
     return out
 
 
@@ -243,8 +264,7 @@ def w4a16_lora_gemv(input, qweight, scales, zeros, lora_A, lora_B, group_size: i
                     lora_alpha: float = 16.0, *, zero_offset: int = 0):
     """``fp16(x . W + (alpha / r) (x . A) . B)``; ``r = lora_A.size(1)``
     (reference: ``csrc/kernels/w4a16_lora_gemv.cu:268-323``)."""
-    r = lora_A.size(1)
-    scale = float(np.float32(lora_alpha) / np.float32(r))  # fp32 division, as w4a16_lora_gemv.cu:221
+    scale = _lora_scale(float(lora_alpha), lora_A.size(1))
     return _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, scale, zero_offset)
 
 
