@@ -782,7 +782,10 @@ static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed,
     if (gmax > 256) continue;  // one tensor-map box covers a CTA's scale rows
     if (S > 1 && (Gt + S - 2) / (S - 1) == gmax) continue;  // a smaller cluster is as short
     pl.Ts_max = gmax * KPG;
-    pl.nst = std::min(gmax, MAX_NST);
+    // a shallower weight ring (down to 2 stages) buys shared memory for more
+    // CTAs per SM, hence wider clusters in one wave on deep-K shapes
+    for (int nst = std::min(gmax, MAX_NST); nst >= std::min(gmax, 2); --nst) {
+    pl.nst = nst;
     pl.smem = layout(M, KPG, pl.Ts_max, rank, S, pl.nst, zeros_packed).total;
     if (pl.smem > SMEM_LIMIT) continue;
     cudaLaunchConfig_t cfg = {};
@@ -804,11 +807,12 @@ static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed,
     }
     const long waves = (long(tiles) + clusters - 1) / clusters;
     // order: waves first, then groups per CTA (S grows, so later S wins ties
-    // on waves only when it shortens the CTA)
-    const long key2 = waves * 1000000L + long(gmax) * 1000L;
+    // on waves only when it shortens the CTA), then the deeper ring
+    const long key2 = waves * 1000000L + long(gmax) * 1000L + (MAX_NST - nst);
     if (best_key < 0 || key2 < best_key) {
       best = pl;
       best_key = key2;
+    }
     }
   }
   if (best_key < 0) {
