@@ -84,8 +84,10 @@ int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const void* scales
  * off).  When on, a GEMV launches as soon as every CTA of the GEMV before it
  * in the stream is running: it streams its weights and stages scales /
  * zeros / LoRA factors while that kernel finishes, and waits for it only
- * before reading x (and so before writing y).  Kernels that do not trigger
- * early (every kernel outside this library) still complete first.  The
+ * before reading x (and so before writing y).  The library's RMSNorm, SwiGLU,
+ * decode-step and decode-attention kernels trigger at their start too, so a
+ * GEMV after them streams its weights while they run; kernels that do not
+ * trigger early (every kernel outside this library) still complete first.  The
  * weight operands must therefore not be written by a GEMV issued just
  * before on the same stream (true for model weights).  Returns 0. */
 int qx_set_pdl(int enable);

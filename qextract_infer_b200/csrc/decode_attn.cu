@@ -90,6 +90,7 @@ __device__ __forceinline__ uint32_t swz(int r, int ch) {
 }
 
 __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
+  pdl_trigger();
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ unsigned s_is_last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;

@@ -30,6 +30,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(uint4* __restrict__ x,
                                                           const uint4* __restrict__ w,
                                                           uint4* __restrict__ y, int h8, float inv_h,
                                                           float eps) {
+  pdl_trigger();
   __shared__ float s_part[8];
   __shared__ float s_r;
   const size_t row = blockIdx.x;
@@ -93,6 +94,7 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(
     const __half* __restrict__ kw, float eps, const float* __restrict__ cosr,
     const float* __restrict__ sinr, __half* __restrict__ q_out, __half* __restrict__ k_cache,
     __half* __restrict__ v_cache, int cap, int64_t slot) {
+  pdl_trigger();
   constexpr int D = EPL * 32;
   const int lane = threadIdx.x & 31;
   const int item = blockIdx.x * 4 + (threadIdx.x >> 5);
@@ -141,6 +143,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 __global__ void __launch_bounds__(256) swiglu_packed_kernel(const uint4* __restrict__ gu,
                                                             uint4* __restrict__ y, int64_t rows,
                                                             int i8) {
+  pdl_trigger();
   const int64_t n = rows * i8;
   const int64_t stride = int64_t(gridDim.x) * blockDim.x;
   for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < n; t += stride) {

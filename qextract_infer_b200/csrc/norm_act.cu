@@ -24,6 +24,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_vec_kernel(const uint4* __restri
                                                            const uint4* __restrict__ w,
                                                            uint4* __restrict__ y, int h8,
                                                            float inv_h, float eps) {
+  pdl_trigger();
   __shared__ float s_part[32];
   __shared__ float s_r;
   const size_t row = blockIdx.x;
@@ -110,6 +111,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 __global__ void __launch_bounds__(256) swiglu_vec_kernel(const uint4* __restrict__ gate,
                                                          const uint4* __restrict__ up,
                                                          uint4* __restrict__ out, int64_t n8) {
+  pdl_trigger();
   const int64_t stride = int64_t(gridDim.x) * blockDim.x;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += stride) {
     const uint4 gv = __ldcs(gate + i);

@@ -98,6 +98,12 @@ __device__ __forceinline__ float2 h2_to_f2(uint32_t v) {
   return __half22float2(h);
 }
 
+// Lets the next kernel in the stream launch now if it was launched with
+// programmatic dependent launch (the GEMVs): it streams its weights while this
+// kernel runs and waits for this kernel's completion before reading its
+// inputs.  No effect on kernels launched without that attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
