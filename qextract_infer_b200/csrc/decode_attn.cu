@@ -91,6 +91,7 @@ __device__ __forceinline__ uint32_t swz(int r, int ch) {
 
 __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
   pdl_trigger();
+  pdl_wait();  // q and the cache come from earlier kernels
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ unsigned s_is_last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -423,7 +424,9 @@ extern "C" int qx_decode_attention(const void* q, const void* k_cache, const voi
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  attn::decode_attn_kernel<<<dim3(pl.nch, batch * kv_heads), attn::THREADS, attn::SMEM, st>>>(prm);
+  QX_CUDA_TRY(launch_pdl(attn::decode_attn_kernel, dim3(pl.nch, batch * kv_heads), dim3(attn::THREADS),
+                         size_t(attn::SMEM), st, prm),
+              "decode_attention: launch");
   return check_launch("decode_attention");
 }
 

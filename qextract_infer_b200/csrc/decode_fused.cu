@@ -31,6 +31,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(uint4* __restrict__ x,
                                                           uint4* __restrict__ y, int h8, float inv_h,
                                                           float eps) {
   pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel
   __shared__ float s_part[8];
   __shared__ float s_r;
   const size_t row = blockIdx.x;
@@ -95,6 +96,7 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(
     const float* __restrict__ sinr, __half* __restrict__ q_out, __half* __restrict__ k_cache,
     __half* __restrict__ v_cache, int cap, int64_t slot) {
   pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel
   constexpr int D = EPL * 32;
   const int lane = threadIdx.x & 31;
   const int item = blockIdx.x * 4 + (threadIdx.x >> 5);
@@ -144,6 +146,7 @@ __global__ void __launch_bounds__(256) swiglu_packed_kernel(const uint4* __restr
                                                             uint4* __restrict__ y, int64_t rows,
                                                             int i8) {
   pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel
   const int64_t n = rows * i8;
   const int64_t stride = int64_t(gridDim.x) * blockDim.x;
   for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < n; t += stride) {
@@ -185,11 +188,14 @@ extern "C" int qx_add_rmsnorm(void* x, const void* delta, const void* weight, vo
   auto Y = static_cast<uint4*>(y);
   const dim3 grid{static_cast<unsigned>(rows)};
   if (h8 <= 256)
-    dfused::add_rmsnorm_kernel<1><<<grid, 256, 0, st>>>(X, D, W, Y, h8, inv_h, eps);
+    QX_CUDA_TRY(launch_pdl(dfused::add_rmsnorm_kernel<1>, grid, dim3(256), 0, st, X, D, W, Y, h8, inv_h, eps),
+                "add_rmsnorm: launch");
   else if (h8 <= 512)
-    dfused::add_rmsnorm_kernel<2><<<grid, 256, 0, st>>>(X, D, W, Y, h8, inv_h, eps);
+    QX_CUDA_TRY(launch_pdl(dfused::add_rmsnorm_kernel<2>, grid, dim3(256), 0, st, X, D, W, Y, h8, inv_h, eps),
+                "add_rmsnorm: launch");
   else
-    dfused::add_rmsnorm_kernel<4><<<grid, 256, 0, st>>>(X, D, W, Y, h8, inv_h, eps);
+    QX_CUDA_TRY(launch_pdl(dfused::add_rmsnorm_kernel<4>, grid, dim3(256), 0, st, X, D, W, Y, h8, inv_h, eps),
+                "add_rmsnorm: launch");
   return check_launch("add_rmsnorm");
 }
 
@@ -218,16 +224,19 @@ extern "C" int qx_qk_norm_rope_append(const void* qkv, int batch, int q_heads, i
   auto VC = static_cast<__half*>(v_cache);
   switch (head_dim) {
     case 64:
-      dfused::qk_norm_rope_append_kernel<2><<<grid, 128, 0, st>>>(
-          Q, batch, q_heads, kv_heads, QW, KW, eps, cos_row, sin_row, QO, KC, VC, cap, slot);
+      QX_CUDA_TRY(launch_pdl(dfused::qk_norm_rope_append_kernel<2>, grid, dim3(128), 0, st, Q, batch,
+                             q_heads, kv_heads, QW, KW, eps, cos_row, sin_row, QO, KC, VC, cap, slot),
+                  "qk_norm_rope_append: launch");
       break;
     case 128:
-      dfused::qk_norm_rope_append_kernel<4><<<grid, 128, 0, st>>>(
-          Q, batch, q_heads, kv_heads, QW, KW, eps, cos_row, sin_row, QO, KC, VC, cap, slot);
+      QX_CUDA_TRY(launch_pdl(dfused::qk_norm_rope_append_kernel<4>, grid, dim3(128), 0, st, Q, batch,
+                             q_heads, kv_heads, QW, KW, eps, cos_row, sin_row, QO, KC, VC, cap, slot),
+                  "qk_norm_rope_append: launch");
       break;
     default:
-      dfused::qk_norm_rope_append_kernel<8><<<grid, 128, 0, st>>>(
-          Q, batch, q_heads, kv_heads, QW, KW, eps, cos_row, sin_row, QO, KC, VC, cap, slot);
+      QX_CUDA_TRY(launch_pdl(dfused::qk_norm_rope_append_kernel<8>, grid, dim3(128), 0, st, Q, batch,
+                             q_heads, kv_heads, QW, KW, eps, cos_row, sin_row, QO, KC, VC, cap, slot),
+                  "qk_norm_rope_append: launch");
       break;
   }
   return check_launch("qk_norm_rope_append");
@@ -244,7 +253,9 @@ extern "C" int qx_swiglu_packed(const void* gate_up, void* y, int64_t rows, int 
   const int64_t n = rows * i8;
   const int sms = device_sm_count();
   const unsigned blocks = unsigned(std::min<int64_t>((n + 255) / 256, int64_t(sms) * 8));
-  dfused::swiglu_packed_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint4*>(gate_up), static_cast<uint4*>(y), rows, i8);
+  QX_CUDA_TRY(launch_pdl(dfused::swiglu_packed_kernel, dim3(blocks), dim3(256), 0,
+                         reinterpret_cast<cudaStream_t>(stream), static_cast<const uint4*>(gate_up),
+                         static_cast<uint4*>(y), rows, i8),
+              "swiglu_packed: launch");
   return check_launch("swiglu_packed");
 }

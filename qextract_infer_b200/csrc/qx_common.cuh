@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 
@@ -103,6 +104,31 @@ __device__ __forceinline__ float2 h2_to_f2(uint32_t v) {
 // kernel runs and waits for this kernel's completion before reading its
 // inputs.  No effect on kernels launched without that attribute.
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+// Waits for the previous kernel in the stream to complete (its writes
+// visible); a no-op when this kernel was launched without programmatic
+// dependent launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+extern std::atomic<int> g_pdl_enabled;  // w4a16_gemv.cu (qx_set_pdl)
+
+// Launch with programmatic dependent launch when it is on: the kernel may
+// start while the previous one finishes and must call pdl_wait() before it
+// reads anything that kernel wrote.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = g_pdl_enabled.load(std::memory_order_relaxed) ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
