@@ -77,6 +77,10 @@ __device__ __forceinline__ uint64_t gtime() {
 
 template <int VPT>
 __global__ void __launch_bounds__(THREADS) ar_add_rmsnorm_kernel(const Params p) {
+  // the next GEMV may start streaming its weights now; it waits for this
+  // kernel's completion before reading x (calls of this kernel still never
+  // overlap: the kernels between two of them wait for their predecessors)
+  pdl_trigger();
   __shared__ float s_part[THREADS / 32];
   __shared__ float s_r;
   const int row = blockIdx.x, tid = threadIdx.x;
