@@ -661,6 +661,33 @@ def run_profile_cases(args):
     return 0
 
 
+def run_profile_decode_step(args):
+    """One Qwen3-8B decode step at TP 1 inside an NVTX range named "step" (the
+    ring pre-filled with 8192 random positions, two eager steps before it): the
+    command the committed decode-step launch list was captured from, with
+    ``ncu --nvtx --nvtx-include "step/"``.  Batch from ``--batches`` (first value)."""
+    import torch
+    from qextract_infer_b200.tp_decoder import DecoderConfig, TPDecoder
+    B = int(args.batches.split(",")[0])
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = DecoderConfig()
+    dec = TPDecoder(cfg, batch=B, device=dev, seed=4)
+    dec.cache.k.normal_()
+    dec.cache.v.normal_()
+    dec.cache._write_count = args.prompt
+    tok = torch.randint(0, cfg.vocab, (B,), device=dev)
+    for _ in range(2):
+        tok = dec.decode_step(tok)
+    torch.cuda.synchronize(dev)
+    torch.cuda.nvtx.range_push("step")
+    tok = dec.decode_step(tok)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"profile_decode_step": "done", "batch": B}), flush=True)
+    dec.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -675,7 +702,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=8192, help="decode_tp: prompt tokens")
     ap.add_argument("--decode", type=int, default=64, help="decode_tp: greedy decode tokens")
     ap.add_argument("--workload", choices=["decode_gemv", "kernels", "prefill_gemm", "decode_tp",
-                                           "profile_cases"],
+                                           "profile_cases", "profile_decode_step"],
                     default="decode_gemv",
                     help="decode_gemv: the headline line; kernels: RMSNorm/SwiGLU/ring/attention lines; "
                          "prefill_gemm: the tcgen05 GEMM over the Qwen3-8B shapes at M=4096")
@@ -688,6 +715,8 @@ def main():
         return run_decode_tp(args)
     if args.workload == "profile_cases":
         return run_profile_cases(args)
+    if args.workload == "profile_decode_step":
+        return run_profile_decode_step(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)
