@@ -281,49 +281,66 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
   if (!s_is_last) return;
   __threadfence();
   {
-    // Merge the chunks with every load issued up front (no serial chains):
-    // (1) all (max, sum) pairs, (2) the chunk weights, (3) O by 4 interleaved
-    // chunk subsets with 16-byte loads, (4) fixed-order sum of the subsets.
+    // Merge the chunks: (1) one warp per query row loads its chunks' (max,
+    // sum) pairs, reduces the max and the weighted sum with shuffles (fixed
+    // butterfly order: deterministic) and stores the chunk weights; (2) O by 4
+    // interleaved chunk subsets with 16-byte loads, two rows per pass so their
+    // loads are in flight together; (3) fixed-order sum of the subsets.
     const int G = p.G, nch = p.nch;
     const float* pb = p.part + size_t(bh) * nch * G * PSTRIDE;
-    float* sm_m = reinterpret_cast<float*>(smem);  // [G][nch]
-    float* sm_l = sm_m + G * nch;                  // [G][nch]
-    float* sm_L = sm_l + G * nch;                  // [16]
+    float* sm_m = reinterpret_cast<float*>(smem);  // [G][nch] chunk weights
+    float* sm_L = sm_m + 2 * G * nch;              // [16]
     // [4][G][D], 16-byte aligned for the float4 stores
     float* sm_o = sm_m + ((2 * G * nch + 16 + 3) & ~3);
-    for (int i = tid; i < G * nch; i += THREADS) {
-      const int r = i / nch, k = i - r * nch;
-      const float* pk = pb + (size_t(k) * G + r) * PSTRIDE;
-      sm_m[i] = __ldcg(pk);
-      sm_l[i] = __ldcg(pk + 1);
-    }
-    __syncthreads();
-    if (tid < G) {
-      float mx = -INFINITY;
-      for (int k = 0; k < nch; ++k) mx = fmaxf(mx, sm_m[tid * nch + k]);
-      float L = 0.f;
-      for (int k = 0; k < nch; ++k) {
-        const float f = sm_m[tid * nch + k] == -INFINITY ? 0.f : exp2f(sm_m[tid * nch + k] - mx);
-        sm_m[tid * nch + k] = f;  // reuse as the chunk weight
-        L = fmaf(sm_l[tid * nch + k], f, L);
+    for (int r = warp; r < G; r += WARPS) {
+      float mk[MAX_CHUNKS / 32], lk[MAX_CHUNKS / 32];
+#pragma unroll
+      for (int i = 0; i < MAX_CHUNKS / 32; ++i) {
+        const int k = lane + 32 * i;
+        const float* pk = pb + (size_t(k) * G + r) * PSTRIDE;
+        mk[i] = k < nch ? __ldcg(pk) : -INFINITY;
+        lk[i] = k < nch ? __ldcg(pk + 1) : 0.f;
       }
-      sm_L[tid] = L;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < MAX_CHUNKS / 32; ++i) mx = fmaxf(mx, mk[i]);
+      mx = warp_max(mx);
+      float L = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAX_CHUNKS / 32; ++i) {
+        const int k = lane + 32 * i;
+        const float f = mk[i] == -INFINITY ? 0.f : exp2f(mk[i] - mx);
+        if (k < nch) sm_m[r * nch + k] = f;
+        L = fmaf(lk[i], f, L);
+      }
+      L = warp_sum(L);
+      if (lane == 0) sm_L[r] = L;
     }
     __syncthreads();
     const int d4 = tid & 31, kq = tid >> 5;
-    for (int r = 0; r < G; ++r) {
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < G; r += 2) {
+      const bool two = r + 1 < G;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b2 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
       for (int k = kq; k < nch; k += 4) {
         const float4 v =
             __ldcg(reinterpret_cast<const float4*>(pb + (size_t(k) * G + r) * PSTRIDE + 4) + d4);
+        const float4 w = two ? __ldcg(reinterpret_cast<const float4*>(
+                                   pb + (size_t(k) * G + r + 1) * PSTRIDE + 4) + d4)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
         const float f = sm_m[r * nch + k];
+        const float f2 = two ? sm_m[(r + 1) * nch + k] : 0.f;
         a.x = fmaf(f, v.x, a.x);
         a.y = fmaf(f, v.y, a.y);
         a.z = fmaf(f, v.z, a.z);
         a.w = fmaf(f, v.w, a.w);
+        b2.x = fmaf(f2, w.x, b2.x);
+        b2.y = fmaf(f2, w.y, b2.y);
+        b2.z = fmaf(f2, w.z, b2.z);
+        b2.w = fmaf(f2, w.w, b2.w);
       }
       *reinterpret_cast<float4*>(sm_o + (kq * G + r) * D + 4 * d4) = a;
+      if (two) *reinterpret_cast<float4*>(sm_o + (kq * G + r + 1) * D + 4 * d4) = b2;
     }
     __syncthreads();
     const int d = tid;
