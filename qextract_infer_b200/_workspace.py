@@ -1,12 +1,13 @@
-"""Per-(device, stream, op) scratch buffers for the kernels that reduce across CTAs.
+"""Per-(device, stream, op) scratch buffers for the kernels that take a workspace.
 
-The library allocates nothing itself.  The split-K GEMV and the split-slot
-decode attention need a workspace whose counter region starts at zero; each
-kernel leaves its counters at zero again (the rest of the buffer holds
-partial results), so one zero-filled buffer per (stream, op) is reused across
-calls.  Calls on one stream are ordered and never overlap on the buffer; ops
-of different kinds get different buffers because one op's partials would
-otherwise sit where the other keeps its counters.
+The library allocates nothing itself.  The split-slot decode attention needs a
+workspace whose counter region starts at zero (it leaves its counters at zero
+again; the rest of the buffer holds partial results) and the prefill GEMM one
+for its LoRA down-projection, so one zero-filled buffer per (stream, op) is
+reused across calls.  Calls on one stream are ordered and never overlap on the
+buffer; ops of different kinds get different buffers because one op's partials
+would otherwise sit where the other keeps its counters.  (The decode GEMV
+reduces through distributed shared memory and takes no workspace.)
 """
 
 from __future__ import annotations
