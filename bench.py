@@ -282,24 +282,30 @@ def run_b200(args):
         ev1.synchronize()
         torch.cuda.synchronize(device)
         ms = ev0.elapsed_time(ev1)
-        # e2e through the public API: pinned host x -> device, GEMV, y -> pinned host
+        # e2e through the public API: pinned host x -> device buffer, GEMV into a
+        # device output buffer, y -> pinned host, every step
         x_host = torch.randn(M, K).half().pin_memory()
         y_host = torch.empty(M, N, dtype=torch.float16).pin_memory()
+        x_dev = torch.empty(M, K, dtype=torch.float16, device=device)
+        y_dev = torch.empty(M, N, dtype=torch.float16, device=device)
         e_steps = 0 if args.skip_e2e else max(1, min(steps, 2000))
+
+        def e2e_step(i):
+            x_dev.copy_(x_host, non_blocking=True)
+            qw, sc, qz, A, B = sets[i % nsets]
+            qx.w4a16_lora_gemv(x_dev, qw, sc, qz, A, B, GROUP, ALPHA, out=y_dev)
+            y_host.copy_(y_dev, non_blocking=True)
+
         with torch.cuda.stream(stream):
-            for i in range(3 if e_steps else 0):
-                xd = x_host.to(device, non_blocking=True)
-                qw, sc, qz, A, B = sets[i % nsets]
-                y_host.copy_(qx.w4a16_lora_gemv(xd, qw, sc, qz, A, B, GROUP, ALPHA), non_blocking=True)
+            for i in range(nsets if e_steps else 0):  # every weight set once: cached launch plans
+                e2e_step(i)
             stream.synchronize()
             if world > 1:
                 dist.barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             for i in range(e_steps):
-                xd = x_host.to(device, non_blocking=True)
-                qw, sc, qz, A, B = sets[i % nsets]
-                y_host.copy_(qx.w4a16_lora_gemv(xd, qw, sc, qz, A, B, GROUP, ALPHA), non_blocking=True)
+                e2e_step(i)
             e1.record(stream)
             e1.synchronize()
         e_ms = e0.elapsed_time(e1) if e_steps else float("nan")
@@ -309,6 +315,13 @@ def run_b200(args):
         t = torch.tensor([ms, e_ms], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e_ms = float(t[0]), float(t[1])
+    del sets, g_timed, g_warm
+    torch.cuda.empty_cache()
+    _C.check_device_error("decode GEMV bench")
+    # the rest of the metric, measured in the same run: Qwen3-8B decode tok/s
+    # tensor-parallel over the ranks, and at one GPU the prefill GEMM
+    tp_lines = [] if args.skip_tp else tp_decode_measure(args, world, rank, device)
+    gemm_line = prefill_gemm_measure(args, device) if (world == 1 and not args.skip_gemm) else None
     per_call_s = ms / 1e3 / steps
     achieved = BYTES_PER_CALL / per_call_s / 1e9  # one GPU, GB/s
     peak, peak_kind = measured_peaks()
@@ -347,10 +360,11 @@ def run_b200(args):
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": steps,
+            "tp_decode": tp_lines or None,
+            "prefill_gemm": gemm_line,
         }
     if world > 1:
         dist.barrier()
-        del g_timed, g_warm
         dist.destroy_process_group()
     if result is not None:
         print(json.dumps(result), flush=True)
@@ -464,19 +478,29 @@ def measured_tflops():
 
 
 def run_prefill_suite(args):
+    """Prefill W4A16-LoRA GEMM at M=4096 over the 7 Qwen3-8B projection shapes:
+    one JSON line per shape and one for the whole set (prefill_gemm_measure)."""
+    import torch
+    dev = torch.device("cuda", torch.cuda.current_device())
+    summary = prefill_gemm_measure(args, dev, per_shape=lambda d: print(json.dumps(d), flush=True))
+    print(json.dumps(summary), flush=True)
+    return 0
+
+
+def prefill_gemm_measure(args, dev, per_shape=None):
     """Prefill W4A16-LoRA GEMM at M=4096 over the 7 Qwen3-8B projection shapes
-    (GPTQ int4 g128, packed qzeros, LoRA r=64, alpha/r=2): one JSON line per
-    shape (tcgen05 path through the public API, us, TFLOP/s, fraction of the
-    measured dense fp16/bf16 peak) and one line for the whole set."""
+    (GPTQ int4 g128, packed qzeros, LoRA r=64, alpha/r=2) through the public
+    API (tcgen05 path): per shape us, TFLOP/s and fraction of the measured
+    dense bf16 peak (passed to ``per_shape``); returns the whole-set summary."""
     import torch
     from qextract_infer_b200 import _C
-    dev = torch.device("cuda", torch.cuda.current_device())
     st = torch.cuda.Stream(dev)
     peak, peak_sus, kind = measured_tflops()
     Mr, R, G = 4096, 64, 128
     gen = torch.Generator(device=dev).manual_seed(3)
     x = torch.randn(Mr, 12288, generator=gen, device=dev).half()
     total_flop, total_us = 0.0, 0.0
+    shapes = {}
     for name, K, N in QWEN3_8B_PREFILL:
         qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), generator=gen, device=dev, dtype=torch.int32)
         sc = (torch.rand(K // G, N, generator=gen, device=dev) * 0.015 + 0.005).half()
@@ -490,29 +514,28 @@ def run_prefill_suite(args):
         tf = flop / us / 1e6
         total_flop += flop
         total_us += us
-        print(json.dumps({"metric": "prefill W4A16-LoRA GEMM TFLOP/s", "shape": name, "M": Mr, "K": K,
-                          "N": N, "rank": R, "us_per_call": us, "TFLOP/s": tf, "peak": peak,
-                          "tensor_frac": tf / peak, "peak_kind": kind,
-                          "kernels": ["lora_down_split_kernel", "lora_down_finalize_kernel", "w4a16_gemm_kernel"]}), flush=True)
+        if per_shape:
+            per_shape({"metric": "prefill W4A16-LoRA GEMM TFLOP/s", "shape": name, "M": Mr, "K": K,
+                       "N": N, "rank": R, "us_per_call": us, "TFLOP/s": tf, "peak": peak,
+                       "tensor_frac": tf / peak, "peak_kind": kind})
+        shapes[name] = {"us": us, "TFLOP/s": tf}
+        del qw, sc, qz, A, B, xk
+    del x
+    torch.cuda.empty_cache()
+    _C.check_device_error("prefill GEMM bench")
     tf = total_flop / total_us / 1e6
-    print(json.dumps({"metric": "prefill W4A16-LoRA GEMM TFLOP/s (7 Qwen3-8B shapes, M=4096)",
-                      "value": tf, "unit": "TFLOP/s", "us_total": total_us, "flop_total": total_flop,
-                      "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
-                                   "frac": tf / peak, "peak_kind": kind}}), flush=True)
-    return 0
+    return {"metric": "prefill W4A16-LoRA GEMM TFLOP/s (7 Qwen3-8B shapes, M=4096, r=64)",
+            "value": tf, "unit": "TFLOP/s", "us_total": total_us, "flop_total": total_flop,
+            "shapes": shapes,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tf / peak, "peak_kind": kind,
+                         "timing": "CUDA graph of back-to-back calls per shape, best of 3 replays"}}
 
 
 def run_decode_tp(args):
-    """Qwen3-8B-architecture decode (random init, GPTQ int4 g128 + LoRA r16
-    linears, fp16 norms/embeddings/lm_head, ring of 4 sink + 4092 window),
-    tensor-parallel over the torchrun ranks: an 8192-token prompt prefilled in
-    2048-token chunks, then 64 greedy decode steps replayed from per-step CUDA
-    graphs (NCCL all-reduces inside).  One JSON line per batch size; value =
-    decoded tokens per second over the whole job, time = max over ranks."""
+    """Qwen3-8B decode alone (tp_decode_measure), one JSON line per batch size."""
     import torch
     import torch.distributed as dist
-    from qextract_infer_b200.tp_decoder import DecoderConfig, TPDecoder
-
     world, rank, local = dist_setup()
     if world > 1:
         torch.cuda.set_device(local)
@@ -520,19 +543,53 @@ def run_decode_tp(args):
                                 timeout=__import__("datetime").timedelta(seconds=300))
     dev = torch.device("cuda", local if world > 1 else torch.cuda.current_device())
     torch.cuda.set_device(dev)
+    for line in tp_decode_measure(args, world, rank, dev):
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def tp_decode_measure(args, world, rank, dev):
+    """Qwen3-8B-architecture decode (random init, GPTQ int4 g128 + LoRA r16
+    linears, fp16 norms/embeddings/lm_head, ring of 4 sink + 4092 window),
+    tensor-parallel over the ranks of the initialised process group (or one
+    GPU): an 8192-token prompt prefilled in 2048-token chunks, then 64 greedy
+    decode steps replayed from per-step CUDA graphs.  One dict per batch size;
+    tok_s = decoded tokens per second over the whole job, time = max over
+    ranks.  At more than one rank, also the device time of one NVLink
+    all-reduce (+ residual add + RMSNorm) call at the batch's rows."""
+    import torch
+    import torch.distributed as dist
+    from qextract_infer_b200 import _C
+    from qextract_infer_b200.tp_decoder import DecoderConfig, TPDecoder
+
     cfg = DecoderConfig()
     prompt_len, decode_steps, chunk = args.prompt, args.decode, 2048
     batches = [int(b) for b in args.batches.split(",")]
     hbm = measured_peaks()[0]
+    lines = []
+
+    def max_over_ranks(v):
+        if world > 1:
+            t = torch.tensor([v], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            v = float(t[0])
+        return v
+
     for B in batches:
         dec = TPDecoder(cfg, batch=B, device=dev, seed=4)
         prompt = torch.randint(0, cfg.vocab, (B, prompt_len), generator=torch.Generator().manual_seed(4))
         prompt = prompt.to(dev)
         torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
         t0 = time.time()
         nxt = dec.prefill(prompt, chunk=chunk)
         torch.cuda.synchronize(dev)
-        prefill_s = time.time() - t0
+        prefill_s = max_over_ranks(time.time() - t0)
         count0 = dec.cache.get_total_written()
         k0, v0 = dec.cache.k.clone(), dec.cache.v.clone()
         tok = torch.empty_like(nxt)
@@ -569,40 +626,58 @@ def run_decode_tp(args):
                     g.replay()
                 e1.record(st)
             e1.synchronize()
-        ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ms], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t[0])
+        ms = max_over_ranks(e0.elapsed_time(e1))
         step_ms = ms / decode_steps
+        dec.check_device_error()
         # bytes one decode step reads per rank: int4 weights + scales/qzeros + LoRA, lm_head
         # shard, and the ring (all layers, this rank's KV heads, every sequence)
         wbytes = sum(L[k].weight_bytes() for L in dec.layers for k in ("qkv", "o", "gate_up", "down"))
         wbytes += dec.lm_head.numel() * 2
         kvbytes = 2 * cfg.num_layers * B * (cfg.sink + cfg.window) * dec.hkv * cfg.head_dim * 2
         per_rank_gbs = (wbytes + kvbytes) / (step_ms / 1e3) / 1e9
-        line = {"metric": "Qwen3-8B decode tok/s", "value": B * decode_steps / (ms / 1e3),
-                "unit": "tok/s", "n_gpus": world, "steps": decode_steps, "warmup": 1,
-                "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
-                "vs_baseline": None, "dtype": "fp16 activations, int4 weights, fp32 accumulate",
-                "data": "synthetic (random-init Qwen3-8B architecture, uniform random prompt tokens)",
-                "config": {"workload": "Qwen3-8B decoder, TP decode", "batch": B,
-                           "prompt": prompt_len, "decode_tokens": decode_steps,
-                           "parallelism": f"tp{world}", "prefill_chunk": chunk,
-                           "graphs": "one CUDA graph per decode step"},
-                "prefill_s": prefill_s, "prefill_tok_s": B * prompt_len / prefill_s,
-                "roofline": {"bound": "hbm", "achieved": per_rank_gbs, "peak": hbm, "unit": "GB/s",
-                             "frac": per_rank_gbs / hbm, "bytes_per_step_per_rank": wbytes + kvbytes}}
-        if rank == 0:
-            print(json.dumps(line), flush=True)
+        ar_us = None
+        if dec.ar is not None:  # one NVLink all-reduce + add + RMSNorm call, device time
+            part = torch.randn(B, cfg.hidden, device=dev).half()
+            xr = torch.randn(B, cfg.hidden, device=dev).half()
+            w = torch.ones(cfg.hidden, device=dev).half()
+            with torch.cuda.stream(st):
+                for _ in range(3):
+                    dec.ar.add_rmsnorm(part, xr, w, cfg.rms_eps)
+            st.synchronize()
+            ga = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(ga, stream=st):
+                for _ in range(72):
+                    dec.ar.add_rmsnorm(part, xr, w, cfg.rms_eps)
+            with torch.cuda.stream(st):
+                ga.replay()
+            st.synchronize()
+            dist.barrier()
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(st):
+                a0.record(st)
+                ga.replay()
+                a1.record(st)
+            a1.synchronize()
+            ar_us = max_over_ranks(a0.elapsed_time(a1) * 1e3 / 72)
+            del ga
+            dec.check_device_error()
+        lines.append({
+            "metric": "Qwen3-8B decode tok/s", "value": B * decode_steps / (ms / 1e3), "unit": "tok/s",
+            "batch": B, "n_gpus": world, "parallelism": f"tp{world}", "steps": decode_steps,
+            "ms_per_step": step_ms, "scaling": "strong",
+            "config": {"workload": "Qwen3-8B decoder (36 layers, hidden 4096, 32/8 heads, "
+                                   "GPTQ int4 g128 + LoRA r16), TP decode",
+                       "prompt": prompt_len, "decode_tokens": decode_steps, "prefill_chunk": chunk,
+                       "graphs": "one CUDA graph per decode step"},
+            "prefill_s": prefill_s, "prefill_tok_s": B * prompt_len / prefill_s,
+            "nvlink_allreduce_us": ar_us,
+            "roofline": {"bound": "hbm", "achieved": per_rank_gbs, "peak": hbm, "unit": "GB/s",
+                         "frac": per_rank_gbs / hbm, "bytes_per_step_per_rank": wbytes + kvbytes}})
         del graphs, g
         dec.close()
         del dec, k0, v0
         torch.cuda.empty_cache()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+    return lines
 
 
 def run_profile_cases(args):
@@ -698,6 +773,8 @@ def main():
                     help="weight sets in the rotation (default: enough for > 2x L2)")
     ap.add_argument("--skip-e2e", action="store_true", help="omit the public-API timing")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline")
+    ap.add_argument("--skip-tp", action="store_true", help="omit the Qwen3-8B TP decode keys")
+    ap.add_argument("--skip-gemm", action="store_true", help="omit the prefill GEMM key")
     ap.add_argument("--batches", default="1,32", help="decode_tp: batch sizes")
     ap.add_argument("--prompt", type=int, default=8192, help="decode_tp: prompt tokens")
     ap.add_argument("--decode", type=int, default=64, help="decode_tp: greedy decode tokens")

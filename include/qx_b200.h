@@ -43,7 +43,7 @@ const char* qx_last_error(void);
  * GPU (the kernel then finishes with undefined output).  New component: the
  * reference has no device-side error reporting. */
 #define QX_DEVERR_MBAR_TIMEOUT 1u
-/* a peer rank's flag did not arrive within ~2 s (qx_nvlink_ar_add_rmsnorm) */
+/* a peer rank's flag did not arrive within the wait limit (qx_nvlink_ar_add_rmsnorm) */
 #define QX_DEVERR_PEER_TIMEOUT 2u
 /* Reads (and with reset != 0 clears) the sticky error bits of the current
  * device; synchronises with the device. */
@@ -128,7 +128,7 @@ int qx_w4a16_lora_gemm_sm100(const void* x, const int32_t* qweight, const void* 
 
 /* ------------------------------------------------------------------------
  * Fused kernels of the tensor-parallel decode step (new components; the
- * reference's patched Qwen3 layer, qextract/patch_qwen.py, runs each as
+ * reference's patched Qwen3 layer, qextract/patch.py, runs each as
  * separate torch ops).  Rounding points equal the unfused sequence.
  *
  * qx_add_rmsnorm: x <- fp16(x + delta) in place (the residual add), then
@@ -169,11 +169,21 @@ int qx_swiglu_packed(const void* gate_up, void* y, int64_t rows, int inter, qx_s
  * (all-gather, rank order) and call qx_nvlink_ar_open with all of them; then
  * a barrier before the first call.  Calls: every rank makes the same sequence
  * of calls; calls on one rank must not overlap (stream order).  A peer that
- * does not arrive within ~2 s sets QX_DEVERR_PEER_TIMEOUT.
+ * does not arrive within the wait limit (2 s unless qx_nvlink_ar_set_timeout
+ * sets another) sets QX_DEVERR_PEER_TIMEOUT and that call's output is
+ * undefined; the rank that timed out is then one epoch ahead, so its later
+ * calls time out too until the communicator is rebuilt.
  * ---------------------------------------------------------------------- */
 size_t qx_nvlink_ar_handle_bytes(void);
 int qx_nvlink_ar_create(int world, int rank, int max_rows, int hidden, void** ctx, void* handle_out);
 int qx_nvlink_ar_open(void* ctx, const void* handles);
+/* Alternative to qx_nvlink_ar_open when every rank's context lives in this
+ * process (one process driving several GPUs, or several ranks on one GPU):
+ * ctxs[r] is rank r's context; peer access is enabled between distinct
+ * devices. */
+int qx_nvlink_ar_open_local(void* ctx, void* const* ctxs);
+/* Limit of each wait for a peer's flag, in nanoseconds (default 2e9). */
+int qx_nvlink_ar_set_timeout(void* ctx, int64_t timeout_ns);
 int qx_nvlink_ar_add_rmsnorm(void* ctx, const void* partial, void* x, const void* weight, void* y,
                              int rows, float eps, qx_stream_t stream);
 int qx_nvlink_ar_destroy(void* ctx);
@@ -255,7 +265,8 @@ int qx_decode_attention(const void* q, const void* k_cache, const void* v_cache,
  * library (held by every GPU that loads it until the process exits) instead
  * of a caller workspace.  Shapes whose scratch exceeds that size are rejected
  * with QX_ERR_UNSUPPORTED and a message (Qwen3-8B geometry, 32 query / 8 KV
- * heads, 4 + 4092 slots, fits up to batch 32).
+ * heads, 4 + 4092 slots, fits every batch up to 247 on a 148-SM B200; the
+ * need is qx_decode_attention_workspace_size for the same shape).
  * The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) for that device; make that first call before any
  * stream capture.  Each call clears the counters it needs with

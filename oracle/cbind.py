@@ -46,6 +46,9 @@ def lib():
                                           ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                           ctypes.c_int, ctypes.c_int, ctypes.c_float,
                                           ctypes.c_int]
+        L.qxo_dequantize.restype = ctypes.c_int
+        L.qxo_dequantize.argtypes = [p, p, p, ctypes.c_int, ctypes.c_int, p, ctypes.c_int,
+                                     ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.qxo_ring_write_pos.restype = ctypes.c_int64
         L.qxo_ring_write_pos.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int]
         L.qxo_ring_valid_length.restype = ctypes.c_int64
@@ -87,6 +90,21 @@ def c_w4a16_lora_gemv(x, qweight, scales, zeros, lora_A=None, lora_B=None,
         raise ValueError("qxo_w4a16_lora_gemv: bad shapes")
     out = yf if return_f32 else y
     return out.reshape(*lead, N)
+
+
+def c_dequantize(qweight, scales, zeros, group_size=128, zero_offset=0, nthreads=0):
+    """C oracle: same contract as ``oracle.gptq.dequantize_gptq`` (fp16 ``[K, N]``)."""
+    qweight = np.ascontiguousarray(qweight, dtype=np.int32)
+    K, N = qweight.shape[0] * 8, qweight.shape[1]
+    scales = np.ascontiguousarray(scales, dtype=np.float16)
+    packed = 1 if zeros.dtype == np.int32 else 0
+    zeros = np.ascontiguousarray(zeros)
+    W = np.empty((K, N), dtype=np.float16)
+    rc = lib().qxo_dequantize(_ptr(qweight), _ptr(scales), _ptr(zeros), packed, zero_offset,
+                              _ptr(W), K, N, group_size, int(nthreads))
+    if rc != 0:
+        raise ValueError("qxo_dequantize: bad shapes")
+    return W
 
 
 def c_ring_indices(count: int, sink: int, window: int) -> np.ndarray:

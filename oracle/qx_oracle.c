@@ -159,6 +159,33 @@ int qxo_w4a16_lora_gemv(const uint16_t *x, const int32_t *qweight,
     return 0;
 }
 
+/* W[K, N] = fp16((q - z) * s) in fp32, rounded once (tests/test_w4a16_gemv.py:68-90),
+ * the dequantised weight of the GEMV above, written out for the large checks.
+ * Returns 0, or -1 on a shape error. */
+int qxo_dequantize(const int32_t *qweight, const uint16_t *scales, const void *zeros,
+                   int zeros_packed, int zero_offset, uint16_t *W, int K, int N,
+                   int group_size, int nthreads) {
+    if (K <= 0 || N <= 0 || K % 8 || group_size <= 0 || K % group_size) return -1;
+    if (zeros_packed && N % 8) return -1;
+#ifdef _OPENMP
+    if (nthreads > 0) omp_set_num_threads(nthreads);
+#else
+    (void)nthreads;
+#endif
+#pragma omp parallel for schedule(static)
+    for (int pr = 0; pr < K / 8; pr++) {
+        int g = (pr * 8) / group_size;
+        for (int n = 0; n < N; n++) {
+            uint32_t word = (uint32_t)qweight[(size_t)pr * N + n];
+            float s = qxo_h2f(scales[(size_t)g * N + n]);
+            float z = zero_at(zeros, zeros_packed, zero_offset, g, n, N);
+            for (int i = 0; i < 8; i++)
+                W[(size_t)(pr * 8 + i) * N + n] = qxo_f2h(((float)((word >> (4 * i)) & 0xfu) - z) * s);
+        }
+    }
+    return 0;
+}
+
 /* Ring-buffer index math (qextract/kv_cache.py:114-152). */
 int64_t qxo_ring_write_pos(int64_t count, int sink, int window) {
     if (count < sink) return count;

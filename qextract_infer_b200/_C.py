@@ -71,6 +71,29 @@ def _ptr(t):
     return None if t is None else t.data_ptr()
 
 
+DEVERR_MBAR_TIMEOUT, DEVERR_PEER_TIMEOUT = 1, 2
+
+
+def device_error(reset: bool = True) -> int:
+    """The sticky device-side error bits of the current device (a bounded
+    wait inside a kernel that ran out: 1 = an mbarrier phase, 2 = a peer
+    rank's flag); synchronises with the device.  ``reset`` clears them."""
+    import ctypes
+    code = ctypes.c_uint(0)
+    _lib.check(_LIB.qx_get_device_error(ctypes.byref(code), 1 if reset else 0), "get_device_error")
+    return int(code.value)
+
+
+def check_device_error(what: str = "device") -> None:
+    """Raise if a kernel's bounded wait ran out since the last check (its
+    output was undefined); clears the bits."""
+    code = device_error(reset=True)
+    if code:
+        names = [n for b, n in ((DEVERR_MBAR_TIMEOUT, "mbarrier wait timed out"),
+                                (DEVERR_PEER_TIMEOUT, "peer rank did not arrive")) if code & b]
+        raise RuntimeError(f"{what}: device-side error 0x{code:x} ({', '.join(names)})")
+
+
 # ------------------------------------------------------------------ norms --
 def fused_rmsnorm(input: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     """``fp16((x * rsqrt(mean(x^2) + eps)) * w)`` over the last dim
@@ -189,20 +212,27 @@ def _prepare_lora(lora_A, lora_B):
 GEMM_MIN_ROWS = 128
 
 
-def _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale, zero_offset,
-           path: str | None = None):
-    """``path`` (tests and benchmarks): "gemm" forces the tensor-core GEMM;
-    None routes by shape (GEMM for >= GEMM_MIN_ROWS rows, else the GEMV)."""
-    for t, n in ((input, "input"), (qweight, "qweight"), (scales, "scales"), (zeros, "zeros")):
+class _Weights:
+    """Validated description of one (qweight, scales, zeros, lora_A, lora_B,
+    group_size, zero_offset) set, kept so that a decode loop calling the same
+    weights again only checks that the tensors are still the same ones."""
+
+    __slots__ = ("refs", "ptrs", "qw_shape", "K", "N", "packed", "rank", "A", "B", "dev",
+                 "group", "zero_offset", "args")
+
+
+_WCACHE: dict = {}
+_WCACHE_MAX = 4096
+
+
+def _validate_weights(qweight, scales, zeros, lora_A, lora_B, group_size, zero_offset) -> _Weights:
+    for t, n in ((qweight, "qweight"), (scales, "scales"), (zeros, "zeros")):
         _check_input(t, n)
-    _check_fp16(input, "input")
     _check_fp16(scales, "scales")
     if qweight.dtype != torch.int32 or qweight.dim() != 2:
         raise RuntimeError("qweight must be int32 [K/8, N]")
-    K = input.size(-1)
+    K = qweight.size(0) * 8
     N = qweight.size(1)
-    if qweight.size(0) * 8 != K:
-        raise RuntimeError(f"qweight has {qweight.size(0)} packed rows; input K={K} needs {K // 8}")
     G = K // group_size if group_size > 0 else 0
     if scales.dim() != 2 or scales.size(0) != G or scales.size(1) != N:
         raise RuntimeError(f"scales must be [{G}, {N}], got {list(scales.shape)}")
@@ -226,46 +256,111 @@ def _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale
                 lora_B.size(0) != lora_A.size(1) or lora_B.size(1) != N:
             raise RuntimeError(f"lora_A must be [{K}, r] and lora_B [r, {N}]")
         lora_A, lora_B, rank = _prepare_lora(lora_A, lora_B)
+    devs = {t.get_device() for t in (qweight, scales, zeros, lora_A, lora_B) if t is not None}
+    if len(devs) != 1:
+        raise RuntimeError("qweight, scales, zeros and the LoRA factors must be on one device")
+    w = _Weights()
+    w.qw_shape = qweight.shape
+    w.K, w.N, w.packed, w.rank = K, N, packed, rank
+    w.A, w.B = lora_A, lora_B  # the (possibly padded) factors stay alive with the entry
+    w.dev = devs.pop()
+    w.group, w.zero_offset = int(group_size), int(zero_offset)
+    w.args = (qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), packed, w.zero_offset,
+              _ptr(lora_A), _ptr(lora_B))
+    return w
+
+
+def _weights(qweight, scales, zeros, lora_A, lora_B, group_size, zero_offset) -> _Weights:
+    import weakref
+    key = (id(qweight), id(scales), id(zeros), id(lora_A), id(lora_B), group_size, zero_offset)
+    w = _WCACHE.get(key)
+    if w is not None:
+        r = w.refs
+        if (r[0]() is qweight and r[1]() is scales and r[2]() is zeros
+                and (lora_A is None or (r[3]() is lora_A and r[4]() is lora_B))
+                and qweight.data_ptr() == w.ptrs[0] and scales.data_ptr() == w.ptrs[1]
+                and zeros.data_ptr() == w.ptrs[2] and qweight.shape == w.qw_shape
+                and (lora_A is None or (lora_A.data_ptr() == w.ptrs[3]
+                                        and lora_B.data_ptr() == w.ptrs[4]))):
+            return w
+    w = _validate_weights(qweight, scales, zeros, lora_A, lora_B, group_size, zero_offset)
+    w.refs = tuple(weakref.ref(t) if t is not None else (lambda: None)
+                   for t in (qweight, scales, zeros, lora_A, lora_B))
+    w.ptrs = tuple(t.data_ptr() if t is not None else 0 for t in (qweight, scales, zeros, lora_A, lora_B))
+    if len(_WCACHE) >= _WCACHE_MAX:
+        _WCACHE.clear()
+    _WCACHE[key] = w
+    return w
+
+
+def _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale, zero_offset,
+           path: str | None = None, out: torch.Tensor | None = None):
+    """``path`` (tests and benchmarks): "gemm" forces the tensor-core GEMM;
+    None routes by shape (GEMM for >= GEMM_MIN_ROWS rows, else the GEMV).
+    ``out``: optional preallocated fp16 output ``[..., N]`` (written, returned)."""
+    w = _weights(qweight, scales, zeros, lora_A, lora_B, group_size, zero_offset)
+    if not (isinstance(input, torch.Tensor) and input.is_cuda and input.dtype == torch.float16
+            and input.is_contiguous()):
+        _check_input(input, "input")
+        _check_fp16(input, "input")
+    K, N = w.K, w.N
+    if input.size(-1) != K:
+        raise RuntimeError(f"qweight has {K // 8} packed rows; input K={input.size(-1)} needs "
+                           f"{input.size(-1) // 8}")
+    di = input.get_device()
+    if di != w.dev:
+        raise RuntimeError(f"input is on cuda:{di} but the weights are on cuda:{w.dev}")
     lead = input.shape[:-1]
-    M = math.prod(lead)
-    dev = input.device
-    out = torch.empty(*lead, N, dtype=torch.float16, device=dev)
+    M = input.numel() // K
+    if out is None:
+        out = torch.empty(lead + (N,), dtype=torch.float16, device=input.device)
+    elif not (out.is_cuda and out.dtype == torch.float16 and out.is_contiguous()
+              and out.shape == lead + (N,) and out.get_device() == di):
+        raise RuntimeError(f"out must be a contiguous fp16 CUDA tensor of shape {list(lead) + [N]} "
+                           f"on cuda:{di}")
+    rank = w.rank
     if path == "gemm" or (path is None and M >= GEMM_MIN_ROWS and N % 256 == 0 and K % 64 == 0
                           and rank <= 64):
         # prefill: the tcgen05 tensor-core GEMM
+        dev = input.device
         st = _stream(dev)
         with torch.cuda.device(dev):
             need = _LIB.qx_w4a16_lora_gemm_sm100_workspace_size(M, rank)
             ws = _workspace.get(dev, st, need, "w4a16_gemm") if need else None
             _lib.check(_LIB.qx_w4a16_lora_gemm_sm100(
-                input.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), packed,
-                int(zero_offset), _ptr(lora_A), _ptr(lora_B), out.data_ptr(), M, K, N, rank,
-                int(group_size), float(lora_scale), _ptr(ws), int(need), st.cuda_stream),
-                "w4a16_gemm")
+                input.data_ptr(), *w.args, out.data_ptr(), M, K, N, rank, w.group, float(lora_scale),
+                _ptr(ws), int(need), st.cuda_stream), "w4a16_gemm")
         return out
-    args = (input.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), packed,
-            int(zero_offset), _ptr(lora_A), _ptr(lora_B), out.data_ptr(), M, K, N, rank,
-            int(group_size), float(lora_scale))
-    if dev.index == torch.cuda.current_device():  # the decode hot path: no device switch
-        _lib.check(_LIB.qx_w4a16_lora_gemv(*args, _raw_stream(dev)), "w4a16_gemv")
+    if di == torch.cuda.current_device():  # the decode hot path: no device switch
+        rc = _LIB.qx_w4a16_lora_gemv(input.data_ptr(), *w.args, out.data_ptr(), M, K, N, rank, w.group,
+                                     lora_scale, _raw_stream_of(di) if _raw_stream_of else
+                                     torch.cuda.current_stream(di).cuda_stream)
+        if rc < 0:
+            _lib.check(rc, "w4a16_gemv")
     else:
-        with torch.cuda.device(dev):
-            _lib.check(_LIB.qx_w4a16_lora_gemv(*args, _raw_stream(dev)), "w4a16_gemv")
+        with torch.cuda.device(di):
+            _lib.check(_LIB.qx_w4a16_lora_gemv(input.data_ptr(), *w.args, out.data_ptr(), M, K, N, rank,
+                                               w.group, lora_scale, _raw_stream(input.device)),
+                       "w4a16_gemv")
     return out
 
 
-def w4a16_gemv(input, qweight, scales, zeros, group_size: int = 128, *, zero_offset: int = 0):
+def w4a16_gemv(input, qweight, scales, zeros, group_size: int = 128, *, zero_offset: int = 0,
+               out: torch.Tensor | None = None):
     """``fp16(x . W)`` with ``W = s (q - z)`` from GPTQ int4 packing
-    (reference: ``csrc/kernels/w4a16_lora_gemv.cu:233-265``)."""
-    return _w4a16(input, qweight, scales, zeros, None, None, group_size, 0.0, zero_offset)
+    (reference: ``csrc/kernels/w4a16_lora_gemv.cu:233-265``).  ``out``: an
+    optional preallocated output (an addition to the reference signature)."""
+    return _w4a16(input, qweight, scales, zeros, None, None, group_size, 0.0, zero_offset, out=out)
 
 
 def w4a16_lora_gemv(input, qweight, scales, zeros, lora_A, lora_B, group_size: int = 128,
-                    lora_alpha: float = 16.0, *, zero_offset: int = 0):
+                    lora_alpha: float = 16.0, *, zero_offset: int = 0,
+                    out: torch.Tensor | None = None):
     """``fp16(x . W + (alpha / r) (x . A) . B)``; ``r = lora_A.size(1)``
-    (reference: ``csrc/kernels/w4a16_lora_gemv.cu:268-323``)."""
+    (reference: ``csrc/kernels/w4a16_lora_gemv.cu:268-323``).  ``out``: an
+    optional preallocated output (an addition to the reference signature)."""
     scale = _lora_scale(float(lora_alpha), lora_A.size(1))
-    return _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, scale, zero_offset)
+    return _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, scale, zero_offset, out=out)
 
 
 # ------------------------------------------------------------- ring cache --

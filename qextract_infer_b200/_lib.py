@@ -45,6 +45,8 @@ SIGNATURES = {
     "qx_nvlink_ar_handle_bytes": (c_size_t, []),
     "qx_nvlink_ar_create": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "qx_nvlink_ar_open": (c_int, [c_void_p, c_void_p]),
+    "qx_nvlink_ar_open_local": (c_int, [c_void_p, c_void_p]),
+    "qx_nvlink_ar_set_timeout": (c_int, [c_void_p, c_int64]),
     "qx_nvlink_ar_add_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                                          c_float, c_void_p]),
     "qx_nvlink_ar_destroy": (c_int, [c_void_p]),

@@ -38,7 +38,7 @@ constexpr int ROW_BYTES = D * 2;                 // 256
 constexpr int TILE_BYTES = TILE * ROW_BYTES;     // 4 KB
 constexpr int WARP_SMEM = 2 * 2 * TILE_BYTES;    // 2 stages x (K, V)
 constexpr int SMEM = WARPS * WARP_SMEM;          // 64 KB
-constexpr int CHUNK_ALIGN = WARPS * TILE;        // 64 slots
+constexpr int CHUNK_ALIGN = TILE;                // chunks are whole 16-slot tiles
 constexpr int CTAS_PER_SM = 3;
 constexpr int PSTRIDE = D + 4;                   // floats per (row) partial: m, l, pad, pad, O[D]
 constexpr int COUNTER_SLOTS = 4096;              // fixed counter region at the workspace start
@@ -375,6 +375,21 @@ static Plan make_plan(int batch, int kv_heads, int G, int cap, int valid, int sm
   return pl;
 }
 
+// Raises the kernel's dynamic shared-memory limit once per device (both
+// entry points; the per-device flags are guarded by a mutex).
+static int prepare_kernel() {
+  static std::mutex mu;
+  static bool done[64] = {};
+  int dev = 0;
+  QX_CUDA_TRY(cudaGetDevice(&dev), "decode_attention: cudaGetDevice");
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev >= 0 && dev < 64 && done[dev]) return QX_OK;
+  QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM),
+              "decode_attention: set smem limit");
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return QX_OK;
+}
+
 }  // namespace attn
 }  // namespace qx
 
@@ -431,14 +446,9 @@ extern "C" int qx_decode_attention(const void* q, const void* k_cache, const voi
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   prm.counters = reinterpret_cast<unsigned*>(ws);
   prm.part = reinterpret_cast<float*>(ws + pl.off_part);
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    QX_CUDA_TRY(cudaFuncSetAttribute(attn::decode_attn_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM),
-                "decode_attention: set smem limit");
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  {
+    const int rc = attn::prepare_kernel();
+    if (rc != QX_OK) return rc;
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // plain launch (measured: launched early, its CTAs wait resident and the
@@ -540,9 +550,10 @@ extern "C" int qx_decode_attention_noalloc(const void* q, const void* k_cache,
   unsigned char* ws = static_cast<unsigned char*>(scratch);
   prm.counters = reinterpret_cast<unsigned*>(ws);
   prm.part = reinterpret_cast<float*>(ws + pl.off_part);
-  QX_CUDA_TRY(cudaFuncSetAttribute(attn::decode_attn_kernel,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM),
-              "decode_attention_noalloc: set smem limit");
+  {
+    const int rc = attn::prepare_kernel();
+    if (rc != QX_OK) return rc;
+  }
   attn::decode_attn_kernel<<<dim3(pl.nch, batch * kv_heads), attn::THREADS, attn::SMEM, st>>>(prm);
   return check_launch("decode_attention_noalloc");
 }

@@ -1,5 +1,5 @@
 // Fused elementwise kernels of the tensor-parallel decode step (new
-// components: the reference's patched Qwen3 layer, qextract/patch_qwen.py,
+// components: the reference's patched Qwen3 layer, qextract/patch.py,
 // runs these as separate torch ops around its GEMV calls).  Each keeps the
 // rounding points of the unfused sequence, so results equal it:
 //

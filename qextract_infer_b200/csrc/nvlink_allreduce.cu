@@ -13,9 +13,10 @@
 //   1. e = counter[r] + 1; copy partial[r] into data[e & 1][r] (local stores),
 //      then one thread: fence.sys + st.release.sys flags[r] = e;
 //   2. one thread per peer polls the peer's flags[r] (ld.acquire.sys over
-//      NVLink) until it reaches e, bounded (~2 s by %globaltimer; on timeout the
-//      device error word gets QX_DEVERR_PEER_TIMEOUT and the row is reduced
-//      with whatever is there);
+//      NVLink) until it reaches e, bounded (2 s by %globaltimer unless
+//      qx_nvlink_ar_set_timeout says otherwise; on timeout the device error
+//      word gets QX_DEVERR_PEER_TIMEOUT and the row is reduced with whatever is
+//      there, so the output of that call is undefined);
 //   3. every rank sums the world rows in rank order (fp32, L2-only loads of
 //      peer memory), rounds once, adds the residual, RMS-normalises; all ranks
 //      compute identical bits.
@@ -43,7 +44,8 @@ struct Ctx {
   char* own = nullptr;    // this rank's shared buffer (data[2] then flags)
   uint32_t* counter = nullptr;  // private: epochs per row
   char* peer[MAX_WORLD] = {};   // every rank's buffer as mapped here (own included)
-  bool opened[MAX_WORLD] = {};
+  bool opened[MAX_WORLD] = {};  // peer[r] is an IPC mapping to close at destroy
+  uint64_t timeout_ns = 2000000000ull;  // limit of each wait for a peer's flag
 };
 
 struct Params {
@@ -55,6 +57,7 @@ struct Params {
   uint32_t* own_flags;
   uint32_t* counter;
   size_t data_bytes;
+  uint64_t timeout_ns;
   int world, rank, hidden, flags_off;
   float eps;
 };
@@ -104,7 +107,7 @@ __global__ void __launch_bounds__(THREADS) ar_add_rmsnorm_kernel(const Params p)
     if (ld_acquire_sys(f) < e) {
       const uint64_t t0 = gtime();
       while (ld_acquire_sys(f) < e) {
-        if (gtime() - t0 > 2000000000ull) {
+        if (gtime() - t0 > p.timeout_ns) {
           atomicOr(&g_ar_error, QX_DEVERR_PEER_TIMEOUT);
           break;
         }
@@ -121,9 +124,17 @@ __global__ void __launch_bounds__(THREADS) ar_add_rmsnorm_kernel(const Params p)
     xv[v] = make_uint4(0u, 0u, 0u, 0u);
     if (i < h8) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int r = 0; r < p.world; ++r) {
-        const uint4 d = __ldcg(reinterpret_cast<const uint4*>(p.buf[r] + off) + i);
-        const uint32_t dd[4] = {d.x, d.y, d.z, d.w};
+      // every rank's 16 bytes requested at once (NVLink round trips overlap),
+      // then summed in rank order
+      uint4 d[MAX_WORLD];
+#pragma unroll
+      for (int r = 0; r < MAX_WORLD; ++r)
+        d[r] = r < p.world ? __ldcg(reinterpret_cast<const uint4*>(p.buf[r] + off) + i)
+                           : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int r = 0; r < MAX_WORLD; ++r) {
+        if (r >= p.world) break;
+        const uint32_t dd[4] = {d[r].x, d[r].y, d[r].z, d[r].w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float2 f = h2_to_f2(dd[j]);
@@ -246,6 +257,37 @@ extern "C" int qx_nvlink_ar_open(void* ctx, const void* handles) {
   return QX_OK;
 }
 
+extern "C" int qx_nvlink_ar_open_local(void* ctx, void* const* ctxs) {
+  QX_REQUIRE(ctx && ctxs, "nvlink_ar_open_local: null argument");
+  auto* c = static_cast<nvar::Ctx*>(ctx);
+  for (int r = 0; r < c->world; ++r) {
+    if (r == c->rank) continue;
+    const auto* o = static_cast<const nvar::Ctx*>(ctxs[r]);
+    QX_REQUIRE(o && o->world == c->world && o->rank == r && o->max_rows == c->max_rows &&
+                   o->hidden == c->hidden,
+               "nvlink_ar_open_local: context %d is not rank %d of the same communicator", r, r);
+    if (o->device != c->device) {
+      int can = 0;
+      QX_CUDA_TRY(cudaDeviceCanAccessPeer(&can, c->device, o->device), "nvlink_ar_open_local: peer query");
+      QX_REQUIRE(can, "nvlink_ar_open_local: device %d cannot reach device %d", c->device, o->device);
+      const cudaError_t e = cudaDeviceEnablePeerAccess(o->device, 0);
+      if (e == cudaErrorPeerAccessAlreadyEnabled)
+        cudaGetLastError();
+      else
+        QX_CUDA_TRY(e, "nvlink_ar_open_local: enable peer access");
+    }
+    c->peer[r] = o->own;
+  }
+  return QX_OK;
+}
+
+extern "C" int qx_nvlink_ar_set_timeout(void* ctx, int64_t timeout_ns) {
+  QX_REQUIRE(ctx, "nvlink_ar_set_timeout: null context");
+  QX_REQUIRE(timeout_ns > 0, "nvlink_ar_set_timeout: timeout must be positive (ns)");
+  static_cast<nvar::Ctx*>(ctx)->timeout_ns = uint64_t(timeout_ns);
+  return QX_OK;
+}
+
 extern "C" int qx_nvlink_ar_destroy(void* ctx) {
   if (!ctx) return QX_OK;
   auto* c = static_cast<nvar::Ctx*>(ctx);
@@ -280,6 +322,7 @@ extern "C" int qx_nvlink_ar_add_rmsnorm(void* ctx, const void* partial, void* x,
   p.own_flags = reinterpret_cast<uint32_t*>(c->own + 2 * c->data_bytes);
   p.counter = c->counter;
   p.data_bytes = c->data_bytes;
+  p.timeout_ns = c->timeout_ns;
   p.world = c->world;
   p.rank = c->rank;
   p.hidden = c->hidden;

@@ -39,6 +39,12 @@ int device_sm_count();  // SM count of the current device (cached per device)
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // ---------------------------------------------------------------- device --
+// Limit of every bounded wait inside a kernel (mbarrier phases), measured with
+// %globaltimer: 2 s, far above any healthy wait, so that a GPU time-sliced
+// with other processes does not trip it; a wait that runs out sets an error
+// bit read by qx_get_device_error and the kernel returns.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
 __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
   // weights are read exactly once per call: do not keep them in L1
   uint4 r;

@@ -29,7 +29,7 @@
 //   parts of (alpha/r) h (two MMAs, ~22-bit product) and the LoRA B tile, both
 //   by TMA before the weight stream; warps 2-9 transpose the B tile into the
 //   K-major swizzled layout in shared memory.
-// Every wait is bounded (~200 ms, then QX_DEVERR_MBAR_TIMEOUT in the device
+// Every wait is bounded (2 s, then QX_DEVERR_MBAR_TIMEOUT in the device
 // error word); every copy targets this CTA only.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -109,7 +109,7 @@ __device__ __forceinline__ void bar_wait(uint32_t b, uint32_t parity) {
   while (!bar_try(b, parity)) {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    if (t - t0 > 200000000ull) {
+    if (t - t0 > kWaitLimitNs) {
       atomicOr(&g_gemm_error, QX_DEVERR_MBAR_TIMEOUT);
       return;
     }

@@ -58,7 +58,9 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstring>
 #include <map>
+#include <unordered_map>
 #include <mutex>
 #include <tuple>
 
@@ -228,13 +230,13 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Waits at most ~200 ms for the phase; on timeout records QX_DEVERR_MBAR_TIMEOUT
+// Waits at most kWaitLimitNs (2 s) for the phase; on timeout records QX_DEVERR_MBAR_TIMEOUT
 // in the device error word (read with qx_get_device_error) and returns false.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   while (!mbar_try(bar, parity)) {
-    if (global_ns() - t0 > 200000000ull) {
+    if (global_ns() - t0 > kWaitLimitNs) {
       atomicOr(&g_device_error, QX_DEVERR_MBAR_TIMEOUT);
       return false;
     }
@@ -862,7 +864,86 @@ static int encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* bas
 }
 
 template <int NT, int KPG>
+static int build_params(Params& prm, Plan* plo);
+template <int NT, int KPG>
+static int launch(const Params& prm, const Plan& pl, cudaStream_t st);
+
+// Launch parameters (plan and tensor maps) of recent calls, keyed by every
+// input that shapes them except the activations and the output: a decode loop
+// calls the same weights again and again, so the host work per call is a
+// lookup.  A tensor map only encodes an address, sizes and strides, so an
+// entry stays valid for whatever tensor later occupies the same address with
+// the same sizes.
+struct ParamKey {
+  const void *qw, *sc, *z, *A, *B;
+  int dev, M, K, N, rank, group, zp, zo, pdl, nt, kpg;
+  uint32_t ls;
+  bool operator==(const ParamKey& o) const {
+    return qw == o.qw && sc == o.sc && z == o.z && A == o.A && B == o.B && dev == o.dev && M == o.M &&
+           K == o.K && N == o.N && rank == o.rank && group == o.group && zp == o.zp && zo == o.zo &&
+           pdl == o.pdl && nt == o.nt && kpg == o.kpg && ls == o.ls;
+  }
+};
+struct ParamKeyHash {
+  size_t operator()(const ParamKey& k) const {
+    size_t h = 1469598103934665603ull;
+    auto mix = [&h](uint64_t v) { h = (h ^ v) * 1099511628211ull; };
+    mix(reinterpret_cast<uintptr_t>(k.qw));
+    mix(reinterpret_cast<uintptr_t>(k.sc));
+    mix(reinterpret_cast<uintptr_t>(k.z));
+    mix(reinterpret_cast<uintptr_t>(k.A));
+    mix(reinterpret_cast<uintptr_t>(k.B));
+    mix((uint64_t(k.M) << 32) ^ uint64_t(k.N) ^ (uint64_t(k.dev) << 56));
+    mix((uint64_t(k.K) << 32) ^ uint64_t(k.rank) ^ (uint64_t(k.nt) << 48) ^ (uint64_t(k.kpg) << 56));
+    mix((uint64_t(k.ls) << 32) ^ uint64_t(k.group) ^ (uint64_t(k.zp) << 16) ^ (uint64_t(k.zo) << 24) ^
+        (uint64_t(k.pdl) << 28));
+    return h;
+  }
+};
+struct ParamEntry {
+  Params prm;
+  Plan pl;
+};
+static std::mutex g_param_mu;
+static std::unordered_map<ParamKey, ParamEntry, ParamKeyHash> g_params;
+constexpr size_t PARAM_CACHE_MAX = 1024;
+
+template <int NT, int KPG>
 static int run(Params prm, cudaStream_t st) {
+  int dev = 0;
+  QX_CUDA_TRY(cudaGetDevice(&dev), "w4a16_gemv: cudaGetDevice");
+  uint32_t ls_bits;
+  std::memcpy(&ls_bits, &prm.lora_scale, 4);
+  const ParamKey key{prm.qw, prm.scales, prm.zeros, prm.A, prm.B, dev, prm.M, prm.K, prm.N, prm.rank,
+                     prm.group, prm.zeros_packed, prm.zero_offset, prm.pdl, NT, KPG, ls_bits};
+  Plan pl;
+  bool hit = false;
+  {
+    std::lock_guard<std::mutex> lk(g_param_mu);
+    auto it = g_params.find(key);
+    if (it != g_params.end()) {
+      const __half* x = prm.x;
+      __half* y = prm.y;
+      prm = it->second.prm;
+      prm.x = x;
+      prm.y = y;
+      pl = it->second.pl;
+      hit = true;
+    }
+  }
+  if (!hit) {
+    const int rc = build_params<NT, KPG>(prm, &pl);
+    if (rc != QX_OK) return rc;
+    std::lock_guard<std::mutex> lk(g_param_mu);
+    if (g_params.size() >= PARAM_CACHE_MAX) g_params.clear();
+    g_params.emplace(key, ParamEntry{prm, pl});
+  }
+  return launch<NT, KPG>(prm, pl, st);
+}
+
+// Plan and tensor maps of one call (everything but the activations and output).
+template <int NT, int KPG>
+static int build_params(Params& prm, Plan* plo) {
   Plan pl;
   int rc = make_plan<NT, KPG>(prm.M, prm.K, prm.N, prm.rank, prm.group, prm.zeros_packed, &pl);
   if (rc != QX_OK) return rc;
@@ -897,6 +978,12 @@ static int run(Params prm, cudaStream_t st) {
                    uint64_t(prm.rank), uint64_t(prm.N) * 2, COLS, uint32_t(prm.rank), "lora_B");
     if (rc != QX_OK) return rc;
   }
+  *plo = pl;
+  return QX_OK;
+}
+
+template <int NT, int KPG>
+static int launch(const Params& prm, const Plan& pl, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.tiles, pl.S, 1);
   cfg.blockDim = dim3(THREADS, 1, 1);

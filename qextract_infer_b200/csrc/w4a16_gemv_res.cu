@@ -147,12 +147,12 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Waits at most ~200 ms; on timeout sets QX_DEVERR_MBAR_TIMEOUT and returns false.
+// Waits at most kWaitLimitNs (2 s); on timeout sets QX_DEVERR_MBAR_TIMEOUT and returns false.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   while (!mbar_try(bar, parity)) {
-    if (global_ns() - t0 > 200000000ull) {
+    if (global_ns() - t0 > kWaitLimitNs) {
       atomicOr(&g_res_error, QX_DEVERR_MBAR_TIMEOUT);
       return false;
     }

@@ -45,6 +45,7 @@ import torch
 import torch.distributed as dist
 
 from . import _C
+from .tp_shard import merge_greedy, shard_quant_linear, shard_vocab
 
 
 @dataclass
@@ -80,17 +81,8 @@ class ShardedQuantLinear:
         A = (torch.randn(K, r, generator=g, device=device) * 0.02).half()
         B = (torch.randn(r, N, generator=g, device=device) * 0.02).half()
         qz = torch.full((K // G, N // 8), 0x88888888 - 2 ** 32, dtype=torch.int32, device=device)
-        if split == "col" and world > 1:
-            n = N // world
-            c0, c1 = rank * n, (rank + 1) * n
-            qw, sc, qz, B = qw[:, c0:c1], sc[:, c0:c1], qz[:, c0 // 8:c1 // 8], B[:, c0:c1]
-            N = n
-        elif split == "row" and world > 1:
-            k = K // world
-            k0, k1 = rank * k, (rank + 1) * k
-            qw, sc, qz, A = qw[k0 // 8:k1 // 8], sc[k0 // G:k1 // G], qz[k0 // G:k1 // G], A[k0:k1]
-            K = k
-        self.K, self.N = K, N
+        qw, sc, qz, A, B = shard_quant_linear(qw, sc, qz, A, B, split, rank, world, G)
+        self.K, self.N = qw.size(0) * 8, qw.size(1)
         self.qweight, self.scales, self.qzeros = qw.contiguous(), sc.contiguous(), qz.contiguous()
         self.lora_A, self.lora_B = A.contiguous(), B.contiguous()
         self.group = G
@@ -173,8 +165,7 @@ class TPDecoder:
             return (torch.randn(*shape, generator=gen, device=dev) * cfg.init_std).half()
 
         self.embed = normal((cfg.vocab, H), seed * 1000003 + 1)
-        vs = cfg.vocab // w
-        self.lm_head = normal((H, cfg.vocab), seed * 1000003 + 2)[:, r * vs:(r + 1) * vs].contiguous()
+        self.lm_head = shard_vocab(normal((H, cfg.vocab), seed * 1000003 + 2), r, w).contiguous()
         self.final_norm = normal((H,), seed * 1000003 + 3)
         self.layers = []
         for li in range(cfg.num_layers):
@@ -207,6 +198,13 @@ class TPDecoder:
         if self.world > 1 and nvlink_allreduce:
             from .nvlink_allreduce import NVLinkAllReduce
             self.ar = NVLinkAllReduce(group if group is not None else dist.group.WORLD, batch, H, dev)
+
+    def check_device_error(self) -> None:
+        """Raise if a bounded wait inside one of this rank's kernels ran out
+        (a peer that did not arrive, a stalled copy): the tokens of the steps
+        since the last check are then undefined.  Synchronises the device."""
+        with torch.cuda.device(self.device):
+            _C.check_device_error(f"tensor-parallel decoder rank {self.rank}")
 
     def close(self) -> None:
         """release the NVLink all-reduce buffers (collective: call on every rank)"""
@@ -283,9 +281,7 @@ class TPDecoder:
             idxs = [torch.empty_like(idx) for _ in range(self.world)]
             dist.all_gather(vals, val, group=self.group)
             dist.all_gather(idxs, idx, group=self.group)
-            v, i = torch.stack(vals), torch.stack(idxs)  # [world, B]
-            best = v.argmax(dim=0)
-            idx = i.gather(0, best[None, :])[0]
+            idx = merge_greedy(torch.stack(vals), torch.stack(idxs))  # [world, B] -> [B]
         return idx
 
     # ----------------------------------------------------------------- prefill

@@ -2,9 +2,10 @@
 
 Run from the repository root, with the QExtract-Infer sources available:
 
-    python tests/golden/make_golden.py [/path/to/QExtract_Infer]
+    python tests/golden/make_golden.py /path/to/QExtract_Infer
 
-(default path: /root/reference).  It imports, unmodified, the reference's
+(or with the path in the environment variable ``QEXTRACT_REF``).  It
+imports, unmodified, the reference's
 CPU reference functions
 
 * ``tests/test_w4a16_gemv.py``: ``simulate_gptq_quantize`` (:14-65),
@@ -166,7 +167,9 @@ def gen_ring(KVCache, out):
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("QEXTRACT_REF")
+    if not ref:
+        sys.exit("usage: make_golden.py /path/to/QExtract_Infer (or set QEXTRACT_REF)")
     sys.path.insert(0, ref)
     sys.path.insert(0, os.path.join(ref, "tests"))
     import test_rmsnorm  # noqa: E402

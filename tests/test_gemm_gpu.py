@@ -103,6 +103,32 @@ def test_qwen3_8b_shapes_reduced_rows(C, K, N):
     assert_close(y, _torch_ref(d, 128, 128.0, 64), RTOL, ATOL, f"K={K} N={N}")
 
 
+QWEN3_8B_PROJ = [("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 4096),
+                 ("gate", 4096, 12288), ("up", 4096, 12288), ("down", 12288, 4096)]
+
+
+@pytest.mark.parametrize("name,K,N", QWEN3_8B_PROJ, ids=[p[0] for p in QWEN3_8B_PROJ])
+def test_prefill_config_full_size(C, name, K, N):
+    """The prefill configuration at full size: M = 4096 tokens through each of
+    the 7 Qwen3-8B projections, GPTQ int4 g128 with packed qzeros (all 8),
+    LoRA r = 64, alpha / r = 2, x ~ N(0, 1), against the oracle's fp16-rounded
+    dequantised W followed by fp32 matmuls (reference math:
+    csrc/kernels/w4a16_lora_gemv.cu:268-323, tests/test_w4a16_gemv.py:178-186)."""
+    from oracle import cbind
+    d = _inputs(1, K, N, 64, 128, seed=K * 7 + N)
+    # x ~ N(0, 1) at 4096 rows from torch's CPU generator (the numpy one is slow at this size)
+    d["x"] = torch.randn(4096, K, generator=torch.Generator().manual_seed(K + N)).half().numpy()
+    y = _run(C, d, 128, 128.0, 64)
+    assert y.shape == (4096, N)
+    W = cbind.c_dequantize(d["qweight"], d["scales"], d["zeros"], 128)  # == oracle.dequantize_gptq
+    x = torch.from_numpy(d["x"]).cuda().float()
+    ref = x @ torch.from_numpy(W).cuda().float()
+    A = torch.from_numpy(d["lora_A"]).cuda().float()
+    B = torch.from_numpy(d["lora_B"]).cuda().float()
+    ref = (ref + 2.0 * ((x @ A) @ B)).half().cpu().numpy()
+    assert_close(y, ref, RTOL, ATOL, f"{name} M=4096 K={K} N={N}")
+
+
 def test_matches_decode_gemv(C):
     """the GEMM at 128 rows against the decode GEMV on the same rows (32 at a time)"""
     d = _inputs(128, 1024, 512, 16, 128, seed=11, random_zeros=True)

@@ -23,6 +23,8 @@ def test_gptq_gemv_matches_reference(case):
         # dequantisation is bit-exact against dequantize_gptq_ref
         np.testing.assert_array_equal(dequantize_gptq(qw, s, z).view(np.uint16),
                                       d["w_dequant"].view(np.uint16))
+        np.testing.assert_array_equal(cbind.c_dequantize(qw, s, z).view(np.uint16),
+                                      d["w_dequant"].view(np.uint16))
     yf = w4a16_gemv_ref(x, qw, s, z, return_f32=True)
     np.testing.assert_allclose(yf, d["y_base_f32"], rtol=1e-5, atol=1e-5)
     assert_f16_match(w4a16_gemv_ref(x, qw, s, z), d["y_base"])
@@ -55,6 +57,10 @@ def test_packed_qzeros_matches_reference():
     np.testing.assert_allclose(yl, d["y_lora_f32"], rtol=1e-5, atol=1e-5)
     yc = cbind.c_w4a16_lora_gemv(*args, lora_alpha=float(d["alpha"]))
     assert_f16_match(yc, d["y_lora"])
+    for off in (0, 1):  # the C dequantisation (large checks) equals the numpy one, bit for bit
+        np.testing.assert_array_equal(
+            cbind.c_dequantize(d["qweight"], d["scales"], d["qzeros"], zero_offset=off).view(np.uint16),
+            dequantize_gptq(d["qweight"], d["scales"], d["qzeros"], zero_offset=off).view(np.uint16))
     # GPTQ-v1 storage (+1): identical to unpacked zeros + 1
     np.testing.assert_array_equal(unpack_qzeros(d["qzeros"], N, zero_offset=1),
                                   d["zeros_unpacked"] + 1)
