@@ -56,14 +56,9 @@ def measured_peaks():
 
 
 def gemv_kernel_name():
-    """The kernel qx_w4a16_lora_gemv runs for the decode shape (its own routing)."""
-    import ctypes
-    from qextract_infer_b200 import _lib
-    k = ctypes.c_int(0)
-    _lib.check(_lib.load().qx_w4a16_gemv_route(M, K, N, RANK, GROUP, 1, ctypes.byref(k)),
-               "w4a16_gemv_route")
-    return ("qx::gres::w4a16_gemv_res_kernel<4, 1>" if k.value == 1
-            else "qx::gemv::w4a16_gemv_kernel<1, 4>")
+    """The kernel qx_w4a16_lora_gemv runs for the decode shape (one row: NT = 1,
+    128-row groups: KPG = 4)."""
+    return "qx::gemv::w4a16_gemv_kernel<1, 4>"
 
 
 def profiled_traffic():
@@ -282,19 +277,30 @@ def run_b200(args):
         ev1.synchronize()
         torch.cuda.synchronize(device)
         ms = ev0.elapsed_time(ev1)
-        # e2e through the public API: pinned host x -> device buffer, GEMV into a
-        # device output buffer, y -> pinned host, every step
+        # e2e through the reference-facing C-ABI with host buffers, as a C, cgo
+        # or ctypes caller makes it: pinned host x -> device (qx_copy_async),
+        # qx_w4a16_lora_gemv, device y -> pinned host, every step
+        from qextract_infer_b200 import _lib
+        lib = _lib.load()
         x_host = torch.randn(M, K).half().pin_memory()
         y_host = torch.empty(M, N, dtype=torch.float16).pin_memory()
         x_dev = torch.empty(M, K, dtype=torch.float16, device=device)
         y_dev = torch.empty(M, N, dtype=torch.float16, device=device)
         e_steps = 0 if args.skip_e2e else max(1, min(steps, 2000))
+        raw = stream.cuda_stream
+        xh, yh, xd, yd = x_host.data_ptr(), y_host.data_ptr(), x_dev.data_ptr(), y_dev.data_ptr()
+        xb, yb = M * K * 2, M * N * 2
+        cargs = [(qw.data_ptr(), sc.data_ptr(), qz.data_ptr(), 1, 0, A.data_ptr(), B.data_ptr())
+                 for qw, sc, qz, A, B in sets]
+        scale = float(np.float32(ALPHA) / np.float32(RANK))
+        copy, gemv = lib.qx_copy_async, lib.qx_w4a16_lora_gemv
 
         def e2e_step(i):
-            x_dev.copy_(x_host, non_blocking=True)
-            qw, sc, qz, A, B = sets[i % nsets]
-            qx.w4a16_lora_gemv(x_dev, qw, sc, qz, A, B, GROUP, ALPHA, out=y_dev)
-            y_host.copy_(y_dev, non_blocking=True)
+            copy(xd, xh, xb, raw)
+            rc = gemv(xd, *cargs[i % nsets], yd, M, K, N, RANK, GROUP, scale, raw)
+            copy(yh, yd, yb, raw)
+            if rc:
+                _lib.check(rc, "w4a16_lora_gemv")
 
         with torch.cuda.stream(stream):
             for i in range(nsets if e_steps else 0):  # every weight set once: cached launch plans
@@ -356,7 +362,8 @@ def run_b200(args):
                     "value": BYTES_PER_CALL * e_steps / (e_ms / 1e3) / 1e9 * world, "unit": "GB/s",
                     "us_per_call": e_ms * 1e3 / e_steps,
                     "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
-                    "api": "qextract_infer_b200.w4a16_lora_gemv (ctypes C-ABI)"},
+                    "api": "C-ABI qx_copy_async + qx_w4a16_lora_gemv + qx_copy_async (ctypes), "
+                           "host buffers pinned"},
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": steps,

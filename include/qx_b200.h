@@ -50,6 +50,11 @@ const char* qx_last_error(void);
 int qx_get_device_error(unsigned* code, int reset);
 /* Library version string. */
 const char* qx_version(void);
+/* Host plumbing for callers without their own CUDA runtime binding (ctypes,
+ * cgo, JNI): one cudaMemcpyAsync of `bytes` from src to dst on `stream`, the
+ * direction taken from the pointers (pinned host or device).  No counterpart
+ * in the reference (its pybind layer moves data with torch). */
+int qx_copy_async(void* dst, const void* src, size_t bytes, qx_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * W4A16(-LoRA) GEMV.
@@ -92,18 +97,6 @@ int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const void* scales
  * before on the same stream (true for model weights).  Returns 0. */
 int qx_set_pdl(int enable);
 
-/* Which decode kernel qx_w4a16_lora_gemv runs for a shape (new component;
- * the reference has one kernel, w4a16_lora_gemv.cu:155-226).  *kernel = 1:
- * the resident kernel (up to 4 rows whose weight slice fits half of an SM's
- * shared memory: one CTA per SM holds its whole slice of 8-column units, so
- * the next call's weights stream while this call computes; integer tensor-core
- * main loop with the activations as exact 15-bit fixed point per group);
- * 0: the clustered split-K kernel.  Returns 0. */
-int qx_w4a16_gemv_route(int M, int K, int N, int rank, int group_size, int zeros_packed,
-                        int* kernel);
-/* 1 lets qx_w4a16_gemv_route pick the resident kernel where it fits; 0
- * (default) routes every shape to the clustered split-K kernel.  Returns 0. */
-int qx_set_gemv_resident(int enable);
 
 /* ------------------------------------------------------------------------
  * W4A16-LoRA GEMM on the tcgen05 tensor cores (prefill, large M).

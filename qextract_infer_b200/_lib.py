@@ -23,12 +23,11 @@ c_int, c_int64, c_float, c_size_t, c_void_p, c_char_p = (
 SIGNATURES = {
     "qx_last_error": (c_char_p, []),
     "qx_version": (c_char_p, []),
+    "qx_copy_async": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
     "qx_w4a16_lora_gemv": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p,
                                    c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float,
                                    c_void_p]),
     "qx_set_pdl": (c_int, [c_int]),
-    "qx_w4a16_gemv_route": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),
-    "qx_set_gemv_resident": (c_int, [c_int]),
     "qx_w4a16_lora_gemm_sm100_workspace_size": (c_size_t, [c_int, c_int]),
     "qx_w4a16_lora_gemm_sm100": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                          c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,

@@ -49,3 +49,11 @@ int device_sm_count() {
 extern "C" const char* qx_last_error(void) { return qx::g_last_error; }
 
 extern "C" const char* qx_version(void) { return "qextract_infer_b200 0.1.0 (sm_100a)"; }
+
+extern "C" int qx_copy_async(void* dst, const void* src, size_t bytes, qx_stream_t stream) {
+  if (bytes == 0) return QX_OK;
+  QX_REQUIRE(dst && src, "copy_async: null pointer");
+  QX_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, reinterpret_cast<cudaStream_t>(stream)),
+              "copy_async");
+  return QX_OK;
+}

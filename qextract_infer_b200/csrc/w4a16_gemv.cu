@@ -1031,10 +1031,6 @@ using namespace qx;
 namespace qx {
 int gemm_device_error(unsigned* code, int reset);      // w4a16_gemm.cu
 int nvar_device_error(unsigned* code, int reset);      // nvlink_allreduce.cu
-int gemv_res_device_error(unsigned* code, int reset);  // w4a16_gemv_res.cu
-int gemv_resident(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
-                  int zeros_packed, int zero_offset, const void* lora_A, const void* lora_B, void* y,
-                  int M, int K, int N, int rank, int group, float lora_scale, cudaStream_t st);
 }
 
 extern "C" int qx_get_device_error(unsigned* code, int reset) {
@@ -1051,9 +1047,6 @@ extern "C" int qx_get_device_error(unsigned* code, int reset) {
   if (rc != QX_OK) return rc;
   *code |= other;
   rc = qx::nvar_device_error(&other, reset);
-  if (rc != QX_OK) return rc;
-  *code |= other;
-  rc = qx::gemv_res_device_error(&other, reset);
   if (rc != QX_OK) return rc;
   *code |= other;
   return QX_OK;
@@ -1089,11 +1082,6 @@ extern "C" int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const v
              "w4a16_gemv: misaligned zeros/y");
   QX_REQUIRE(zeros_packed == 0 || zeros_packed == 1, "w4a16_gemv: zeros_packed must be 0 or 1");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  // a few rows whose weight slice fits half an SM: the resident kernel
-  // (w4a16_gemv_res.cu); it launches nothing when the shape does not suit it
-  const int rrc = gemv_resident(x, qweight, scales, zeros, zeros_packed, zero_offset, lora_A, lora_B,
-                                y, M, K, N, rank, group_size, lora_scale, st);
-  if (rrc != QX_ERR_UNSUPPORTED) return rrc;
   // up to 32 rows per launch; fewer when the activations of 32 rows and the
   // kernel's weight stages do not fit in shared memory together
   int mrows = gemv::MROWS;
