@@ -97,6 +97,19 @@ int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const void* scales
  * before on the same stream (true for model weights).  Returns 0. */
 int qx_set_pdl(int enable);
 
+/* The split-K plan qx_w4a16_lora_gemv uses for a shape (at most 32 rows of M
+ * per launch): out[0] = 256-column tiles, out[1] = CTAs splitting K per tile
+ * (the cluster size S), out[2] = weight stages in flight per CTA, out[3] =
+ * quantisation groups of the longest CTA, out[4] = shared memory per CTA in
+ * bytes.  Plans are chosen on the current device.  New component (the
+ * reference has one launch shape).  Returns 0 or an error status. */
+int qx_w4a16_gemv_plan(int M, int K, int N, int rank, int group_size, int zeros_packed, int* out);
+/* Pins the split-K plan of every later qx_w4a16_lora_gemv call whose shape
+ * admits it: S CTAs per tile and nst weight stages (0 = chosen per shape);
+ * shapes the pinned plan does not fit fail with QX_ERR_UNSUPPORTED.  For
+ * tuning; process-wide.  Returns 0 or QX_ERR_INVALID. */
+int qx_w4a16_gemv_pin_plan(int S, int nst);
+
 
 /* ------------------------------------------------------------------------
  * W4A16-LoRA GEMM on the tcgen05 tensor cores (prefill, large M).

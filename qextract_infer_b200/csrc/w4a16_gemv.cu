@@ -38,11 +38,14 @@
 //             and Off / Sx come from a second MMA of the same activation
 //             fragments against a constant matrix (rows 1024|64 and 1|1).
 //   LoRA    = h_s = x[:, Ks] A[Ks, :] on the tensor cores (ldmatrix.trans
-//             of the staged A slice): by the helper while the compute warps
-//             stream the weights for up to 8 rows and ranks below 32, else by
-//             the compute warps (tiles split over the 8 warps); the LoRA product is
-//             linear in K, so each CTA adds (alpha/r) h_s B[:, tile] into its
-//             own partial sums and no h is exchanged.
+//             of A): each ring stage carries its group's LoRA A rows beside
+//             the weights (one bulk copy), so h_s accumulates group by group
+//             and no CTA holds an A slice the size of its K range (which at
+//             ranks 32-48 and deep K cost whole CTAs of occupancy); by the
+//             helper warp for up to 8 rows and ranks below 32, else by the
+//             compute warps (16 x 8 tiles spread over the warps).  The LoRA
+//             product is linear in K, so each CTA adds (alpha/r) h_s B[:, tile]
+//             into its own partial sums and no h is exchanged.
 //   reduce  = each CTA sends its fp32 partial of the columns owned by CTA j
 //             straight into CTA j's shared memory with st.async, which
 //             completes on CTA j's receive mbarrier; CTA j waits for its
@@ -63,6 +66,7 @@
 #include <unordered_map>
 #include <mutex>
 #include <tuple>
+#include <type_traits>
 
 #include "qx_b200.h"
 #include "qx_common.cuh"
@@ -70,6 +74,8 @@
 namespace qx {
 
 std::atomic<int> g_pdl_enabled{1};
+// split-K plan pinned by qx_w4a16_gemv_pin_plan (0: chosen per shape)
+std::atomic<int> g_pin_S{0}, g_pin_nst{0};
 
 // Sticky device-side error word (QX_DEVERR_* bits), read by qx_get_device_error.
 static __device__ unsigned g_device_error = 0;
@@ -81,7 +87,7 @@ constexpr int THREADS = (WARPS + 1) * 32;  // + the helper warp
 constexpr int COLS = WARPS * 32;         // output columns per tile
 constexpr int KSTEP = 32;                // K rows per step (4 packed rows)
 constexpr int ROWB = 1056;               // smem bytes per staged packed row (1 KB + 32 B: no bank conflicts)
-constexpr int MAX_NST = 4;               // weight stages (quantisation groups) resident per CTA
+constexpr int MAX_NST = 4;               // weight stages (quantisation groups) in flight per CTA
 constexpr int MROWS = 32;                // batch rows per launch (4 n-tiles of 8)
 constexpr int MAX_S = 16;                // largest cluster (non-portable size)
 constexpr size_t SMEM_LIMIT = 227 * 1024;
@@ -90,7 +96,7 @@ __host__ __device__ constexpr int ctas_per_sm(int nt) { return nt == 1 ? 3 : (nt
 
 // Shared-memory carve-up (byte offsets), identical on host and device.
 struct Layout {
-  unsigned bars, ring, sz_s, sz_z, sf, xraw, xs, xks, As, Bs, hs, recv, total;
+  unsigned bars, ring, sz_s, sz_z, sf, xraw, xs, xks, Bs, hs, recv, total;
 };
 
 struct alignas(64) Params {
@@ -109,6 +115,7 @@ struct alignas(64) Params {
   int zeros_tma;  // zero points by TMA (fp16 always; packed when rows are 16 B multiples)
   float lora_scale;
   int T, S, cpr, Ts_max, gmax, nst, pdl;
+  int stage;                    // bytes per ring stage: a group's packed weights, then its LoRA A rows
   uint32_t s_magic, cpr_magic;  // ceil(2^32 / S) (S > 1), ceil(2^32 / cpr): exact floor division of small values
   Layout lay;                   // shared-memory carve-up, computed on the host
 };
@@ -127,16 +134,19 @@ __host__ __device__ inline int xstride(int Ts_max) { return Ts_max * KSTEP + 8; 
 // columns each CTA of an S-cluster finalises: 256 / S rounded up to 8
 __host__ __device__ inline int owner_cols(int S) { return ((COLS + S - 1) / S + 7) / 8 * 8; }
 
-// LoRA down-projection on the compute warps for batches above 8 rows or
-// ranks of 32 and more, as (16-row block, 8-rank block) tiles split into k
-// parts so that each warp has an item; else the helper warp computes it while
-// the compute warps stream the weights.
+// LoRA down-projection, one quantisation group at a time as its ring stage
+// lands (the stage holds the group's LoRA A rows beside its weights, so no
+// CTA keeps an A slice the size of its K range): on the compute warps for
+// batches above 8 rows or ranks of 32 and more, as (16-row block, 8-rank
+// block) tiles spread over the warps; else on the helper warp while the
+// compute warps stream the weights.
 __host__ __device__ inline bool lora_on_warps(int M, int rank) { return rank > 0 && (M > 8 || rank >= 32); }
 __host__ __device__ inline int lora_tiles(int M, int rank) { return ((M + 15) / 16) * (rank / 8); }
-__host__ __device__ inline int lora_kparts(int M, int rank) {
-  if (!lora_on_warps(M, rank)) return 1;
-  const int t = lora_tiles(M, rank);
-  return t >= WARPS ? 1 : WARPS / t;
+// tiles per compute warp (registers of the kernel instance: NT batch tiles)
+__host__ __device__ constexpr int lora_items(int nt) { return nt == 4 ? 4 : 2; }
+// bytes of one ring stage: KPG*4 packed rows of 1056 B, then KPG*32 rows of A
+__host__ __device__ inline int stage_bytes(int KPG, int rank) {
+  return (KPG * 4 * ROWB + KPG * KSTEP * rank * 2 + 127) & ~127;
 }
 
 // M = batch rows of this launch (<= 32).
@@ -147,16 +157,15 @@ __host__ __device__ inline Layout layout(int M, int KPG, int Ts_max, int rank, i
   Layout L;
   unsigned o = 0;
   L.bars = take(o, size_t(4 + 2 * nst) * 8);  // statics, B, h, recv, full[nst], empty[nst]
-  L.ring = take(o, size_t(nst) * KPG * 4 * ROWB);     // weight stages
+  L.ring = take(o, size_t(nst) * stage_bytes(KPG, rank));  // weight (+ LoRA A) stages
   L.sz_s = take(o, size_t(gmax) * COLS * 2);          // scales [gmax][256]
   L.sz_z = take(o, size_t(gmax) * (zeros_packed ? COLS / 2 : COLS * 2));  // [gmax][32] u32 or [gmax][256] fp16
   L.sf = take(o, size_t(gmax) * COLS * 8);            // (s, s*z) as floats [gmax][256]
   L.xraw = take(o, size_t(M) * xstride(Ts_max) * 2);  // activations [M][Ks(+8)]
-  L.xs = take(o, size_t(Ts_max) * Mp * 4 * 16);       // in MMA-B order [t][Mp][c], rows >= M zero
+  L.xs = take(o, size_t(Ts_max) * M * 4 * 16 + 64);   // in MMA-B order [t][M][c], then a zero block
   L.xks = take(o, size_t(gmax) * Mp * 2 * 4);         // per group (Off, Sx) per row [g][Mp]
-  L.As = take(o, size_t(Ts_max) * KSTEP * rank * 2);  // LoRA A slice [Ks][r]
   L.Bs = take(o, size_t(rank) * COLS * 2);            // LoRA B tile [r][256]
-  L.hs = take(o, size_t(lora_kparts(M, rank)) * M * rank * 4);  // h_s [parts][M][r]
+  L.hs = take(o, size_t(M) * rank * 4);                // h_s [M][r]
   L.recv = take(o, size_t(S) * M * owner_cols(S) * 4);  // partials from the cluster [S][M][cpr]
   L.total = o;
   return L;
@@ -288,8 +297,9 @@ __device__ __forceinline__ uint32_t map_rank(uint32_t addr, int rank) {
   return r;
 }
 
-// KPG = k-steps per quantisation group (group_size / 32).
-template <int NT, int KPG>
+// KPG = k-steps per quantisation group (group_size / 32); LW = the LoRA
+// down-projection on the compute warps (lora_on_warps), else on the helper.
+template <int NT, int KPG, bool LW>
 __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     w4a16_gemv_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -308,9 +318,12 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   const int Ks = ngrp * KPG * KSTEP;
   const int XS = xstride(p.Ts_max);
   const int M = p.M, N = p.N, R = p.rank;
-  constexpr int STAGE = KPG * 4 * ROWB;
+  constexpr int WBYTES = KPG * 4 * ROWB;  // the weights of a stage (full box, zero-filled past N)
+  constexpr int GROUPK = KPG * KSTEP;      // rows of a quantisation group
   constexpr int Mp = NT * 8;
-  constexpr uint32_t STAGE_TX = uint32_t(STAGE);  // full box, zero-filled past N
+  const int STAGE = p.stage;
+  const uint32_t ABYTES = uint32_t(GROUPK * p.rank) * 2u;  // the group's LoRA A rows
+  const uint32_t STAGE_TX = uint32_t(WBYTES) + ABYTES;
   const int nst = p.nst;
   const int n_tile0 = tile * COLS;
   const int k0 = ks0 * KSTEP;
@@ -339,9 +352,12 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     mbar_init(bar_b, 1);
     mbar_init(bar_h, 32);
     mbar_init(bar_rv, 1);
+    // a stage is free once every compute warp, and the helper when it takes
+    // the group's LoRA A rows, has read it
+    const int readers = WARPS + ((p.rank > 0 && !lora_on_warps(p.M, p.rank)) ? 1 : 0);
     for (int i = 0; i < nst; ++i) {
       mbar_init(full0 + 8 * i, 1);
-      mbar_init(empty0 + 8 * i, WARPS);
+      mbar_init(empty0 + 8 * i, readers);
     }
     asm volatile("fence.mbarrier_init.release.cluster;\nfence.proxy.async.shared::cta;" :::
                      "memory");
@@ -353,21 +369,21 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
 
   if (warp == WARPS) {
     // ---------------- helper warp ----------------
-    __half* As = reinterpret_cast<__half*>(smem + L.As);
     if (lane == 0) {
       // bytes the S CTAs of the cluster will send for this CTA's columns
       mbar_expect_tx(bar_rv, uint32_t(S * M * own_cols) * 4u);
       const uint32_t sz_bytes =
           uint32_t(p.gmax) * (COLS * 2 + (p.zeros_tma ? (p.zeros_packed ? COLS / 2 : COLS * 2) : 0));
-      mbar_expect_tx(bar_st, sz_bytes + uint32_t(Ks * R) * 2);
-      // LoRA A rows (the helper's next job), the weight groups, scales / fp16
-      // zero points of this CTA's groups (gmax rows; rows past the CTA's
-      // range are read but unused), the LoRA B tile
-      if (R > 0) bulk_g2s(smem_addr(As), p.A + size_t(k0) * R, uint32_t(Ks * R) * 2, bar_st);
+      mbar_expect_tx(bar_st, sz_bytes);
+      // the weight groups with their LoRA A rows, scales / fp16 zero points of
+      // this CTA's groups (gmax rows; rows past the CTA's range are read but
+      // unused), the LoRA B tile
       const uint64_t pol = evict_first_policy();
       for (int i = 0; i < min(ngrp, nst); ++i) {
         mbar_expect_tx(full0 + 8 * i, STAGE_TX);
         tma_2d_hint(ring_s + i * STAGE, &p.tw, wx, (ks0 + i * KPG) * 4, full0 + 8 * i, pol);
+        if (R > 0)
+          bulk_g2s(ring_s + i * STAGE + WBYTES, p.A + size_t(k0 + i * GROUPK) * R, ABYTES, full0 + 8 * i);
       }
       tma_2d(smem_addr(smem + L.sz_s), &p.ts, n_tile0, gr0, bar_st);
       if (p.zeros_tma)
@@ -391,7 +407,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   }
 
   // activations (plain 128-bit loads) in MMA-B order (x0,x4 | x1,x5 | x2,x6 | x3,x7) per packed row,
-  // rows M..Mp-1 zero, and per group the sums over the two nibble classes:
+  // and per group the sums over the two nibble classes:
   // (Off, Sx) = (1024 Xa + 64 Xb, Xa + Xb), by the whole CTA.  A group of a
   // row is an aligned block of 4*KPG lanes (whole warps join the shuffles).
   {
@@ -400,10 +416,8 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     float* xksw = reinterpret_cast<float*>(smem + L.xks);
     // work in chunks of 32 items (8 k-steps, whole groups) of one row, spread over the warps
     const int TB = (Ts + 7) >> 3;  // chunks per row
-    for (int id = warp; id < (Mp - M) * TB; id += WARPS + 1) {  // zero rows
-      const int mz = id / TB, it = (id - mz * TB) * 32 + lane;
-      if (it < Ts * 4) xsw[((it >> 2) * Mp + M + mz) * 4 + (it & 3)] = make_uint4(0u, 0u, 0u, 0u);
-    }
+    // rows M..Mp-1 of every B fragment read one zero block past the rows
+    if (tid < 4) xsw[size_t(p.Ts_max) * M * 4 + tid] = make_uint4(0u, 0u, 0u, 0u);
     // the activations may come from the previous kernel in the stream: wait
     // for it here, after every weight and static copy has been started
     if (p.pdl) grid_dep_wait();
@@ -415,7 +429,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
       if (ok) {
         v = *reinterpret_cast<const uint4*>(xg + size_t(m) * p.K + t * KSTEP + cc * 8);
         *reinterpret_cast<uint4*>(xraw + m * XS + t * KSTEP + cc * 8) = v;  // natural order, LoRA-down
-        xsw[(t * Mp + m) * 4 + cc] = make_uint4(prmt(v.x, v.z, 0x5410u), prmt(v.x, v.z, 0x7632u),
+        xsw[(t * M + m) * 4 + cc] = make_uint4(prmt(v.x, v.z, 0x5410u), prmt(v.x, v.z, 0x7632u),
                                                 prmt(v.y, v.w, 0x5410u), prmt(v.y, v.w, 0x7632u));
       }
       const float2 a0 = h2_to_f2(v.x), a1 = h2_to_f2(v.y), a2 = h2_to_f2(v.z), a3 = h2_to_f2(v.w);
@@ -450,89 +464,82 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   }
   __syncthreads();  // permuted activations, group sums, scales ready
 
-  const bool lora_warps = lora_on_warps(M, R);
+  constexpr bool lora_warps = LW;  // == lora_on_warps(M, R), chosen by the host
   if (warp == WARPS) {  // helper: the LoRA down-projection of small batches and ranks
     if (R == 0 || lora_warps) return;
-    __half* As = reinterpret_cast<__half*>(smem + L.As);
     float* hs = reinterpret_cast<float*>(smem + L.hs);
-    // LoRA down-projection h_s^T[r][m] = A^T[r][Ks] . x^T[Ks][m]: 16 x 8 tiles
-    // (rank rows x batch rows), two accumulators per tile (even / odd k blocks)
-    mbar_wait(bar_st, 0);
-    const int RT = R >= 16 ? R / 16 : 1;
-    const int KB = Ks / 16;
+    // h_s^T[r][m] = A^T[r][Ks] . x^T[Ks][m] as one 16 x 8 tile (rank rows x
+    // batch rows; ranks 8 and 16, at most 8 rows), two accumulators (even /
+    // odd k blocks), one group per ring stage as it lands
     const int mi = lane >> 3, ri = lane & 7;
-    for (int tl = 0; tl < RT * NT; ++tl) {
-      const int rt = tl / NT, nt = tl - rt * NT;
-      const int mb = nt * 8 + g;  // batch row of this lane's B fragment
-      const __half* xrow = xraw + mb * XS + 2 * c;
-      const int j = rt * 16 + 8 * (mi & 1);
-      float h4[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      for (int kb = 0; kb < KB; kb += 2) {
+    const __half* xrow = xraw + g * XS + 2 * c;  // batch row g of the B fragment
+    const int j = 8 * (mi & 1);
+    float h4[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    int hst = 0, huse = 0;
+    for (int gi = 0; gi < ngrp; ++gi) {
+      mbar_wait(full0 + 8 * hst, huse & 1);
+      const __half* Ag = reinterpret_cast<const __half*>(smem + L.ring + hst * STAGE + WBYTES);
+#pragma unroll
+      for (int kb = 0; kb < 2 * KPG; kb += 2) {
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int k = (kb + u) * 16 + ri + 8 * (mi >> 1);
           uint32_t a[4];
           if (R >= 16) {
-            ldsm_x4_t(a, As + k * R + j);
+            ldsm_x4_t(a, Ag + k * R + j);
           } else {  // rank 8: rows 8..15 of the tile are zero
-            ldsm_x4_t(a, As + k * R + (j & 7));
+            ldsm_x4_t(a, Ag + k * R + (j & 7));
             a[1] = 0u;
             a[3] = 0u;
           }
           uint32_t b0 = 0u, b1 = 0u;
-          if (mb < M) {
-            b0 = *reinterpret_cast<const uint32_t*>(xrow + (kb + u) * 16);
-            b1 = *reinterpret_cast<const uint32_t*>(xrow + (kb + u) * 16 + 8);
+          if (g < M) {
+            b0 = *reinterpret_cast<const uint32_t*>(xrow + gi * GROUPK + (kb + u) * 16);
+            b1 = *reinterpret_cast<const uint32_t*>(xrow + gi * GROUPK + (kb + u) * 16 + 8);
           }
           mma_16816(h4[u], a[0], a[1], a[2], a[3], b0, b1);
         }
       }
-      const int j0 = rt * 16 + g, m0 = nt * 8 + 2 * c;
-      if (m0 < M) hs[m0 * R + j0] = h4[0][0] + h4[1][0];
-      if (m0 + 1 < M) hs[(m0 + 1) * R + j0] = h4[0][1] + h4[1][1];
-      if (j0 + 8 < R) {
-        if (m0 < M) hs[m0 * R + j0 + 8] = h4[0][2] + h4[1][2];
-        if (m0 + 1 < M) hs[(m0 + 1) * R + j0 + 8] = h4[0][3] + h4[1][3];
+      if (gi + nst < ngrp) {  // the compute warps refill this stage
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * hst);
       }
+      if (++hst == nst) {
+        hst = 0;
+        ++huse;
+      }
+    }
+    const int j0 = g, m0 = 2 * c;
+    if (m0 < M) hs[m0 * R + j0] = h4[0][0] + h4[1][0];
+    if (m0 + 1 < M) hs[(m0 + 1) * R + j0] = h4[0][1] + h4[1][1];
+    if (j0 + 8 < R) {
+      if (m0 < M) hs[m0 * R + j0 + 8] = h4[0][2] + h4[1][2];
+      if (m0 + 1 < M) hs[(m0 + 1) * R + j0 + 8] = h4[0][3] + h4[1][3];
     }
     mbar_arrive(bar_h);  // every lane: its h_s stores are released
     return;
   }
 
   // ---------------- compute warps ----------------
-  const int KP = lora_kparts(M, R);  // h_s partial sums (1: the helper's complete h_s)
-  if (lora_warps) {
-    // LoRA down-projection h_s = x[:, Ks] A[Ks, :] on the compute warps:
-    // C[16 rows][8 ranks] tiles (mma.sync), each split into KP interleaved k
-    // parts (k16 blocks), item w = (tile, part) on warp w % 8; partial sums to
-    // hs[part][row][rank], summed in part order where the LoRA term is applied
-    const __half* As = reinterpret_cast<const __half*>(smem + L.As);
-    float* hp = reinterpret_cast<float*>(smem + L.hs);
-    const int RT8 = R >> 3, ntl = lora_tiles(M, R), KB = Ks >> 4;
-    for (int w = warp; w < ntl * KP; w += WARPS) {
-      const int tl = w % ntl, kp = w / ntl;
-      const int mt = tl / RT8, rt = tl - mt * RT8;
-      const int m0 = mt * 16 + g, m1 = m0 + 8;
-      const __half* x0 = xraw + (m0 < M ? m0 : 0) * XS + 2 * c;
-      const __half* x1 = xraw + (m1 < M ? m1 : 0) * XS + 2 * c;
-      float h[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int kb = kp; kb < KB; kb += KP) {
-        const uint32_t a0 = m0 < M ? *reinterpret_cast<const uint32_t*>(x0 + kb * 16) : 0u;
-        const uint32_t a2 = m0 < M ? *reinterpret_cast<const uint32_t*>(x0 + kb * 16 + 8) : 0u;
-        const uint32_t a1 = m1 < M ? *reinterpret_cast<const uint32_t*>(x1 + kb * 16) : 0u;
-        const uint32_t a3 = m1 < M ? *reinterpret_cast<const uint32_t*>(x1 + kb * 16 + 8) : 0u;
-        uint32_t bf[2];
-        ldsm_x2_t(bf, As + (kb * 16 + (lane & 15)) * R + rt * 8);
-        mma_16816(h, a0, a1, a2, a3, bf[0], bf[1]);
-      }
-      float* dst = hp + size_t(kp) * M * R + rt * 8 + 2 * c;
-      if (m0 < M) *reinterpret_cast<float2*>(dst + m0 * R) = make_float2(h[0], h[1]);
-      if (m1 < M) *reinterpret_cast<float2*>(dst + m1 * R) = make_float2(h[2], h[3]);
-    }
-  }
+  // LoRA down-projection items of this warp (batches above 8 rows, ranks of
+  // 32 and more): (16-row block, 8-rank block) tiles warp, warp + 8, ...,
+  // accumulated over the groups in registers
+  constexpr int LITEMS = LW ? lora_items(NT) : 1;
+  float hl[LITEMS][4];
+#pragma unroll
+  for (int ii = 0; ii < LITEMS; ++ii) hl[ii][0] = hl[ii][1] = hl[ii][2] = hl[ii][3] = 0.f;
   const int lcol = warp * 32 + 4 * g;  // first of this lane's 4 columns (tile-local)
   const bool col_ok = n_tile0 + lcol < N;  // N % 8 == 0: all 4 columns valid or none
   const uint4* xs = reinterpret_cast<const uint4*>(smem + L.xs);
+  // B fragment rows nt*8 + g: the staged row, or the zero block (stride 0) past M
+  const uint4* xrow[NT];
+  int xstep[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int row = nt * 8 + g;
+    xrow[nt] = row < M ? xs + row * 4 + c : xs + size_t(p.Ts_max) * M * 4 + c;
+    xstep[nt] = row < M ? M * 4 : 0;
+  }
   const float* xks = reinterpret_cast<const float*>(smem + L.xks);
 
   // acc[pp][nt][i] holds column lcol + 2 pp + (i >> 1), row nt*8 + 2c + (i & 1)
@@ -566,7 +573,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         // activations of row nt*8 + g, packed row c: (x0,x4 | x1,x5 | x2,x6 | x3,x7)
-        const uint4 bx = xs[(t * Mp + nt * 8 + g) * 4 + c];
+        const uint4 bx = xrow[nt][t * xstep[nt]];
 #pragma unroll
         for (int pp = 0; pp < 2; ++pp) {
           if (j == 0)  // the group's first products start from zero
@@ -580,7 +587,31 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
         }
       }
     }
-    if (gi + nst < ngrp) {  // every warp has read this stage: refill it with group gi + nst
+    if (lora_warps) {  // this group's part of the warp's LoRA tiles, A rows from the stage
+      const __half* Ag = reinterpret_cast<const __half*>(smem + L.ring + st * STAGE + WBYTES);
+      const int RT8 = R >> 3, ntl = lora_tiles(M, R);
+#pragma unroll
+      for (int ii = 0; ii < LITEMS; ++ii) {
+        const int tl = warp + WARPS * ii;
+        if (tl < ntl) {
+          const int mt = tl / RT8, rt = tl - mt * RT8;
+          const int m0 = mt * 16 + g, m1 = m0 + 8;
+          const __half* x0 = xraw + (m0 < M ? m0 : 0) * XS + gi * GROUPK + 2 * c;
+          const __half* x1 = xraw + (m1 < M ? m1 : 0) * XS + gi * GROUPK + 2 * c;
+#pragma unroll
+          for (int kb = 0; kb < 2 * KPG; ++kb) {
+            const uint32_t a0 = m0 < M ? *reinterpret_cast<const uint32_t*>(x0 + kb * 16) : 0u;
+            const uint32_t a2 = m0 < M ? *reinterpret_cast<const uint32_t*>(x0 + kb * 16 + 8) : 0u;
+            const uint32_t a1 = m1 < M ? *reinterpret_cast<const uint32_t*>(x1 + kb * 16) : 0u;
+            const uint32_t a3 = m1 < M ? *reinterpret_cast<const uint32_t*>(x1 + kb * 16 + 8) : 0u;
+            uint32_t bf[2];
+            ldsm_x2_t(bf, Ag + (kb * 16 + (lane & 15)) * R + rt * 8);
+            mma_16816(hl[ii], a0, a1, a2, a3, bf[0], bf[1]);
+          }
+        }
+      }
+    }
+    if (gi + nst < ngrp) {  // every reader has read this stage: refill it with group gi + nst
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8 * st);
       if (tid == 0) {
@@ -588,6 +619,9 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
         mbar_expect_tx(full0 + 8 * st, STAGE_TX);
         tma_2d_hint(ring_s + st * STAGE, &p.tw, wx, (ks0 + (gi + nst) * KPG) * 4, full0 + 8 * st,
                     evict_first_policy());
+        if (R > 0)
+          bulk_g2s(ring_s + st * STAGE + WBYTES, p.A + size_t(k0 + (gi + nst) * GROUPK) * R, ABYTES,
+                   full0 + 8 * st);
       }
       __syncwarp();
     }
@@ -619,6 +653,21 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     }
   }
 
+  if (lora_warps) {  // the warps' LoRA tiles into h_s [M][r]
+    float* hp = reinterpret_cast<float*>(smem + L.hs);
+    const int RT8 = R >> 3, ntl = lora_tiles(M, R);
+#pragma unroll
+    for (int ii = 0; ii < LITEMS; ++ii) {
+      const int tl = warp + WARPS * ii;
+      if (tl < ntl) {
+        const int mt = tl / RT8, rt = tl - mt * RT8;
+        const int m0 = mt * 16 + g, m1 = m0 + 8;
+        float* dst = hp + rt * 8 + 2 * c;
+        if (m0 < M) *reinterpret_cast<float2*>(dst + m0 * R) = make_float2(hl[ii][0], hl[ii][1]);
+        if (m1 < M) *reinterpret_cast<float2*>(dst + m1 * R) = make_float2(hl[ii][2], hl[ii][3]);
+      }
+    }
+  }
   // this CTA's LoRA term (alpha/r) h_s B[:, tile] joins its partial sums on
   // the tensor cores: A = B^T (rows = this lane's columns), B operand =
   // (alpha/r) h_s^T split into fp16 high and low parts (~22-bit product)
@@ -639,8 +688,8 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
         const int m = nt * 8 + g;
         float2 h0 = make_float2(0.f, 0.f), h1 = make_float2(0.f, 0.f);
         if (m < M) {
-          for (int kp = 0; kp < KP; ++kp) {  // partial sums in part order
-            const float* hk = hs + (size_t(kp) * M + m) * R + j;
+          {
+            const float* hk = hs + size_t(m) * R + j;
             const float2 u = *reinterpret_cast<const float2*>(hk);
             h0.x += u.x;
             h0.y += u.y;
@@ -732,13 +781,13 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   }
 }
 
-template <int NT, int KPG>
+template <int NT, int KPG, bool LW>
 static int prepare(int dev) {
   static std::mutex mu;
   static bool done[64] = {};
   std::lock_guard<std::mutex> lk(mu);
   if (dev >= 0 && dev < 64 && done[dev]) return QX_OK;
-  auto kern = w4a16_gemv_kernel<NT, KPG>;
+  auto kern = w4a16_gemv_kernel<NT, KPG, LW>;
   QX_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_LIMIT)),
               "w4a16_gemv: set smem limit");
   QX_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
@@ -751,13 +800,14 @@ static int prepare(int dev) {
 // wave of co-resident clusters (occupancy API), pick the one with the fewest
 // quantisation groups per CTA, then the smallest; if none fits in one wave,
 // the fewest waves.
-template <int NT, int KPG>
+template <int NT, int KPG, bool LW>
 static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed, Plan* out) {
   static std::mutex mu;
-  static std::map<std::tuple<int, int, int, int, int, int, int>, Plan> cache;
+  static std::map<std::tuple<int, int, int, int, int, int, int, int>, Plan> cache;
   int dev = 0;
   QX_CUDA_TRY(cudaGetDevice(&dev), "w4a16_gemv: cudaGetDevice");
-  const auto key = std::make_tuple(dev, M, K, N, rank, group, zeros_packed);
+  const int pin_S = g_pin_S.load(), pin_nst = g_pin_nst.load();
+  const auto key = std::make_tuple(dev, M, K, N, rank, group, zeros_packed, pin_S * 64 + pin_nst);
   {
     std::lock_guard<std::mutex> lk(mu);
     auto itc = cache.find(key);
@@ -769,12 +819,13 @@ static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed,
       return QX_OK;
     }
   }
-  const int rc = prepare<NT, KPG>(dev);
+  const int rc = prepare<NT, KPG, LW>(dev);
   if (rc != QX_OK) return rc;
   const int tiles = (N + COLS - 1) / COLS, T = K / KSTEP, Gt = K / group;
   Plan best{};
   long best_key = -1;
   for (int S = 1; S <= MAX_S && S <= Gt; ++S) {
+    if (pin_S > 0 && S != pin_S) continue;
     Plan pl{};
     pl.NT = NT;
     pl.tiles = tiles;
@@ -782,11 +833,12 @@ static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed,
     pl.S = S;
     const int gmax = (Gt + S - 1) / S;
     if (gmax > 256) continue;  // one tensor-map box covers a CTA's scale rows
-    if (S > 1 && (Gt + S - 2) / (S - 1) == gmax) continue;  // a smaller cluster is as short
+    if (pin_S == 0 && S > 1 && (Gt + S - 2) / (S - 1) == gmax) continue;  // a smaller cluster is as short
     pl.Ts_max = gmax * KPG;
     // a shallower weight ring (down to 2 stages) buys shared memory for more
     // CTAs per SM, hence wider clusters in one wave on deep-K shapes
     for (int nst = std::min(gmax, MAX_NST); nst >= std::min(gmax, 2); --nst) {
+    if (pin_nst > 0 && nst != pin_nst) continue;
     pl.nst = nst;
     pl.smem = layout(M, KPG, pl.Ts_max, rank, S, pl.nst, zeros_packed).total;
     if (pl.smem > SMEM_LIMIT) continue;
@@ -802,14 +854,17 @@ static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed,
     cfg.attrs = at;
     cfg.numAttrs = 1;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, w4a16_gemv_kernel<NT, KPG>, &cfg) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveClusters(&clusters, w4a16_gemv_kernel<NT, KPG, LW>, &cfg) != cudaSuccess ||
         clusters <= 0) {
       cudaGetLastError();
       continue;
     }
     const long waves = (long(tiles) + clusters - 1) / clusters;
     // order: waves first, then groups per CTA (S grows, so later S wins ties
-    // on waves only when it shortens the CTA), then the deeper ring
+    // on waves only when it shortens the CTA), then the deeper ring.  (Models
+    // of the busiest SM's streaming time that favoured one CTA per SM with a
+    // deep ring measured slower: with 9 warps an SM's int4 arithmetic, not
+    // its bytes in flight, bounds a single-row GEMV.)
     const long key2 = waves * 1000000L + long(gmax) * 1000L + (MAX_NST - nst);
     if (best_key < 0 || key2 < best_key) {
       best = pl;
@@ -863,9 +918,9 @@ static int encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* bas
   return QX_OK;
 }
 
-template <int NT, int KPG>
+template <int NT, int KPG, bool LW>
 static int build_params(Params& prm, Plan* plo);
-template <int NT, int KPG>
+template <int NT, int KPG, bool LW>
 static int launch(const Params& prm, const Plan& pl, cudaStream_t st);
 
 // Launch parameters (plan and tensor maps) of recent calls, keyed by every
@@ -908,14 +963,14 @@ static std::mutex g_param_mu;
 static std::unordered_map<ParamKey, ParamEntry, ParamKeyHash> g_params;
 constexpr size_t PARAM_CACHE_MAX = 1024;
 
-template <int NT, int KPG>
+template <int NT, int KPG, bool LW>
 static int run(Params prm, cudaStream_t st) {
   int dev = 0;
   QX_CUDA_TRY(cudaGetDevice(&dev), "w4a16_gemv: cudaGetDevice");
   uint32_t ls_bits;
   std::memcpy(&ls_bits, &prm.lora_scale, 4);
   const ParamKey key{prm.qw, prm.scales, prm.zeros, prm.A, prm.B, dev, prm.M, prm.K, prm.N, prm.rank,
-                     prm.group, prm.zeros_packed, prm.zero_offset, prm.pdl, NT, KPG, ls_bits};
+                     prm.group, prm.zeros_packed, prm.zero_offset, prm.pdl, NT, KPG * 2 + (LW ? 1 : 0), ls_bits};
   Plan pl;
   bool hit = false;
   {
@@ -932,20 +987,20 @@ static int run(Params prm, cudaStream_t st) {
     }
   }
   if (!hit) {
-    const int rc = build_params<NT, KPG>(prm, &pl);
+    const int rc = build_params<NT, KPG, LW>(prm, &pl);
     if (rc != QX_OK) return rc;
     std::lock_guard<std::mutex> lk(g_param_mu);
     if (g_params.size() >= PARAM_CACHE_MAX) g_params.clear();
     g_params.emplace(key, ParamEntry{prm, pl});
   }
-  return launch<NT, KPG>(prm, pl, st);
+  return launch<NT, KPG, LW>(prm, pl, st);
 }
 
 // Plan and tensor maps of one call (everything but the activations and output).
-template <int NT, int KPG>
+template <int NT, int KPG, bool LW>
 static int build_params(Params& prm, Plan* plo) {
   Plan pl;
-  int rc = make_plan<NT, KPG>(prm.M, prm.K, prm.N, prm.rank, prm.group, prm.zeros_packed, &pl);
+  int rc = make_plan<NT, KPG, LW>(prm.M, prm.K, prm.N, prm.rank, prm.group, prm.zeros_packed, &pl);
   if (rc != QX_OK) return rc;
   prm.T = pl.T;
   prm.S = pl.S;
@@ -956,6 +1011,7 @@ static int build_params(Params& prm, Plan* plo) {
   prm.Ts_max = pl.Ts_max;
   prm.gmax = pl.Ts_max / KPG;
   prm.nst = pl.nst;
+  prm.stage = stage_bytes(KPG, prm.rank);
   // qweight as 64-bit elements [K/8][N/2]; one box = a group of packed rows x
   // (256 + 8) columns, i.e. 1056 B rows
   rc = encode_2d(&prm.tw, CU_TENSOR_MAP_DATA_TYPE_UINT64, prm.qw, uint64_t(prm.N) / 2,
@@ -982,7 +1038,7 @@ static int build_params(Params& prm, Plan* plo) {
   return QX_OK;
 }
 
-template <int NT, int KPG>
+template <int NT, int KPG, bool LW>
 static int launch(const Params& prm, const Plan& pl, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.tiles, pl.S, 1);
@@ -1003,24 +1059,25 @@ static int launch(const Params& prm, const Plan& pl, cudaStream_t st) {
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  QX_CUDA_TRY(cudaLaunchKernelEx(&cfg, w4a16_gemv_kernel<NT, KPG>, prm), "w4a16_gemv: launch");
+  QX_CUDA_TRY(cudaLaunchKernelEx(&cfg, w4a16_gemv_kernel<NT, KPG, LW>, prm), "w4a16_gemv: launch");
   return check_launch("w4a16_gemv");
 }
 
-template <int NT>
+template <int NT, bool LW>
 static int dispatch_kpg(const Params& prm, int kpg, cudaStream_t st) {
   switch (kpg) {
-    case 1: return run<NT, 1>(prm, st);
-    case 2: return run<NT, 2>(prm, st);
-    case 4: return run<NT, 4>(prm, st);
-    default: return run<NT, 8>(prm, st);
+    case 1: return run<NT, 1, LW>(prm, st);
+    case 2: return run<NT, 2, LW>(prm, st);
+    case 4: return run<NT, 4, LW>(prm, st);
+    default: return run<NT, 8, LW>(prm, st);
   }
 }
 
 static int dispatch(const Params& prm, int kpg, cudaStream_t st) {
-  if (prm.M <= 8) return dispatch_kpg<1>(prm, kpg, st);
-  if (prm.M <= 16) return dispatch_kpg<2>(prm, kpg, st);
-  return dispatch_kpg<4>(prm, kpg, st);
+  const bool lw = lora_on_warps(prm.M, prm.rank);
+  if (prm.M <= 8) return lw ? dispatch_kpg<1, true>(prm, kpg, st) : dispatch_kpg<1, false>(prm, kpg, st);
+  if (prm.M <= 16) return lw ? dispatch_kpg<2, true>(prm, kpg, st) : dispatch_kpg<2, false>(prm, kpg, st);
+  return lw ? dispatch_kpg<4, true>(prm, kpg, st) : dispatch_kpg<4, false>(prm, kpg, st);
 }
 
 }  // namespace gemv
@@ -1049,6 +1106,55 @@ extern "C" int qx_get_device_error(unsigned* code, int reset) {
   rc = qx::nvar_device_error(&other, reset);
   if (rc != QX_OK) return rc;
   *code |= other;
+  return QX_OK;
+}
+
+extern "C" int qx_w4a16_gemv_plan(int M, int K, int N, int rank, int group_size, int zeros_packed,
+                                  int* out) {
+  QX_REQUIRE(out, "w4a16_gemv_plan: null output");
+  QX_REQUIRE(M >= 1 && K > 0 && K % gemv::KSTEP == 0 && N > 0 && N % 8 == 0 &&
+                 (group_size == 32 || group_size == 64 || group_size == 128 || group_size == 256) &&
+                 K % group_size == 0,
+             "w4a16_gemv_plan: bad shape M=%d K=%d N=%d group=%d", M, K, N, group_size);
+  const int mc = std::min(M, gemv::MROWS);
+  const int kpg = group_size / gemv::KSTEP;
+  const bool lw = gemv::lora_on_warps(mc, rank);
+  gemv::Plan pl{};
+  int rc = QX_OK;
+  auto pick = [&](auto nt_tag) {
+    constexpr int NT = decltype(nt_tag)::value;
+    switch (kpg) {
+      case 1: rc = lw ? gemv::make_plan<NT, 1, true>(mc, K, N, rank, group_size, zeros_packed, &pl)
+                      : gemv::make_plan<NT, 1, false>(mc, K, N, rank, group_size, zeros_packed, &pl); break;
+      case 2: rc = lw ? gemv::make_plan<NT, 2, true>(mc, K, N, rank, group_size, zeros_packed, &pl)
+                      : gemv::make_plan<NT, 2, false>(mc, K, N, rank, group_size, zeros_packed, &pl); break;
+      case 4: rc = lw ? gemv::make_plan<NT, 4, true>(mc, K, N, rank, group_size, zeros_packed, &pl)
+                      : gemv::make_plan<NT, 4, false>(mc, K, N, rank, group_size, zeros_packed, &pl); break;
+      default: rc = lw ? gemv::make_plan<NT, 8, true>(mc, K, N, rank, group_size, zeros_packed, &pl)
+                       : gemv::make_plan<NT, 8, false>(mc, K, N, rank, group_size, zeros_packed, &pl); break;
+    }
+  };
+  if (mc <= 8) pick(std::integral_constant<int, 1>{});
+  else if (mc <= 16) pick(std::integral_constant<int, 2>{});
+  else pick(std::integral_constant<int, 4>{});
+  if (rc != QX_OK) return rc;
+  out[0] = pl.tiles;
+  out[1] = pl.S;
+  out[2] = pl.nst;
+  out[3] = pl.Ts_max / kpg;
+  out[4] = int(pl.smem);
+  return QX_OK;
+}
+
+extern "C" int qx_w4a16_gemv_pin_plan(int S, int nst) {
+  QX_REQUIRE(S >= 0 && S <= gemv::MAX_S && nst >= 0 && nst <= gemv::MAX_NST,
+             "w4a16_gemv_pin_plan: S=%d (0..%d), stages=%d (0..%d)", S, gemv::MAX_S, nst, gemv::MAX_NST);
+  g_pin_S.store(S);
+  g_pin_nst.store(nst);
+  {
+    std::lock_guard<std::mutex> lk(gemv::g_param_mu);
+    gemv::g_params.clear();  // cached launch parameters carry the old plan
+  }
   return QX_OK;
 }
 
