@@ -19,8 +19,9 @@ e2e    : the same metric through the public Python API
 roofline, cpu_baseline, clocks, gpu_launches: see the keys in the JSON line.
 
 Under torchrun every rank runs its own replica; rank 0 prints one JSON line.
-``--impl reference`` times the CPU restatement of the reference's algorithm
-(oracle/qx_oracle.c, all host cores) on the same workload; ranks > 0 exit.
+``--impl reference`` times the reference's own PyTorch CPU path (restated op
+for op in oracle/torch_ref.py; all host cores) on the same workload; ranks > 0
+exit.
 """
 
 from __future__ import annotations
@@ -132,42 +133,52 @@ def dist_setup():
     return world, rank, local
 
 
-def cpu_gemv_baseline(seconds: float = 12.0, max_calls: int = 200, nthreads: int = 0):
-    """The C restatement of the reference algorithm (dequantise to fp16, fp32
-    GEMV + LoRA) on the host cores, on the full decode workload."""
-    from oracle import cbind, make_gemv_inputs
-    d = make_gemv_inputs(M, K, N, RANK, seed=0)
-    cbind.lib()
+def _reference_cpu_call(threads):
+    """One call of the reference's own CPU path (oracle/torch_ref.py: its
+    dequantise loop and fp32 matmuls restated op for op) on the decode
+    workload, on `threads` host threads."""
+    import torch
+    from oracle import make_gemv_inputs
+    from oracle.torch_ref import unpack_qzeros_fp16, w4a16_lora_gemv_cpu
+    torch.set_num_threads(threads)
+    d = {k: torch.from_numpy(v) for k, v in make_gemv_inputs(M, K, N, RANK, seed=0).items()}
+    zeros = unpack_qzeros_fp16(d["zeros"], N)  # the reference's op takes fp16 zero points
+    return lambda: w4a16_lora_gemv_cpu(d["x"], d["qweight"], d["scales"], zeros, d["lora_A"],  # noqa
+                                       d["lora_B"], GROUP, ALPHA)
+
+
+def cpu_gemv_baseline(seconds: float = 15.0, max_calls: int = 200, nthreads: int = 0):
+    """The reference's CPU path (its PyTorch dequantise loop + fp32 GEMV +
+    LoRA, restated in oracle/torch_ref.py) on all host cores, on the full
+    decode workload: a bounded sample of calls."""
     threads = nthreads or os.cpu_count() or 1
-    cbind.c_w4a16_lora_gemv(d["x"], d["qweight"], d["scales"], d["zeros"], d["lora_A"], d["lora_B"],
-                            GROUP, ALPHA, nthreads=threads)
+    call = _reference_cpu_call(threads)
+    call()
     n, t0 = 0, time.perf_counter()
     while n < max_calls and (time.perf_counter() - t0) < seconds:
-        cbind.c_w4a16_lora_gemv(d["x"], d["qweight"], d["scales"], d["zeros"], d["lora_A"],
-                                d["lora_B"], GROUP, ALPHA, nthreads=threads)
+        call()
         n += 1
     dt = time.perf_counter() - t0
     return {"value": BYTES_PER_CALL * n / dt / 1e9, "unit": "GB/s", "cores": threads,
             "kind": "port", "us_per_call": dt / n * 1e6,
-            "sample": f"{n} full decode-GEMV calls (K=2560, N=9728, r=16) in {dt:.1f} s with "
-                      f"oracle/qx_oracle.c on {threads} OpenMP threads"}
+            "sample": f"{n} full decode-GEMV calls (K=2560, N=9728, r=16) in {dt:.1f} s: the reference's "
+                      f"PyTorch CPU path (tests/test_w4a16_gemv.py dequantize_gptq_ref loop + fp32 "
+                      f"matmuls) restated op for op in oracle/torch_ref.py, torch on {threads} threads"}
 
 
 def run_reference(args):
     world, rank, _ = dist_setup()
     if rank != 0:
         return 0
-    from oracle import cbind, make_gemv_inputs
     threads = os.cpu_count() or 1
-    d = make_gemv_inputs(M, K, N, RANK, seed=0)
-    call = lambda: cbind.c_w4a16_lora_gemv(d["x"], d["qweight"], d["scales"], d["zeros"],  # noqa
-                                           d["lora_A"], d["lora_B"], GROUP, ALPHA, nthreads=threads)
-    steps = max(1, min(args.steps, 2000))
-    for _ in range(max(args.warmup, 1)):
+    call = _reference_cpu_call(threads)
+    for _ in range(max(1, min(args.warmup, 3))):
         call()
-    t0 = time.perf_counter()
-    for _ in range(steps):
+    # each step is one full call; the timed steps stop after ~60 s of CPU work
+    steps, t0 = 0, time.perf_counter()
+    while steps < max(1, args.steps) and (steps == 0 or time.perf_counter() - t0 < 60.0):
         call()
+        steps += 1
     dt = time.perf_counter() - t0
     gbs = BYTES_PER_CALL * steps / dt / 1e9
     line = {"metric": METRIC, "value": gbs, "unit": "GB/s", "impl": "reference",
@@ -177,8 +188,9 @@ def run_reference(args):
             "data": "synthetic (seeded; BASELINE decode-GEMV distributions)",
             "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N, "rank": RANK, "group": GROUP},
             "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": f"{steps} full decode-GEMV calls with oracle/qx_oracle.c "
-                                       f"(C restatement of the reference CPU path)"},
+                             "sample": f"{steps} full decode-GEMV calls: the reference's PyTorch CPU "
+                                       f"path restated op for op (oracle/torch_ref.py), torch on "
+                                       f"{threads} threads; timed steps capped at ~60 s"},
             "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -278,8 +290,8 @@ def run_b200(args):
         torch.cuda.synchronize(device)
         ms = ev0.elapsed_time(ev1)
         # e2e through the reference-facing C-ABI with host buffers, as a C, cgo
-        # or ctypes caller makes it: pinned host x -> device (qx_copy_async),
-        # qx_w4a16_lora_gemv, device y -> pinned host, every step
+        # or ctypes caller makes it: pinned host x -> device, the GEMV, device
+        # y -> pinned host, every step (qx_w4a16_lora_gemv_host)
         from qextract_infer_b200 import _lib
         lib = _lib.load()
         x_host = torch.randn(M, K).half().pin_memory()
@@ -289,18 +301,15 @@ def run_b200(args):
         e_steps = 0 if args.skip_e2e else max(1, min(steps, 2000))
         raw = stream.cuda_stream
         xh, yh, xd, yd = x_host.data_ptr(), y_host.data_ptr(), x_dev.data_ptr(), y_dev.data_ptr()
-        xb, yb = M * K * 2, M * N * 2
         cargs = [(qw.data_ptr(), sc.data_ptr(), qz.data_ptr(), 1, 0, A.data_ptr(), B.data_ptr())
                  for qw, sc, qz, A, B in sets]
         scale = float(np.float32(ALPHA) / np.float32(RANK))
-        copy, gemv = lib.qx_copy_async, lib.qx_w4a16_lora_gemv
+        call = lib.qx_w4a16_lora_gemv_host
 
-        def e2e_step(i):
-            copy(xd, xh, xb, raw)
-            rc = gemv(xd, *cargs[i % nsets], yd, M, K, N, RANK, GROUP, scale, raw)
-            copy(yh, yd, yb, raw)
+        def e2e_step(i):  # x_host -> x_dev, GEMV, y_dev -> y_host in one C-ABI call
+            rc = call(xh, yh, xd, yd, *cargs[i % nsets], M, K, N, RANK, GROUP, scale, raw)
             if rc:
-                _lib.check(rc, "w4a16_lora_gemv")
+                _lib.check(rc, "w4a16_lora_gemv_host")
 
         with torch.cuda.stream(stream):
             for i in range(nsets if e_steps else 0):  # every weight set once: cached launch plans
@@ -362,7 +371,7 @@ def run_b200(args):
                     "value": BYTES_PER_CALL * e_steps / (e_ms / 1e3) / 1e9 * world, "unit": "GB/s",
                     "us_per_call": e_ms * 1e3 / e_steps,
                     "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
-                    "api": "C-ABI qx_copy_async + qx_w4a16_lora_gemv + qx_copy_async (ctypes), "
+                    "api": "C-ABI qx_w4a16_lora_gemv_host (ctypes): copy in, GEMV, copy out; "
                            "host buffers pinned"},
             "cpu_baseline": cpu,
             "clocks": clocks,

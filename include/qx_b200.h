@@ -97,6 +97,18 @@ int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const void* scales
  * before on the same stream (true for model weights).  Returns 0. */
 int qx_set_pdl(int enable);
 
+/* qx_w4a16_lora_gemv for callers whose activations and outputs live in host
+ * memory (a cgo / JNI / ctypes plugin): copies x_host [M, K] to x_dev, runs
+ * the GEMV into y_dev, copies y_dev [M, N] to y_host, all enqueued on
+ * `stream` in one call (host buffers pinned for the copies to be
+ * asynchronous; the caller synchronises before reading y_host).  New entry
+ * point: the reference's op takes device tensors only. */
+int qx_w4a16_lora_gemv_host(const void* x_host, void* y_host, void* x_dev, void* y_dev,
+                            const int32_t* qweight, const void* scales, const void* zeros,
+                            int zeros_packed, int zero_offset, const void* lora_A, const void* lora_B,
+                            int M, int K, int N, int rank, int group_size, float lora_scale,
+                            qx_stream_t stream);
+
 /* The split-K plan qx_w4a16_lora_gemv uses for a shape (at most 32 rows of M
  * per launch): out[0] = 256-column tiles, out[1] = CTAs splitting K per tile
  * (the cluster size S), out[2] = weight stages in flight per CTA, out[3] =

@@ -28,6 +28,9 @@ SIGNATURES = {
                                    c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float,
                                    c_void_p]),
     "qx_set_pdl": (c_int, [c_int]),
+    "qx_w4a16_lora_gemv_host": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                        c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_int,
+                                        c_int, c_int, c_float, c_void_p]),
     "qx_w4a16_gemv_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),
     "qx_w4a16_gemv_pin_plan": (c_int, [c_int, c_int]),
     "qx_w4a16_lora_gemm_sm100_workspace_size": (c_size_t, [c_int, c_int]),

@@ -796,10 +796,10 @@ static int prepare(int dev) {
   return QX_OK;
 }
 
-// Among the cluster sizes whose shared memory fits and whose grid runs in one
-// wave of co-resident clusters (occupancy API), pick the one with the fewest
-// quantisation groups per CTA, then the smallest; if none fits in one wave,
-// the fewest waves.
+// Among the cluster sizes and ring depths whose shared memory fits (occupancy
+// API for the co-resident clusters), pick one that keeps every SM busy with
+// two or more CTAs if any does, then the fewest waves, then the fewest
+// quantisation groups per CTA, then the deeper ring.
 template <int NT, int KPG, bool LW>
 static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed, Plan* out) {
   static std::mutex mu;
@@ -860,12 +860,21 @@ static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed,
       continue;
     }
     const long waves = (long(tiles) + clusters - 1) / clusters;
-    // order: waves first, then groups per CTA (S grows, so later S wins ties
-    // on waves only when it shortens the CTA), then the deeper ring.  (Models
-    // of the busiest SM's streaming time that favoured one CTA per SM with a
-    // deep ring measured slower: with 9 warps an SM's int4 arithmetic, not
-    // its bytes in flight, bounds a single-row GEMV.)
-    const long key2 = waves * 1000000L + long(gmax) * 1000L + (MAX_NST - nst);
+    // order: plans that keep every SM busy with at least two CTAs (up to the
+    // instance's residency) first, then fewer waves, then fewer groups per
+    // CTA, then the deeper ring.  (Fewest waves alone ran a 4096 x 24576
+    // single-row GEMV as 96 one-per-SM CTAs: 35 us, against 24 us for 384
+    // CTAs two per SM.  Models of the busiest SM's streaming time that
+    // favoured one CTA per SM with a deep ring measured slower: with 9 warps
+    // an SM's int4 arithmetic bounds it.)
+    int resident = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, w4a16_gemv_kernel<NT, KPG, LW>, THREADS,
+                                                      pl.smem) != cudaSuccess) {
+      cudaGetLastError();
+      resident = 0;
+    }
+    const bool fills = long(tiles) * S >= device_sm_count() && resident >= std::min(2, ctas_per_sm(NT));
+    const long key2 = (fills ? 0L : 1000000000000L) + waves * 1000000L + long(gmax) * 1000L + (MAX_NST - nst);
     if (best_key < 0 || key2 < best_key) {
       best = pl;
       best_key = key2;
@@ -1106,6 +1115,25 @@ extern "C" int qx_get_device_error(unsigned* code, int reset) {
   rc = qx::nvar_device_error(&other, reset);
   if (rc != QX_OK) return rc;
   *code |= other;
+  return QX_OK;
+}
+
+extern "C" int qx_w4a16_lora_gemv_host(const void* x_host, void* y_host, void* x_dev, void* y_dev,
+                                       const int32_t* qweight, const void* scales, const void* zeros,
+                                       int zeros_packed, int zero_offset, const void* lora_A,
+                                       const void* lora_B, int M, int K, int N, int rank, int group_size,
+                                       float lora_scale, qx_stream_t stream) {
+  QX_REQUIRE(x_host && y_host && x_dev && y_dev, "w4a16_gemv_host: null buffer");
+  QX_REQUIRE(M >= 0 && K > 0 && N > 0, "w4a16_gemv_host: bad sizes M=%d K=%d N=%d", M, K, N);
+  if (M == 0) return QX_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  QX_CUDA_TRY(cudaMemcpyAsync(x_dev, x_host, size_t(M) * K * 2, cudaMemcpyHostToDevice, st),
+              "w4a16_gemv_host: copy x to the device");
+  const int rc = qx_w4a16_lora_gemv(x_dev, qweight, scales, zeros, zeros_packed, zero_offset, lora_A, lora_B,
+                                    y_dev, M, K, N, rank, group_size, lora_scale, stream);
+  if (rc != QX_OK) return rc;
+  QX_CUDA_TRY(cudaMemcpyAsync(y_host, y_dev, size_t(M) * N * 2, cudaMemcpyDeviceToHost, st),
+              "w4a16_gemv_host: copy y to the host");
   return QX_OK;
 }
 

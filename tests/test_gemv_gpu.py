@@ -257,3 +257,30 @@ def test_batch_rows_long_k_fall_back_to_fewer_rows(C):
     ref = w4a16_lora_gemv_ref(d["x"], d["qweight"], d["scales"], d["zeros"], d["lora_A"],
                               d["lora_B"], 128, 32.0)
     assert_close(to_np(y), ref, RTOL, ATOL, "M=32 K=12288")
+
+
+def test_host_buffer_entry_point_matches_device_path(C):
+    """qx_w4a16_lora_gemv_host (pinned host x in, pinned host y out, one C-ABI
+    call) returns exactly the device-path result, on two calls in a row."""
+    import ctypes
+    from qextract_infer_b200 import _lib
+    lib = _lib.load()
+    d = make_gemv_inputs(3, 2560, 9728, 16, seed=21)
+    t = _dev(d)
+    ref = to_np(C.w4a16_lora_gemv(t["x"], t["qweight"], t["scales"], t["zeros"], t["lora_A"],
+                                  t["lora_B"], 128, 32.0))
+    x_host = torch.from_numpy(d["x"]).pin_memory()
+    y_host = torch.zeros(3, 9728, dtype=torch.float16).pin_memory()
+    x_dev = torch.empty(3, 2560, dtype=torch.float16, device="cuda")
+    y_dev = torch.empty(3, 9728, dtype=torch.float16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        y_host.zero_()
+        rc = lib.qx_w4a16_lora_gemv_host(
+            x_host.data_ptr(), y_host.data_ptr(), x_dev.data_ptr(), y_dev.data_ptr(),
+            t["qweight"].data_ptr(), t["scales"].data_ptr(), t["zeros"].data_ptr(), 1, 0,
+            t["lora_A"].data_ptr(), t["lora_B"].data_ptr(), 3, 2560, 9728, 16, 128,
+            ctypes.c_float(2.0), st)
+        assert rc == 0, _lib.last_error()
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(y_host.numpy().view(np.uint16), ref.view(np.uint16))

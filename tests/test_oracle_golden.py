@@ -169,3 +169,33 @@ def test_ring_chunk_append_equals_token_by_token():
     np.testing.assert_array_equal(a.k, b.k)
     np.testing.assert_array_equal(a.v, b.v)
     assert a.count == b.count == sum(chunks)
+
+
+@pytest.mark.parametrize("case", GPTQ_CASES)
+def test_torch_restatement_of_reference_cpu_path(case):
+    """oracle/torch_ref.py (the timed CPU baseline) reproduces the reference's
+    own dequantisation bit for bit and its outputs to 1 fp16 ulp."""
+    import torch
+    from oracle.torch_ref import dequantize_rows, w4a16_lora_gemv_cpu
+    d = load_golden(f"gptq_{case}")
+    qw, s, z, x = (torch.from_numpy(d[k]) for k in ("qweight", "scales", "zeros", "x"))
+    if "w_dequant" in d:
+        w = dequantize_rows(qw, s, z, qw.shape[0] * 8)
+        np.testing.assert_array_equal(w.numpy().view(np.uint16), d["w_dequant"].view(np.uint16))
+    assert_f16_match(w4a16_lora_gemv_cpu(x, qw, s, z).numpy(), d["y_base"])
+    if "lora_A" in d:
+        A, B = torch.from_numpy(d["lora_A"]), torch.from_numpy(d["lora_B"])
+        y = w4a16_lora_gemv_cpu(x, qw, s, z, A, B, lora_alpha=float(d["alpha"]))
+        assert_f16_match(y.numpy(), d["y_lora"])
+
+
+def test_torch_restatement_packed_qzeros():
+    import torch
+    from oracle.torch_ref import unpack_qzeros_fp16, w4a16_lora_gemv_cpu
+    d = load_golden("gptq_packed_zeros")
+    N = d["qweight"].shape[1]
+    zf = unpack_qzeros_fp16(torch.from_numpy(d["qzeros"]), N)
+    np.testing.assert_array_equal(zf.numpy().astype(np.float32), d["zeros_unpacked"].astype(np.float32))
+    args = [torch.from_numpy(d[k]) for k in ("x", "qweight", "scales", "qzeros", "lora_A", "lora_B")]
+    y = w4a16_lora_gemv_cpu(*args, lora_alpha=float(d["alpha"]))
+    assert_f16_match(y.numpy(), d["y_lora"])
