@@ -58,8 +58,8 @@ def measured_peaks():
 
 def gemv_kernel_name():
     """The kernel qx_w4a16_lora_gemv runs for the decode shape (one row: NT = 1,
-    128-row groups: KPG = 4)."""
-    return "qx::gemv::w4a16_gemv_kernel<1, 4>"
+    128-row groups: KPG = 4, LoRA-down on the helper warp: LW = false)."""
+    return "qx::gemv::w4a16_gemv_kernel<1, 4, false>"
 
 
 def profiled_traffic():

@@ -860,8 +860,8 @@ static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed,
       continue;
     }
     const long waves = (long(tiles) + clusters - 1) / clusters;
-    // order: plans that keep every SM busy with at least two CTAs (up to the
-    // instance's residency) first, then fewer waves, then fewer groups per
+    // order: single-row plans that keep every SM busy with at least two CTAs
+    // first, then fewer waves, then fewer groups per
     // CTA, then the deeper ring.  (Fewest waves alone ran a 4096 x 24576
     // single-row GEMV as 96 one-per-SM CTAs: 35 us, against 24 us for 384
     // CTAs two per SM.  Models of the busiest SM's streaming time that
@@ -873,7 +873,9 @@ static int make_plan(int M, int K, int N, int rank, int group, int zeros_packed,
       cudaGetLastError();
       resident = 0;
     }
-    const bool fills = long(tiles) * S >= device_sm_count() && resident >= std::min(2, ctas_per_sm(NT));
+    // (single-row instances: wider batches are bounded by their arithmetic and
+    // keep the fewest-waves order, which measured best for them)
+    const bool fills = NT > 1 || (long(tiles) * S >= device_sm_count() && resident >= 2);
     const long key2 = (fills ? 0L : 1000000000000L) + waves * 1000000L + long(gmax) * 1000L + (MAX_NST - nst);
     if (best_key < 0 || key2 < best_key) {
       best = pl;
