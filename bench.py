@@ -371,8 +371,8 @@ def run_b200(args):
                     "value": BYTES_PER_CALL * e_steps / (e_ms / 1e3) / 1e9 * world, "unit": "GB/s",
                     "us_per_call": e_ms * 1e3 / e_steps,
                     "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
-                    "api": "C-ABI qx_w4a16_lora_gemv_host (ctypes): copy in, GEMV, copy out; "
-                           "host buffers pinned"},
+                    "api": "C-ABI qx_w4a16_lora_gemv_host (ctypes), pinned host buffers: the GEMV "
+                           "reads x_host over the bus and writes y into y_host, one launch per step"},
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": steps,

@@ -43,7 +43,7 @@ const char* qx_last_error(void);
  * GPU (the kernel then finishes with undefined output).  New component: the
  * reference has no device-side error reporting. */
 #define QX_DEVERR_MBAR_TIMEOUT 1u
-/* a peer rank's flag did not arrive within the wait limit (qx_nvlink_ar_add_rmsnorm) */
+/* a peer rank's row did not arrive within the wait limit (qx_nvlink_ar_add_rmsnorm) */
 #define QX_DEVERR_PEER_TIMEOUT 2u
 /* Reads (and with reset != 0 clears) the sticky error bits of the current
  * device; synchronises with the device. */
@@ -85,6 +85,21 @@ int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const void* scales
                        int M, int K, int N, int rank, int group_size, float lora_scale,
                        qx_stream_t stream);
 
+/* The gate|up projection of an MLP followed by SwiGLU, in one launch: the
+ * GEMV above over N = 2I columns laid out in blocks of 16 (8 gate columns,
+ * then the 8 up columns of the same outputs), each owner CTA rounding its
+ * gate and up sums to fp16 and writing y[m][i] = fp16(silu(g) u) ([M, I]) with
+ * the formula of qx_fused_swiglu.  Bit-identical to qx_w4a16_lora_gemv on the
+ * interleaved weights followed by SwiGLU on the matching columns.  N % 16 == 0.
+ * Replaces the reference's gate/up projections and fused_swiglu call
+ * (qextract/patch.py:94-113) with one kernel: the [M, 2I] intermediate never
+ * reaches memory. */
+int qx_w4a16_lora_gemv_swiglu(const void* x, const int32_t* qweight, const void* scales,
+                              const void* zeros, int zeros_packed, int zero_offset,
+                              const void* lora_A, const void* lora_B, void* y,
+                              int M, int K, int N, int rank, int group_size, float lora_scale,
+                              qx_stream_t stream);
+
 /* Programmatic dependent launch for the GEMV (on by default; 0 turns it
  * off).  When on, a GEMV launches as soon as every CTA of the GEMV before it
  * in the stream is running: it streams its weights and stages scales /
@@ -98,11 +113,17 @@ int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const void* scales
 int qx_set_pdl(int enable);
 
 /* qx_w4a16_lora_gemv for callers whose activations and outputs live in host
- * memory (a cgo / JNI / ctypes plugin): copies x_host [M, K] to x_dev, runs
- * the GEMV into y_dev, copies y_dev [M, N] to y_host, all enqueued on
- * `stream` in one call (host buffers pinned for the copies to be
- * asynchronous; the caller synchronises before reading y_host).  New entry
- * point: the reference's op takes device tensors only. */
+ * memory (a cgo / JNI / ctypes plugin): moves x_host [M, K] into x_dev, runs
+ * the GEMV, and delivers y [M, N] into y_host, all enqueued on `stream` in one
+ * call; the caller synchronises before reading y_host.  Pinned (device-mapped)
+ * host buffers take the fast form: the GEMV reads x_host over the bus itself,
+ * as soon as it launches (while the previous kernel on the stream still runs:
+ * x_host must hold this call's rows when the call is made, and must not be
+ * written by kernels still pending on the stream, except the previous call of
+ * this function, whose y_host is detected), and writes y straight into y_host
+ * (x_dev and y_dev unused).  Pageable buffers go through cudaMemcpyAsync into
+ * x_dev and out of y_dev.  New entry point: the reference's op takes device
+ * tensors only. */
 int qx_w4a16_lora_gemv_host(const void* x_host, void* y_host, void* x_dev, void* y_dev,
                             const int32_t* qweight, const void* scales, const void* zeros,
                             int zeros_packed, int zero_offset, const void* lora_A, const void* lora_B,
@@ -181,8 +202,8 @@ int qx_swiglu_packed(const void* gate_up, void* y, int64_t rows, int inter, qx_s
  *   y[r]  = fp16((x[r] * rsqrt(mean(x[r]^2) + eps)) * w)
  * Every rank computes identical bits (rank-ordered fp32 sum).
  * Setup, on every rank of one node (one GPU per rank): qx_nvlink_ar_create
- * allocates this rank's shared buffer (2 x max_rows x hidden fp16 + flags; the
- * only allocation in the library) and writes its IPC handle
+ * allocates this rank's inbox (2 x world x max_rows x hidden x 4 bytes: every
+ * peer's rows pushed in with their epoch; the only allocation in the library) and writes its IPC handle
  * (qx_nvlink_ar_handle_bytes() bytes) to handle_out; exchange the handles
  * (all-gather, rank order) and call qx_nvlink_ar_open with all of them; then
  * a barrier before the first call.  Calls: every rank makes the same sequence
@@ -200,7 +221,7 @@ int qx_nvlink_ar_open(void* ctx, const void* handles);
  * ctxs[r] is rank r's context; peer access is enabled between distinct
  * devices. */
 int qx_nvlink_ar_open_local(void* ctx, void* const* ctxs);
-/* Limit of each wait for a peer's flag, in nanoseconds (default 2e9). */
+/* Limit of each wait for a peer's row, in nanoseconds (default 2e9). */
 int qx_nvlink_ar_set_timeout(void* ctx, int64_t timeout_ns);
 int qx_nvlink_ar_add_rmsnorm(void* ctx, const void* partial, void* x, const void* weight, void* y,
                              int rows, float eps, qx_stream_t stream);
@@ -272,6 +293,27 @@ int qx_decode_attention(const void* q, const void* k_cache, const void* v_cache,
                         int batch, int q_heads, int kv_heads, int head_dim, int sink,
                         int window, int64_t count, float softmax_scale, void* workspace,
                         size_t workspace_bytes, qx_stream_t stream);
+
+/* qx_decode_attention with flags.  QX_ATTN_AFTER_APPEND: the kernel just
+ * before this call on `stream` wrote q and position count - 1 of every
+ * sequence into the cache (a decode step's append) and nothing else this call
+ * reads; when its grid is small (at most two CTAs per SM: one or a few
+ * sequences) the attention is then launched early (programmatic dependent
+ * launch) and loads its first K/V tiles while that kernel finishes, reloading
+ * the appended slot once it has.  Without flags it equals qx_decode_attention.
+ * New component (no counterpart in the reference). */
+#define QX_ATTN_AFTER_APPEND 1
+int qx_decode_attention_ex(const void* q, const void* k_cache, const void* v_cache, void* out,
+                           int batch, int q_heads, int kv_heads, int head_dim, int sink,
+                           int window, int64_t count, float softmax_scale, void* workspace,
+                           size_t workspace_bytes, int flags, qx_stream_t stream);
+
+/* How both decode-attention entry points merge the slot chunks of one
+ * sequence and KV head (process-wide; results agree within fp32 rounding):
+ * 0 (default) through distributed shared memory, the chunk CTAs forming one
+ * thread-block cluster (up to 16 chunks; longer chunks when needed),
+ * 1 through the workspace (partials written, the last CTA merges them). */
+int qx_decode_attention_pin_merge(int mode);
 
 /* ------------------------------------------------------------------------
  * Allocation-free decode attention.  No counterpart in the reference.

@@ -345,6 +345,66 @@ def _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale
     return out
 
 
+def interleave_gate_up(t: torch.Tensor, inter: int, packed: bool = False) -> torch.Tensor:
+    """Reorders the columns of a gate|up operand ``[..., 2 I]`` (gate columns,
+    then up; ``[..., 2 I / 8]`` int32 words of 8 columns when ``packed``: GPTQ
+    qzeros) into blocks of 16 columns: the 8 gate columns of outputs
+    8b..8b+7, then their 8 up columns (the layout of
+    ``w4a16_lora_gemv_swiglu``).  Apply it to qweight, scales, qzeros and
+    LoRA B alike."""
+    if packed:
+        nb = inter // 8
+        idx = torch.stack([torch.arange(nb), torch.arange(nb) + nb], 1).reshape(-1)
+    else:
+        if inter % 8:
+            raise RuntimeError(f"interleave_gate_up: I={inter} must be a multiple of 8")
+        b = torch.arange(inter // 8)[:, None] * 8 + torch.arange(8)[None, :]  # [I/8, 8]
+        idx = torch.stack([b, b + inter], 1).reshape(-1)
+    return t.index_select(-1, idx.to(t.device)).contiguous()
+
+
+def _w4a16_swiglu(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale, zero_offset):
+    """SwiGLU of the gate|up projection whose operands ``interleave_gate_up``
+    laid out: ``[..., N / 2]``.  Decode rows run the GEMV with the SwiGLU
+    epilogue (one launch); prefill rows the tensor-core GEMM, then SwiGLU on
+    the gathered gate and up columns."""
+    w = _weights(qweight, scales, zeros, lora_A, lora_B, group_size, zero_offset)
+    if not (isinstance(input, torch.Tensor) and input.is_cuda and input.dtype == torch.float16
+            and input.is_contiguous()):
+        _check_input(input, "input")
+        _check_fp16(input, "input")
+    K, N = w.K, w.N
+    if input.size(-1) != K or N % 16:
+        raise RuntimeError(f"w4a16_lora_gemv_swiglu: input K={input.size(-1)} (weights K={K}), "
+                           f"N={N} must be a multiple of 16")
+    di = input.get_device()
+    if di != w.dev:
+        raise RuntimeError(f"input is on cuda:{di} but the weights are on cuda:{w.dev}")
+    lead = input.shape[:-1]
+    M = input.numel() // K
+    if M >= GEMM_MIN_ROWS and N % 256 == 0 and K % 64 == 0 and w.rank <= 64:
+        y = _w4a16(input, qweight, scales, zeros, lora_A, lora_B, group_size, lora_scale, zero_offset)
+        y = y.view(M, N // 16, 2, 8)
+        return fused_swiglu(y[:, :, 0].reshape(M, N // 2), y[:, :, 1].reshape(M, N // 2)).view(
+            lead + (N // 2,))
+    out = torch.empty(lead + (N // 2,), dtype=torch.float16, device=input.device)
+    with torch.cuda.device(di):
+        _lib.check(_LIB.qx_w4a16_lora_gemv_swiglu(input.data_ptr(), *w.args, out.data_ptr(), M, K, N,
+                                                  w.rank, w.group, lora_scale, _raw_stream(input.device)),
+                   "w4a16_gemv_swiglu")
+    return out
+
+
+def w4a16_lora_gemv_swiglu(input, qweight, scales, zeros, lora_A, lora_B, group_size: int = 128,
+                           lora_alpha: float = 16.0, *, zero_offset: int = 0):
+    """``fused_swiglu(gate, up)`` of one W4A16-LoRA gate|up projection whose
+    operands ``interleave_gate_up`` reordered (new component: the reference
+    runs the two projections and ``fused_swiglu`` separately,
+    ``qextract/patch.py:94-113``)."""
+    scale = _lora_scale(float(lora_alpha), lora_A.size(1))
+    return _w4a16_swiglu(input, qweight, scales, zeros, lora_A, lora_B, group_size, scale, zero_offset)
+
+
 def w4a16_gemv(input, qweight, scales, zeros, group_size: int = 128, *, zero_offset: int = 0,
                out: torch.Tensor | None = None):
     """``fp16(x . W)`` with ``W = s (q - z)`` from GPTQ int4 packing
@@ -377,9 +437,12 @@ def ring_slot_indices(count: int, sink: int, window: int, device) -> torch.Tenso
 
 
 def decode_attention(q, k_cache, v_cache, count: int, sink: int, window: int,
-                     softmax_scale: float | None = None):
+                     softmax_scale: float | None = None, *, after_append: bool = False):
     """GQA decode attention over the ring's valid slots, read in place.
-    ``q`` fp16 ``[B, Hq, D]``; ``k_cache``/``v_cache`` fp16 ``[B, S+W, Hkv, D]``."""
+    ``q`` fp16 ``[B, Hq, D]``; ``k_cache``/``v_cache`` fp16 ``[B, S+W, Hkv, D]``.
+    ``after_append``: the kernel just before on the stream wrote only ``q``
+    and position ``count - 1`` of the cache (``qk_norm_rope_append``); the
+    attention then starts loading the other slots while it finishes."""
     for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
         _check_input(t, n)
         _check_fp16(t, n)
@@ -394,10 +457,10 @@ def decode_attention(q, k_cache, v_cache, count: int, sink: int, window: int,
     with torch.cuda.device(dev):
         need = _LIB.qx_decode_attention_workspace_size(B, Hq, Hkv, D, sink, window)
         ws = _workspace.get(dev, st, need, "decode_attention")
-        _lib.check(_LIB.qx_decode_attention(
+        _lib.check(_LIB.qx_decode_attention_ex(
             q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), B, Hq, Hkv, D,
             sink, window, int(count), float(softmax_scale or 0.0), ws.data_ptr(), ws.numel(),
-            st.cuda_stream), "decode_attention")
+            1 if after_append else 0, st.cuda_stream), "decode_attention")
     return out
 
 

@@ -27,6 +27,9 @@ SIGNATURES = {
     "qx_w4a16_lora_gemv": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p,
                                    c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float,
                                    c_void_p]),
+    "qx_w4a16_lora_gemv_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                          c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                          c_int, c_float, c_void_p]),
     "qx_set_pdl": (c_int, [c_int]),
     "qx_w4a16_lora_gemv_host": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_int,
@@ -63,6 +66,10 @@ SIGNATURES = {
     "qx_decode_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                     c_int, c_int, c_int, c_int64, c_float, c_void_p, c_size_t,
                                     c_void_p]),
+    "qx_decode_attention_ex": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                       c_int, c_int, c_int, c_int64, c_float, c_void_p, c_size_t,
+                                       c_int, c_void_p]),
+    "qx_decode_attention_pin_merge": (c_int, [c_int]),
     "qx_decode_attention_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                             c_int, c_int, c_int, c_int, c_int64, c_float,
                                             c_void_p]),

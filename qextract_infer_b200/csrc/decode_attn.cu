@@ -17,10 +17,18 @@
 // (4 warps) owns a chunk of slots, each warp takes 16-slot tiles staged by
 // cp.async into XOR-swizzled shared memory (double buffered), computes
 // S = Q K^T and O += P V on the tensor cores with an online softmax in fp32,
-// the warps merge in shared memory, each CTA writes (max, sum, O) for its
-// chunk, and the last CTA of each (sequence, KV head) merges the chunks and
-// writes fp16.
+// the warps merge in shared memory.  The chunks of one (sequence, KV head) are
+// then merged one of two ways:
+//  * cluster merge (when a sequence's slots are split into 2..16 chunks): the
+//    chunk CTAs form one thread-block cluster, keep their (max, sum, O) in
+//    shared memory and, after a cluster barrier, each merges a slice of the
+//    output by reading every chunk's values over distributed shared memory;
+//  * global merge (more chunks, or the cluster form pinned off): each CTA
+//    writes (max, sum, O) to the workspace and the last CTA of the
+//    (sequence, KV head), found with an atomic counter, merges them.
+// Both merges sum the chunks in a fixed order (deterministic).
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <mutex>
 
@@ -45,9 +53,12 @@ constexpr int CTAS_PER_SM = 3;
 constexpr int PSTRIDE = D + 4;                   // floats per (row) partial: m, l, pad, pad, O[D]
 constexpr int COUNTER_SLOTS = 4096;              // fixed counter region at the workspace start
 constexpr int MAX_CHUNKS = 64;                   // bounds the merge's shared memory
+constexpr int MAX_CLUSTER = 16;                  // chunks merged through distributed shared memory
+constexpr int CPART_OFF = WARPS * 16 * D * 4 + 2 * WARPS * 16 * 4;  // cluster merge: [G][PSTRIDE]
 static_assert(THREADS == D, "one thread per head dimension in the merges");
 static_assert(WARPS == 4, "the chunk merge interleaves 4 chunk subsets, one per warp");
 static_assert(2 * 16 * MAX_CHUNKS * 4 + 32 * 4 + 4 * 16 * D * 4 <= SMEM, "merge fits the tile smem");
+static_assert(CPART_OFF % 16 == 0 && CPART_OFF + 16 * PSTRIDE * 4 <= SMEM, "cluster partial fits");
 
 struct Params {
   const __half* q;
@@ -58,6 +69,10 @@ struct Params {
   float scale_log2;
   float* part;          // [B*Hkv][nch][G][PSTRIDE], O 16-byte aligned
   unsigned* counters;   // [B*Hkv]
+  int early;            // launched early: the K/V tiles of the first two rounds load before the
+                        // dependency wait, and slot `fresh` (the one the previous kernel wrote)
+                        // is reloaded after it
+  int fresh;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -91,9 +106,27 @@ __device__ __forceinline__ uint32_t swz(int r, int ch) {
   return uint32_t(r * ROW_BYTES + ((ch ^ (r & 7)) << 4));
 }
 
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// CLUSTER: the grid's x extent (the chunks of one sequence and KV head) is one
+// thread-block cluster and the chunks are merged through distributed shared
+// memory; otherwise through the workspace by the last CTA.
+template <bool CLUSTER>
 __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
   pdl_trigger();
-  pdl_wait();  // no-op unless launched with programmatic dependent launch
+  if (!p.early) pdl_wait();  // no-op unless launched with programmatic dependent launch
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ unsigned s_is_last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -109,21 +142,6 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
   const __half* vb = p.v + (size_t(b) * p.cap * p.Hkv + kvh) * D;
   unsigned char* wsm = smem + warp * WARP_SMEM;
   const uint32_t wsm_u = smem_u32(wsm);
-
-  // Q fragments (rows = query heads of this KV head, k = head dim)
-  uint32_t qa[8][4];
-  {
-    const __half* qb = p.q + (size_t(b) * p.Hq + size_t(kvh) * p.G) * D;
-    const bool r0 = g < p.G, r1 = g + 8 < p.G;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const int d0 = kk * 16 + 2 * c;
-      qa[kk][0] = r0 ? *reinterpret_cast<const uint32_t*>(qb + g * D + d0) : 0u;
-      qa[kk][1] = r1 ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * D + d0) : 0u;
-      qa[kk][2] = r0 ? *reinterpret_cast<const uint32_t*>(qb + g * D + d0 + 8) : 0u;
-      qa[kk][3] = r1 ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * D + d0 + 8) : 0u;
-    }
-  }
 
   auto issue_tile = [&](int t, int stage) {
     const uint32_t ks = wsm_u + stage * 2 * TILE_BYTES;
@@ -146,18 +164,49 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
   for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
 
+  // two tiles in flight per warp (an empty commit group where no tile is left)
   if (warp < ntiles) issue_tile(warp, 0);
-  for (int it = 0, t = warp; t < ntiles; ++it, t += WARPS) {
-    const int tn = t + WARPS;
-    if (tn < ntiles) {
-      issue_tile(tn, (it + 1) & 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+  else cp_async_commit();
+  if (warp + WARPS < ntiles) issue_tile(warp + WARPS, 1);
+  else cp_async_commit();
+  if (p.early) pdl_wait();  // q (and slot `fresh`) come from the previous kernel
+
+  // Q fragments (rows = query heads of this KV head, k = head dim)
+  uint32_t qa[8][4];
+  {
+    const __half* qb = p.q + (size_t(b) * p.Hq + size_t(kvh) * p.G) * D;
+    const bool r0 = g < p.G, r1 = g + 8 < p.G;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int d0 = kk * 16 + 2 * c;
+      qa[kk][0] = r0 ? *reinterpret_cast<const uint32_t*>(qb + g * D + d0) : 0u;
+      qa[kk][1] = r1 ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * D + d0) : 0u;
+      qa[kk][2] = r0 ? *reinterpret_cast<const uint32_t*>(qb + g * D + d0 + 8) : 0u;
+      qa[kk][3] = r1 ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * D + d0 + 8) : 0u;
     }
+  }
+
+
+  for (int it = 0, t = warp; t < ntiles; ++it, t += WARPS) {
+    cp_async_wait<1>();  // tile `it` landed; tile it + 1 may still be in flight
     __syncwarp();
     const uint32_t ks = wsm_u + (it & 1) * 2 * TILE_BYTES;
     const uint32_t vs = ks + TILE_BYTES;
+    if (p.early && it < 2) {
+      // the tiles of the first two rounds were requested before the previous
+      // kernel finished: reload the slot it wrote
+      const int r = p.fresh - (c0 + t * TILE);
+      if (r >= 0 && r < TILE && p.fresh < c1) {
+        const int ch = lane & 15;
+        const __half* src = (lane < 16 ? kb : vb) + size_t(p.fresh) * slot_stride + ch * 8;
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src));
+        const uint32_t dst = (lane < 16 ? ks : vs) + swz(r, ch);
+        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(v.x), "r"(v.y),
+                     "r"(v.z), "r"(v.w)
+                     : "memory");
+        __syncwarp();
+      }
+    }
 
     // S = Q K^T : two n-tiles of 8 slots
     float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -226,7 +275,11 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
       }
     }
     __syncwarp();
+    // the stage is free: request tile it + 2 into it
+    if (t + 2 * WARPS < ntiles) issue_tile(t + 2 * WARPS, it & 1);
+    else cp_async_commit();
   }
+  cp_async_wait<0>();
   l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 1);
   l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 2);
   l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 1);
@@ -250,7 +303,8 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
     ls[warp * 16 + g + 8] = l_r[1];
   }
   __syncthreads();
-  float* mypart = p.part + (size_t(bh) * p.nch + ci) * p.G * PSTRIDE;
+  float* mypart = CLUSTER ? reinterpret_cast<float*>(smem + CPART_OFF)
+                          : p.part + (size_t(bh) * p.nch + ci) * p.G * PSTRIDE;
   {
     const int d = tid;  // THREADS == D
     for (int r = 0; r < p.G; ++r) {
@@ -270,6 +324,45 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
         mypart[r * PSTRIDE + 1] = L;
       }
     }
+  }
+
+  if constexpr (CLUSTER) {
+    // every chunk's (max, sum, O) is in its CTA's shared memory: this CTA
+    // merges outputs [lo, hi) of the G x D block, chunks summed in order
+    cluster_sync();
+    const int nch = p.nch, G = p.G;
+    const int per = (G * D + nch - 1) / nch;
+    const int lo = ci * per, hi = min(G * D, lo + per);
+    const uint32_t base = smem_u32(smem + CPART_OFF);
+    for (int idx = lo + tid; idx < hi; idx += THREADS) {
+      const int r = idx / D, d = idx - r * D;
+      float mk[MAX_CLUSTER], lk[MAX_CLUSTER], ok[MAX_CLUSTER];
+#pragma unroll
+      for (int k = 0; k < MAX_CLUSTER; ++k) {
+        if (k < nch) {
+          const uint32_t a = cluster_map(base, uint32_t(k)) + uint32_t(r * PSTRIDE) * 4u;
+          mk[k] = ld_cluster_f32(a);
+          lk[k] = ld_cluster_f32(a + 4u);
+          ok[k] = ld_cluster_f32(a + uint32_t(4 + d) * 4u);
+        }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < MAX_CLUSTER; ++k)
+        if (k < nch) mx = fmaxf(mx, mk[k]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int k = 0; k < MAX_CLUSTER; ++k) {
+        if (k < nch) {
+          const float f = mk[k] == -INFINITY ? 0.f : exp2f(mk[k] - mx);
+          L = fmaf(lk[k], f, L);
+          O = fmaf(ok[k], f, O);
+        }
+      }
+      p.out[(size_t(b) * p.Hq + size_t(kvh) * G + r) * D + d] = __float2half_rn(O / L);
+    }
+    cluster_sync();  // the peers' shared memory stays live until every read is done
+    return;
   }
 
   // the last CTA of this (sequence, KV head) merges the chunks
@@ -357,10 +450,21 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
 
 struct Plan {
   int chunk, nch, nch_max;
+  bool cluster;  // merge the chunks through distributed shared memory
   size_t off_part, total;
 };
 
-static Plan make_plan(int batch, int kv_heads, int G, int cap, int valid, int sms) {
+// 0 (default): the cluster merge whenever a sequence has more than one chunk
+// and every (sequence, KV head) cluster of the grid is resident at once (one
+// wave: measured 10.9 vs 11.7 us at one sequence, while 32 clusters of 13
+// CTAs that took two waves ran 26.9 vs 20.7 us); 1: always the workspace
+// merge (qx_decode_attention_pin_merge)
+static std::atomic<int> g_merge_mode{0};
+
+// fit[n] (n <= MAX_CLUSTER): clusters of n CTAs the device holds at once
+// (0: not schedulable); null: no cluster merge
+static Plan make_plan(int batch, int kv_heads, int G, int cap, int valid, int sms,
+                      const int* fit = nullptr) {
   Plan pl{};
   const int bh = batch * kv_heads;
   const int target = std::min(MAX_CHUNKS, std::max(1, sms * CTAS_PER_SM / std::max(1, bh)));
@@ -374,22 +478,109 @@ static Plan make_plan(int batch, int kv_heads, int G, int cap, int valid, int sm
   pl.nch = (v + chunk - 1) / chunk;
   pl.off_part = size_t(COUNTER_SLOTS) * 4;
   pl.total = pl.off_part + size_t(bh) * pl.nch_max * G * PSTRIDE * 4;
+  pl.cluster = false;
+  const int mode = g_merge_mode.load(std::memory_order_relaxed);
+  if (fit && pl.nch >= 2 && mode != 1) {
+    // fewer, longer chunks so that one cluster holds a whole sequence's chunks
+    int maxc = 0;
+    for (int n = 2; n <= MAX_CLUSTER; ++n)
+      if (fit[n] > 0) maxc = n;
+    const int nc = std::min(pl.nch, maxc);
+    int ch = (v + std::max(nc, 1) - 1) / std::max(nc, 1);
+    ch = (ch + CHUNK_ALIGN - 1) / CHUNK_ALIGN * CHUNK_ALIGN;
+    const int n = (v + ch - 1) / ch;
+    if (nc >= 2 && n >= 2 && n <= maxc && fit[n] >= bh) {
+      pl.chunk = ch;
+      pl.nch = n;
+      pl.cluster = true;
+    }
+  }
   return pl;
 }
 
-// Raises the kernel's dynamic shared-memory limit once per device (both
-// entry points; the per-device flags are guarded by a mutex).
-static int prepare_kernel() {
+// Raises the kernels' dynamic shared-memory limits once per device (both
+// entry points; the per-device state is guarded by a mutex) and records, per
+// cluster size n <= 16, how many chunk clusters the device holds at once.
+static int prepare_kernel(const int** fit_out) {
   static std::mutex mu;
   static bool done[64] = {};
+  static int fit[64][MAX_CLUSTER + 1] = {};
   int dev = 0;
   QX_CUDA_TRY(cudaGetDevice(&dev), "decode_attention: cudaGetDevice");
+  QX_REQUIRE(dev >= 0 && dev < 64, "decode_attention: device index %d unsupported", dev);
   std::lock_guard<std::mutex> lk(mu);
-  if (dev >= 0 && dev < 64 && done[dev]) return QX_OK;
-  QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM),
-              "decode_attention: set smem limit");
-  if (dev >= 0 && dev < 64) done[dev] = true;
+  if (!done[dev]) {
+    QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM),
+                "decode_attention: set smem limit");
+    QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<true>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM),
+                "decode_attention: set smem limit");
+    QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<true>,
+                                     cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                "decode_attention: allow 16-CTA clusters");
+    for (int cs = 2; cs <= MAX_CLUSTER; ++cs) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(cs, 1, 1);
+      cfg.blockDim = dim3(THREADS, 1, 1);
+      cfg.dynamicSmemBytes = SMEM;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = cs;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, decode_attn_kernel<true>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+      fit[dev][cs] = n;
+    }
+    done[dev] = true;
+  }
+  *fit_out = fit[dev];
   return QX_OK;
+}
+
+// Launches the kernel of plan `pl`: clusters of pl.nch CTAs along x for the
+// cluster merge, a plain grid otherwise (measured: launched early, its CTAs
+// wait resident and the grid lands less evenly, 82 vs 89 us at 32 sequences;
+// it still triggers at entry, so the GEMV after it streams its weights
+// meanwhile).
+static int launch(const Plan& pl, const Params& prm, int batch, int kv_heads, cudaStream_t st,
+                  const char* what) {
+  const dim3 grid(pl.nch, batch * kv_heads), block(THREADS);
+  if (!pl.cluster && !prm.early) {
+    decode_attn_kernel<false><<<grid, block, SMEM, st>>>(prm);
+    return check_launch(what);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  int na = 0;
+  if (pl.cluster) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = pl.nch;
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (prm.early) {
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = na;
+  QX_CUDA_TRY(pl.cluster ? cudaLaunchKernelEx(&cfg, decode_attn_kernel<true>, prm)
+                         : cudaLaunchKernelEx(&cfg, decode_attn_kernel<false>, prm),
+              what);
+  return check_launch(what);
 }
 
 }  // namespace attn
@@ -407,10 +598,12 @@ extern "C" size_t qx_decode_attention_workspace_size(int batch, int q_heads, int
       .total;
 }
 
-extern "C" int qx_decode_attention(const void* q, const void* k_cache, const void* v_cache,
-                                   void* out, int batch, int q_heads, int kv_heads, int head_dim,
-                                   int sink, int window, int64_t count, float softmax_scale,
-                                   void* workspace, size_t workspace_bytes, qx_stream_t stream) {
+extern "C" int qx_decode_attention_ex(const void* q, const void* k_cache, const void* v_cache,
+                                      void* out, int batch, int q_heads, int kv_heads, int head_dim,
+                                      int sink, int window, int64_t count, float softmax_scale,
+                                      void* workspace, size_t workspace_bytes, int flags,
+                                      qx_stream_t stream) {
+  QX_REQUIRE((flags & ~QX_ATTN_AFTER_APPEND) == 0, "decode_attention: unknown flags %d", flags);
   QX_REQUIRE(batch > 0 && q_heads > 0 && kv_heads > 0 && q_heads % kv_heads == 0,
              "decode_attention: bad heads q=%d kv=%d", q_heads, kv_heads);
   QX_REQUIRE(head_dim == attn::D, "decode_attention: head_dim=%d unsupported (128)", head_dim);
@@ -427,7 +620,13 @@ extern "C" int qx_decode_attention(const void* q, const void* k_cache, const voi
   const int64_t valid64 = count <= sink ? count : sink + std::min<int64_t>(count - sink, window);
   const int valid = int(valid64);
   const int G = q_heads / kv_heads;
-  const attn::Plan pl = attn::make_plan(batch, kv_heads, G, cap, valid, device_sm_count());
+  const int* fit = nullptr;
+  {
+    const int rc = attn::prepare_kernel(&fit);
+    if (rc != QX_OK) return rc;
+  }
+  const attn::Plan pl =
+      attn::make_plan(batch, kv_heads, G, cap, valid, device_sm_count(), fit);
   if (!workspace || workspace_bytes < pl.total || !aligned(workspace, 256))
     return fail(QX_ERR_WORKSPACE, "decode_attention: workspace needs %zu bytes, 256-byte aligned",
                 pl.total);
@@ -448,16 +647,33 @@ extern "C" int qx_decode_attention(const void* q, const void* k_cache, const voi
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   prm.counters = reinterpret_cast<unsigned*>(ws);
   prm.part = reinterpret_cast<float*>(ws + pl.off_part);
-  {
-    const int rc = attn::prepare_kernel();
-    if (rc != QX_OK) return rc;
-  }
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  // plain launch (measured: launched early, its CTAs wait resident and the
-  // grid lands less evenly; 82 vs 89 us at 32 sequences); it still triggers
-  // at entry, so the GEMV after it streams its weights meanwhile
-  attn::decode_attn_kernel<<<dim3(pl.nch, batch * kv_heads), attn::THREADS, attn::SMEM, st>>>(prm);
-  return check_launch("decode_attention");
+  // after an append of position count - 1 (its physical slot is `fresh`) by
+  // the previous kernel: load the other slots while it finishes
+  // (small grids only: measured on the append + attention pair, one sequence
+  // 12.4 vs 12.7 us, while 32 sequences' waiting CTAs landed unevenly, 95.7
+  // vs 85.0 us)
+  prm.early = (flags & QX_ATTN_AFTER_APPEND) && g_pdl_enabled.load(std::memory_order_relaxed) &&
+                      long(pl.nch) * batch * kv_heads <= 2L * device_sm_count()
+                  ? 1
+                  : 0;
+  const int64_t last = count - 1;
+  prm.fresh = int(last < sink ? last : sink + (last - sink) % window);
+  return attn::launch(pl, prm, batch, kv_heads, reinterpret_cast<cudaStream_t>(stream),
+                      "decode_attention");
+}
+
+extern "C" int qx_decode_attention(const void* q, const void* k_cache, const void* v_cache,
+                                   void* out, int batch, int q_heads, int kv_heads, int head_dim,
+                                   int sink, int window, int64_t count, float softmax_scale,
+                                   void* workspace, size_t workspace_bytes, qx_stream_t stream) {
+  return qx_decode_attention_ex(q, k_cache, v_cache, out, batch, q_heads, kv_heads, head_dim, sink, window,
+                                count, softmax_scale, workspace, workspace_bytes, 0, stream);
+}
+
+extern "C" int qx_decode_attention_pin_merge(int mode) {
+  QX_REQUIRE(mode == 0 || mode == 1, "decode_attention_pin_merge: mode %d (0 auto, 1 workspace)", mode);
+  attn::g_merge_mode.store(mode);
+  return QX_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -522,7 +738,13 @@ extern "C" int qx_decode_attention_noalloc(const void* q, const void* k_cache,
   const int64_t valid64 = count <= sink ? count : sink + std::min<int64_t>(count - sink, window);
   const int valid = int(valid64);
   const int G = q_heads / kv_heads;
-  const attn::Plan pl = attn::make_plan(batch, kv_heads, G, cap, valid, device_sm_count());
+  const int* fit = nullptr;
+  {
+    const int rc = attn::prepare_kernel(&fit);
+    if (rc != QX_OK) return rc;
+  }
+  const attn::Plan pl =
+      attn::make_plan(batch, kv_heads, G, cap, valid, device_sm_count(), fit);
   if (pl.total > size_t(QX_DECODE_ATTN_NOALLOC_SCRATCH_BYTES))
     return fail(QX_ERR_UNSUPPORTED,
                 "decode_attention_noalloc: this shape needs %zu bytes of scratch, more than the "
@@ -552,10 +774,5 @@ extern "C" int qx_decode_attention_noalloc(const void* q, const void* k_cache,
   unsigned char* ws = static_cast<unsigned char*>(scratch);
   prm.counters = reinterpret_cast<unsigned*>(ws);
   prm.part = reinterpret_cast<float*>(ws + pl.off_part);
-  {
-    const int rc = attn::prepare_kernel();
-    if (rc != QX_OK) return rc;
-  }
-  attn::decode_attn_kernel<<<dim3(pl.nch, batch * kv_heads), attn::THREADS, attn::SMEM, st>>>(prm);
-  return check_launch("decode_attention_noalloc");
+  return attn::launch(pl, prm, batch, kv_heads, st, "decode_attention_noalloc");
 }

@@ -6,25 +6,32 @@
 //   x[r] <- fp16(x[r] + fp16(sum over ranks of partial[r]))   (in place)
 //   y[r]  = fp16((x[r] * rsqrt(mean(x[r]^2) + eps)) * w)
 //
-// Every rank owns a buffer shared with its peers through CUDA IPC:
-//   data[2][max_rows][hidden] fp16   (double-buffered by epoch parity)
-//   flags[max_rows] u32              (epoch of the row last published)
-// and a private counter per row (CTA).  One CTA per row r, per call:
-//   1. e = counter[r] + 1; copy partial[r] into data[e & 1][r] (local stores),
-//      then one thread: fence.sys + st.release.sys flags[r] = e;
-//   2. one thread per peer polls the peer's flags[r] (ld.acquire.sys over
-//      NVLink) until it reaches e, bounded (2 s by %globaltimer unless
-//      qx_nvlink_ar_set_timeout says otherwise; on timeout the device error
-//      word gets QX_DEVERR_PEER_TIMEOUT and the row is reduced with whatever is
-//      there, so the output of that call is undefined);
-//   3. every rank sums the world rows in rank order (fp32, L2-only loads of
-//      peer memory), rounds once, adds the residual, RMS-normalises; all ranks
-//      compute identical bits.
-// Parity makes a buffer reusable: a rank overwrites data[p] for epoch e + 2
-// only after finishing e + 1, which needed every peer's flag e + 1, which each
-// peer sets only after it finished reading epoch e.  Calls must not overlap on
-// one rank (plain stream order, no programmatic dependent launch) and every
-// rank must make the same sequence of calls.
+// Push protocol with the epoch carried in every word.  Every rank owns an
+// inbox shared with its peers through CUDA IPC:
+//   inbox[2][world][max_rows][hidden / 2] u64   (parity, source rank, row)
+// whose words are (two fp16 of a partial row) | (epoch << 32).  One CTA per
+// row r, per call, with e = counter[r] + 1:
+//   1. the CTA reads its partial row and stores it, tagged with e, straight
+//      into every peer's inbox[e & 1][rank][r] (relaxed system-scope 64-bit
+//      stores over NVLink: no fence, no separate flag);
+//   2. it polls its own, local inbox[e & 1][src][r] for every peer src until
+//      each word carries e (a 64-bit access is single-copy atomic, so a word
+//      with the right tag holds that epoch's data), bounded by the wait limit
+//      (2 s by %globaltimer unless qx_nvlink_ar_set_timeout says otherwise; on
+//      timeout the device error word gets QX_DEVERR_PEER_TIMEOUT and the row is
+//      reduced with whatever is there, so that call's output is undefined);
+//   3. it sums the world rows in rank order (fp32; its own from registers),
+//      rounds once, adds the residual and RMS-normalises: every rank computes
+//      identical bits.
+// Only one-way NVLink writes sit on the critical path (the pull form it
+// replaces paid a system fence, a remote flag poll and remote data loads).
+// Parity makes an inbox slot reusable: a rank writes epoch e + 2 of row r into
+// a peer's slot only after its own call with epoch e + 1 finished, which needed
+// that peer's epoch e + 1 words, which the peer sends only after its call with
+// epoch e (the reader of the slot) completed.  Calls must not overlap on one
+// rank (stream order: each call waits for the previous kernel's completion
+// before it touches the inbox or the counters) and every rank makes the same
+// sequence of calls.
 #include <algorithm>
 #include <cstring>
 #include <vector>
@@ -40,12 +47,12 @@ constexpr int THREADS = 256;
 
 struct Ctx {
   int world = 0, rank = 0, max_rows = 0, hidden = 0, device = -1;
-  size_t data_bytes = 0;  // one parity half
-  char* own = nullptr;    // this rank's shared buffer (data[2] then flags)
+  size_t data_bytes = 0;  // one parity half of the inbox
+  char* own = nullptr;    // this rank's inbox
   uint32_t* counter = nullptr;  // private: epochs per row
-  char* peer[MAX_WORLD] = {};   // every rank's buffer as mapped here (own included)
+  char* peer[MAX_WORLD] = {};   // every rank's inbox as mapped here (own included)
   bool opened[MAX_WORLD] = {};  // peer[r] is an IPC mapping to close at destroy
-  uint64_t timeout_ns = 2000000000ull;  // limit of each wait for a peer's flag
+  uint64_t timeout_ns = 2000000000ull;  // limit of each wait for a peer's words
 };
 
 struct Params {
@@ -53,24 +60,23 @@ struct Params {
   __half* x;
   const __half* w;
   __half* y;
-  const char* buf[MAX_WORLD];
-  uint32_t* own_flags;
+  char* buf[MAX_WORLD];
   uint32_t* counter;
-  size_t data_bytes;
+  size_t data_bytes, src_bytes;  // parity half; one source rank's block
   uint64_t timeout_ns;
-  int world, rank, hidden, flags_off;
+  int world, rank, hidden;
   float eps;
 };
 
 static __device__ unsigned g_ar_error = 0;
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ uint64_t gtime() {
   uint64_t t;
@@ -78,86 +84,103 @@ __device__ __forceinline__ uint64_t gtime() {
   return t;
 }
 
+// VPT: 32-bit words (two fp16) of the row per thread, hidden / 2 <= VPT * THREADS
 template <int VPT>
 __global__ void __launch_bounds__(THREADS) ar_add_rmsnorm_kernel(const Params p) {
-  // the next GEMV may start streaming its weights now; it waits for this
-  // kernel's completion before reading x (calls of this kernel still never
-  // overlap: the kernels between two of them wait for their predecessors)
+  // the next kernel may launch now; it waits for this one's completion before
+  // it reads x or y.  This kernel waits for its predecessor (the projection
+  // that wrote `partial`, and transitively the previous call) before it reads
+  // anything.
   pdl_trigger();
+  pdl_wait();
   __shared__ float s_part[THREADS / 32];
   __shared__ float s_r;
   const int row = blockIdx.x, tid = threadIdx.x;
-  const int h8 = p.hidden / 8;
+  const int h2 = p.hidden / 2;
   const uint32_t e = p.counter[row] + 1;
-  const size_t off = size_t(e & 1) * p.data_bytes + size_t(row) * p.hidden * 2;
-  // 1. publish this rank's partial row
+  const uint64_t tag = uint64_t(e) << 32;
+  const size_t slot = size_t(e & 1) * p.data_bytes + size_t(row) * h2 * 8;
+
+  // 1. this rank's partial row, pushed into every peer's inbox
+  uint32_t mine[VPT];
   {
-    const uint4* src = reinterpret_cast<const uint4*>(p.partial + size_t(row) * p.hidden);
-    uint4* dst = reinterpret_cast<uint4*>(const_cast<char*>(p.buf[p.rank]) + off);
-    for (int i = tid; i < h8; i += THREADS) dst[i] = src[i];
-  }
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence_system();
-    st_release_sys(p.own_flags + row, e);
-  }
-  // 2. wait for every peer's row of this epoch
-  if (tid < p.world && tid != p.rank) {
-    const uint32_t* f = reinterpret_cast<const uint32_t*>(p.buf[tid] + p.flags_off) + row;
-    if (ld_acquire_sys(f) < e) {
-      const uint64_t t0 = gtime();
-      while (ld_acquire_sys(f) < e) {
-        if (gtime() - t0 > p.timeout_ns) {
-          atomicOr(&g_ar_error, QX_DEVERR_PEER_TIMEOUT);
-          break;
-        }
-      }
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(p.partial + size_t(row) * p.hidden);
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int i = tid + v * THREADS;
+      mine[v] = i < h2 ? src[i] : 0u;
     }
   }
-  __syncthreads();
-  // 3. sum in rank order, residual add, RMSNorm
-  uint4 xv[VPT];
+  for (int r = 0; r < p.world; ++r) {
+    if (r == p.rank) continue;
+    uint64_t* dst = reinterpret_cast<uint64_t*>(p.buf[r] + slot + size_t(p.rank) * p.src_bytes);
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int i = tid + v * THREADS;
+      if (i < h2) st_relaxed_sys_u64(dst + i, tag | mine[v]);
+    }
+  }
+
+  // 2./3. every peer's words from the local inbox, summed in rank order
+  float acc[VPT][2];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) acc[v][0] = acc[v][1] = 0.f;
+  uint64_t t0 = 0;
+  bool late = false;  // this thread's wait ran out: stop waiting
+  for (int r = 0; r < p.world; ++r) {
+    uint32_t d[VPT];
+    if (r == p.rank) {
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) d[v] = mine[v];
+    } else {
+      const uint64_t* in = reinterpret_cast<const uint64_t*>(p.buf[p.rank] + slot + size_t(r) * p.src_bytes);
+      uint64_t wv[VPT];
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int i = tid + v * THREADS;
+        wv[v] = i < h2 ? ld_relaxed_sys_u64(in + i) : tag;
+      }
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int i = tid + v * THREADS;
+        while (!late && uint32_t(wv[v] >> 32) != e) {
+          const uint64_t now = gtime();
+          if (t0 == 0) t0 = now;
+          if (now - t0 > p.timeout_ns) {
+            atomicOr(&g_ar_error, QX_DEVERR_PEER_TIMEOUT);
+            late = true;
+            break;
+          }
+          wv[v] = ld_relaxed_sys_u64(in + i);
+        }
+        d[v] = uint32_t(wv[v]);
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const float2 f = h2_to_f2(d[v]);
+      acc[v][0] += f.x;
+      acc[v][1] += f.y;
+    }
+  }
+
+  // residual add (the all-reduced value rounded once, then the add rounded)
+  uint32_t xv[VPT];
   float ss = 0.f;
+  uint32_t* xrow = reinterpret_cast<uint32_t*>(p.x + size_t(row) * p.hidden);
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
     const int i = tid + v * THREADS;
-    xv[v] = make_uint4(0u, 0u, 0u, 0u);
-    if (i < h8) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      // every rank's 16 bytes requested at once (NVLink round trips overlap),
-      // then summed in rank order
-      uint4 d[MAX_WORLD];
-#pragma unroll
-      for (int r = 0; r < MAX_WORLD; ++r)
-        d[r] = r < p.world ? __ldcg(reinterpret_cast<const uint4*>(p.buf[r] + off) + i)
-                           : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-      for (int r = 0; r < MAX_WORLD; ++r) {
-        if (r >= p.world) break;
-        const uint32_t dd[4] = {d[r].x, d[r].y, d[r].z, d[r].w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = h2_to_f2(dd[j]);
-          acc[2 * j] += f.x;
-          acc[2 * j + 1] += f.y;
-        }
-      }
-      const uint4 xo = reinterpret_cast<const uint4*>(p.x + size_t(row) * p.hidden)[i];
-      const uint32_t xd[4] = {xo.x, xo.y, xo.z, xo.w};
-      uint32_t od[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 fx = h2_to_f2(xd[j]);
-        const __half2 s2 = __floats2half2_rn(acc[2 * j], acc[2 * j + 1]);  // the all-reduced value
-        const float2 fs = __half22float2(s2);
-        const __half2 n2 = __floats2half2_rn(fx.x + fs.x, fx.y + fs.y);    // the residual add
-        od[j] = *reinterpret_cast<const uint32_t*>(&n2);
-        const float2 fn = __half22float2(n2);
-        ss = fmaf(fn.x, fn.x, ss);
-        ss = fmaf(fn.y, fn.y, ss);
-      }
-      xv[v] = make_uint4(od[0], od[1], od[2], od[3]);
-      reinterpret_cast<uint4*>(p.x + size_t(row) * p.hidden)[i] = xv[v];
+    xv[v] = 0u;
+    if (i < h2) {
+      const float2 fx = h2_to_f2(xrow[i]);
+      const float2 fs = __half22float2(__floats2half2_rn(acc[v][0], acc[v][1]));
+      const __half2 n2 = __floats2half2_rn(fx.x + fs.x, fx.y + fs.y);
+      xv[v] = *reinterpret_cast<const uint32_t*>(&n2);
+      xrow[i] = xv[v];
+      const float2 fn = __half22float2(n2);
+      ss = fmaf(fn.x, fn.x, ss);
+      ss = fmaf(fn.y, fn.y, ss);
     }
   }
   ss = warp_sum(ss);
@@ -170,20 +193,15 @@ __global__ void __launch_bounds__(THREADS) ar_add_rmsnorm_kernel(const Params p)
   }
   __syncthreads();
   const float rr = s_r;
+  const uint32_t* wrow = reinterpret_cast<const uint32_t*>(p.w);
+  uint32_t* yrow = reinterpret_cast<uint32_t*>(p.y + size_t(row) * p.hidden);
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
     const int i = tid + v * THREADS;
-    if (i < h8) {
-      const uint4 wv = reinterpret_cast<const uint4*>(p.w)[i];
-      const uint32_t vd[4] = {xv[v].x, xv[v].y, xv[v].z, xv[v].w}, wd[4] = {wv.x, wv.y, wv.z, wv.w};
-      uint32_t od[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = h2_to_f2(vd[j]), g = h2_to_f2(wd[j]);
-        const __half2 o = __floats2half2_rn((f.x * rr) * g.x, (f.y * rr) * g.y);
-        od[j] = *reinterpret_cast<const uint32_t*>(&o);
-      }
-      reinterpret_cast<uint4*>(p.y + size_t(row) * p.hidden)[i] = make_uint4(od[0], od[1], od[2], od[3]);
+    if (i < h2) {
+      const float2 f = h2_to_f2(xv[v]), g = h2_to_f2(wrow[i]);
+      const __half2 o = __floats2half2_rn((f.x * rr) * g.x, (f.y * rr) * g.y);
+      yrow[i] = *reinterpret_cast<const uint32_t*>(&o);
     }
   }
   if (tid == 0) p.counter[row] = e;
@@ -218,11 +236,11 @@ extern "C" int qx_nvlink_ar_create(int world, int rank, int max_rows, int hidden
   c->rank = rank;
   c->max_rows = max_rows;
   c->hidden = hidden;
-  c->data_bytes = (size_t(max_rows) * hidden * 2 + 255) & ~size_t(255);
-  const size_t flags_bytes = (size_t(max_rows) * 4 + 255) & ~size_t(255);
+  // inbox: [2 parities][world sources][max_rows][hidden / 2] tagged 64-bit words
+  c->data_bytes = size_t(world) * max_rows * (hidden / 2) * 8;
   cudaError_t e = cudaGetDevice(&c->device);
-  if (e == cudaSuccess) e = cudaMalloc(&c->own, 2 * c->data_bytes + flags_bytes);
-  if (e == cudaSuccess) e = cudaMemset(c->own, 0, 2 * c->data_bytes + flags_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&c->own, 2 * c->data_bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->own, 0, 2 * c->data_bytes);  // epoch 0: never a live tag
   if (e == cudaSuccess) e = cudaMalloc(&c->counter, size_t(max_rows) * 4);
   if (e == cudaSuccess) e = cudaMemset(c->counter, 0, size_t(max_rows) * 4);
   cudaIpcMemHandle_t h;
@@ -318,22 +336,26 @@ extern "C" int qx_nvlink_ar_add_rmsnorm(void* ctx, const void* partial, void* x,
   p.w = static_cast<const __half*>(weight);
   p.y = static_cast<__half*>(y);
   for (int r = 0; r < c->world; ++r) p.buf[r] = c->peer[r];
-  p.flags_off = int(2 * c->data_bytes);
-  p.own_flags = reinterpret_cast<uint32_t*>(c->own + 2 * c->data_bytes);
   p.counter = c->counter;
   p.data_bytes = c->data_bytes;
+  p.src_bytes = size_t(c->max_rows) * (c->hidden / 2) * 8;
   p.timeout_ns = c->timeout_ns;
   p.world = c->world;
   p.rank = c->rank;
   p.hidden = c->hidden;
   p.eps = eps;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int h8 = c->hidden / 8;
-  if (h8 <= nvar::THREADS)
-    nvar::ar_add_rmsnorm_kernel<1><<<rows, nvar::THREADS, 0, st>>>(p);
-  else if (h8 <= 2 * nvar::THREADS)
-    nvar::ar_add_rmsnorm_kernel<2><<<rows, nvar::THREADS, 0, st>>>(p);
+  const int h2 = c->hidden / 2;
+  const dim3 grid(rows), block(nvar::THREADS);
+  cudaError_t le;
+  if (h2 <= 2 * nvar::THREADS)
+    le = launch_pdl(nvar::ar_add_rmsnorm_kernel<2>, grid, block, 0, st, p);
+  else if (h2 <= 4 * nvar::THREADS)
+    le = launch_pdl(nvar::ar_add_rmsnorm_kernel<4>, grid, block, 0, st, p);
+  else if (h2 <= 8 * nvar::THREADS)
+    le = launch_pdl(nvar::ar_add_rmsnorm_kernel<8>, grid, block, 0, st, p);
   else
-    nvar::ar_add_rmsnorm_kernel<4><<<rows, nvar::THREADS, 0, st>>>(p);
+    le = launch_pdl(nvar::ar_add_rmsnorm_kernel<16>, grid, block, 0, st, p);
+  QX_CUDA_TRY(le, "nvlink_ar_add_rmsnorm: launch");
   return check_launch("nvlink_ar_add_rmsnorm");
 }

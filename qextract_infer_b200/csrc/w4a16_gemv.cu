@@ -115,6 +115,9 @@ struct alignas(64) Params {
   int zeros_tma;  // zero points by TMA (fp16 always; packed when rows are 16 B multiples)
   float lora_scale;
   int T, S, cpr, Ts_max, gmax, nst, pdl;
+  int act;                      // 1: SwiGLU epilogue over column blocks (8 gate, 8 up), y [M][N/2]
+  int x_early;                  // x is not written by the previous kernel (host rows): read it
+                                // before the dependency wait, wait before the output stores
   int stage;                    // bytes per ring stage: a group's packed weights, then its LoRA A rows
   uint32_t s_magic, cpr_magic;  // ceil(2^32 / S) (S > 1), ceil(2^32 / cpr): exact floor division of small values
   Layout lay;                   // shared-memory carve-up, computed on the host
@@ -131,8 +134,20 @@ __host__ __device__ inline unsigned take(unsigned& o, size_t bytes) {
 // 4 banks apart, so 8 rows x 4 words of an MMA fragment hit distinct banks
 __host__ __device__ inline int xstride(int Ts_max) { return Ts_max * KSTEP + 8; }
 
-// columns each CTA of an S-cluster finalises: 256 / S rounded up to 8
-__host__ __device__ inline int owner_cols(int S) { return ((COLS + S - 1) / S + 7) / 8 * 8; }
+// columns each CTA of an S-cluster finalises: 256 / S rounded up to 8 (to 16
+// with the SwiGLU epilogue: an owner holds whole gate|up column-block pairs)
+__host__ __device__ inline int owner_cols(int S, int act = 0) {
+  const int q = act ? 16 : 8;
+  return ((COLS + S - 1) / S + q - 1) / q * q;
+}
+
+// silu(g) * u with the fast exponential and divide (the formula of
+// qx_fused_swiglu)
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return __fdividef(g, 1.0f + __expf(-g)) * u;
+}
+// the fp16 rounding of a column's sum, as the unfused GEMV stores it
+__device__ __forceinline__ float round_h(float v) { return __half2float(__float2half_rn(v)); }
 
 // LoRA down-projection, one quantisation group at a time as its ring stage
 // lands (the stage holds the group's LoRA A rows beside its weights, so no
@@ -151,7 +166,7 @@ __host__ __device__ inline int stage_bytes(int KPG, int rank) {
 
 // M = batch rows of this launch (<= 32).
 __host__ __device__ inline Layout layout(int M, int KPG, int Ts_max, int rank, int S, int nst,
-                                         int zeros_packed) {
+                                         int zeros_packed, int act = 0) {
   const int gmax = Ts_max / KPG;
   const size_t Mp = M <= 8 ? 8 : (M <= 16 ? 16 : 32);  // NT * 8 of the kernel instance
   Layout L;
@@ -166,7 +181,7 @@ __host__ __device__ inline Layout layout(int M, int KPG, int Ts_max, int rank, i
   L.xks = take(o, size_t(gmax) * Mp * 2 * 4);         // per group (Off, Sx) per row [g][Mp]
   L.Bs = take(o, size_t(rank) * COLS * 2);            // LoRA B tile [r][256]
   L.hs = take(o, size_t(M) * rank * 4);                // h_s [M][r]
-  L.recv = take(o, size_t(S) * M * owner_cols(S) * 4);  // partials from the cluster [S][M][cpr]
+  L.recv = take(o, size_t(S) * M * owner_cols(S, act) * 4);  // partials from the cluster [S][M][cpr]
   L.total = o;
   return L;
 }
@@ -420,7 +435,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     if (tid < 4) xsw[size_t(p.Ts_max) * M * 4 + tid] = make_uint4(0u, 0u, 0u, 0u);
     // the activations may come from the previous kernel in the stream: wait
     // for it here, after every weight and static copy has been started
-    if (p.pdl) grid_dep_wait();
+    if (p.pdl && !p.x_early) grid_dep_wait();
     const __half* xg = p.x + k0;
     for (int id = warp; id < M * TB; id += WARPS + 1) {
       const int m = id / TB, it = (id - m * TB) * 32 + lane, t = it >> 2, cc = it & 3;
@@ -733,6 +748,9 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     }
   }
 
+  // host-resident activations were read before the dependency wait: the
+  // previous kernel may still write the output (a previous call's y)
+  if (p.pdl && p.x_early) grid_dep_wait();
   // send the partial of the columns owned by CTA j into j's receive area
   // [S][M][CPR] (rows nt*8 + 2c (+1), columns lcol + 2pp (+1))
   asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
@@ -757,6 +775,23 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   if (own_cols > 0) {
     mbar_wait(bar_rv, 0);
     const int cb = n_tile0 + s * CPR;
+    if (p.act) {
+      // SwiGLU: output j of the block pair (gate cols 16b..16b+7, up cols
+      // 16b+8..16b+15) = silu(g) u from the fp16-rounded sums, at y[m][cb/2 + j]
+      const int nout = own_cols >> 1, N2 = N >> 1;
+      for (int it = tid; it < M * nout; it += WARPS * 32) {
+        const int m = it / nout, j = it - m * nout;
+        const int cg = (j >> 3) * 16 + (j & 7);
+        float gs = 0.f, us = 0.f;
+        for (int r2 = 0; r2 < S; ++r2) {
+          const float* rv = recv + (size_t(r2) * M + m) * CPR;
+          gs += rv[cg];
+          us += rv[cg + 8];
+        }
+        p.y[size_t(m) * N2 + (cb >> 1) + j] = __float2half_rn(silu_mul(round_h(gs), round_h(us)));
+      }
+      return;
+    }
     if (M == 1) {
       for (int cc = tid; cc < own_cols; cc += WARPS * 32) {
         float v = 0.f;
@@ -981,7 +1016,8 @@ static int run(Params prm, cudaStream_t st) {
   uint32_t ls_bits;
   std::memcpy(&ls_bits, &prm.lora_scale, 4);
   const ParamKey key{prm.qw, prm.scales, prm.zeros, prm.A, prm.B, dev, prm.M, prm.K, prm.N, prm.rank,
-                     prm.group, prm.zeros_packed, prm.zero_offset, prm.pdl, NT, KPG * 2 + (LW ? 1 : 0), ls_bits};
+                     prm.group, prm.zeros_packed, prm.zero_offset, prm.pdl + 2 * prm.act + 4 * prm.x_early, NT, KPG * 2 + (LW ? 1 : 0),
+                     ls_bits};
   Plan pl;
   bool hit = false;
   {
@@ -1016,9 +1052,15 @@ static int build_params(Params& prm, Plan* plo) {
   prm.T = pl.T;
   prm.S = pl.S;
   prm.s_magic = pl.S > 1 ? uint32_t((0x100000000ull + pl.S - 1) / pl.S) : 0u;
-  prm.cpr_magic = uint32_t((0x100000000ull + owner_cols(pl.S) - 1) / owner_cols(pl.S));
-  prm.lay = layout(prm.M, KPG, pl.Ts_max, prm.rank, pl.S, pl.nst, prm.zeros_packed);
-  prm.cpr = owner_cols(pl.S);
+  // the SwiGLU epilogue keeps the plan of the plain GEMV (the same split of K,
+  // hence the same sums) with owners of whole 16-column block pairs
+  const int ocols = owner_cols(pl.S, prm.act);
+  prm.cpr_magic = uint32_t((0x100000000ull + ocols - 1) / ocols);
+  prm.lay = layout(prm.M, KPG, pl.Ts_max, prm.rank, pl.S, pl.nst, prm.zeros_packed, prm.act);
+  if (prm.lay.total > SMEM_LIMIT)
+    return fail(QX_ERR_UNSUPPORTED, "w4a16_gemv_swiglu: shared memory %u over the limit", prm.lay.total);
+  pl.smem = prm.lay.total;
+  prm.cpr = ocols;
   prm.Ts_max = pl.Ts_max;
   prm.gmax = pl.Ts_max / KPG;
   prm.nst = pl.nst;
@@ -1120,6 +1162,26 @@ extern "C" int qx_get_device_error(unsigned* code, int reset) {
   return QX_OK;
 }
 
+namespace qx {
+namespace gemv {
+// The device address of host memory the device can access (pinned / mapped),
+// else null.
+static void* device_view(const void* host) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, host) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+}
+}  // namespace gemv
+}  // namespace qx
+
+static int w4a16_gemv_entry(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
+                            int zeros_packed, int zero_offset, const void* lora_A, const void* lora_B, void* y,
+                            int M, int K, int N, int rank, int group_size, float lora_scale,
+                            qx_stream_t stream, int act, int x_early);
+
 extern "C" int qx_w4a16_lora_gemv_host(const void* x_host, void* y_host, void* x_dev, void* y_dev,
                                        const int32_t* qweight, const void* scales, const void* zeros,
                                        int zeros_packed, int zero_offset, const void* lora_A,
@@ -1129,13 +1191,36 @@ extern "C" int qx_w4a16_lora_gemv_host(const void* x_host, void* y_host, void* x
   QX_REQUIRE(M >= 0 && K > 0 && N > 0, "w4a16_gemv_host: bad sizes M=%d K=%d N=%d", M, K, N);
   if (M == 0) return QX_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  QX_CUDA_TRY(cudaMemcpyAsync(x_dev, x_host, size_t(M) * K * 2, cudaMemcpyHostToDevice, st),
-              "w4a16_gemv_host: copy x to the device");
-  const int rc = qx_w4a16_lora_gemv(x_dev, qweight, scales, zeros, zeros_packed, zero_offset, lora_A, lora_B,
-                                    y_dev, M, K, N, rank, group_size, lora_scale, stream);
+  const size_t xbytes = size_t(M) * K * 2;
+  // pinned (device-mapped) host rows: the GEMV reads x_host itself, before
+  // its dependency wait (the host wrote x before this call), so the read
+  // overlaps the previous kernel; pageable rows: a copy into x_dev
+  // (unless x_host overlaps the y_host of the previous call made here, which
+  // that call's GEMV may still be writing: then the read waits)
+  static std::mutex last_mu;
+  static uintptr_t last_y0 = 0, last_y1 = 0;
+  const uintptr_t x0 = reinterpret_cast<uintptr_t>(x_host), x1 = x0 + xbytes;
+  const uintptr_t y0 = reinterpret_cast<uintptr_t>(y_host), y1 = y0 + size_t(M) * N * 2;
+  bool early;
+  {
+    std::lock_guard<std::mutex> lk(last_mu);
+    early = x1 <= last_y0 || last_y1 <= x0;
+    last_y0 = y0;
+    last_y1 = y1;
+  }
+  const void* xh = gemv::device_view(x_host);
+  if (!xh)
+    QX_CUDA_TRY(cudaMemcpyAsync(x_dev, x_host, xbytes, cudaMemcpyHostToDevice, st),
+                "w4a16_gemv_host: copy x to the device");
+  // y: written by the GEMV straight into pinned host memory; else a copy
+  void* yh = gemv::device_view(y_host);
+  const int rc = w4a16_gemv_entry(xh ? xh : x_dev, qweight, scales, zeros, zeros_packed, zero_offset, lora_A,
+                                  lora_B, yh ? yh : y_dev, M, K, N, rank, group_size, lora_scale, stream, 0,
+                                  xh && early ? 1 : 0);
   if (rc != QX_OK) return rc;
-  QX_CUDA_TRY(cudaMemcpyAsync(y_host, y_dev, size_t(M) * N * 2, cudaMemcpyDeviceToHost, st),
-              "w4a16_gemv_host: copy y to the host");
+  if (!yh)
+    QX_CUDA_TRY(cudaMemcpyAsync(y_host, y_dev, size_t(M) * N * 2, cudaMemcpyDeviceToHost, st),
+                "w4a16_gemv_host: copy y to the host");
   return QX_OK;
 }
 
@@ -1193,11 +1278,11 @@ extern "C" int qx_set_pdl(int enable) {
   return QX_OK;
 }
 
-extern "C" int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const void* scales,
+static int w4a16_gemv_entry(const void* x, const int32_t* qweight, const void* scales,
                                   const void* zeros, int zeros_packed, int zero_offset,
                                   const void* lora_A, const void* lora_B, void* y, int M, int K,
                                   int N, int rank, int group_size, float lora_scale,
-                                  qx_stream_t stream) {
+                                  qx_stream_t stream, int act, int x_early) {
   QX_REQUIRE(M >= 0 && K > 0 && N > 0, "w4a16_gemv: bad sizes M=%d K=%d N=%d", M, K, N);
   if (M == 0) return QX_OK;
   QX_REQUIRE(K % gemv::KSTEP == 0, "w4a16_gemv: K=%d must be a multiple of 32", K);
@@ -1230,7 +1315,7 @@ extern "C" int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const v
     prm.zeros = zeros;
     prm.A = static_cast<const __half*>(lora_A);
     prm.B = static_cast<const __half*>(lora_B);
-    prm.y = static_cast<__half*>(y) + size_t(m0) * N;
+    prm.y = static_cast<__half*>(y) + size_t(m0) * (act ? N / 2 : N);
     prm.M = mc;
     prm.K = K;
     prm.N = N;
@@ -1240,6 +1325,8 @@ extern "C" int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const v
     prm.zero_offset = zero_offset;
     prm.lora_scale = rank > 0 ? lora_scale : 0.f;
     prm.pdl = g_pdl_enabled.load(std::memory_order_relaxed);
+    prm.act = act;
+    prm.x_early = x_early;
     const int rc = gemv::dispatch(prm, group_size / gemv::KSTEP, st);
     if (rc == QX_ERR_UNSUPPORTED && mc > 8) {
       mrows = mc > 16 ? 16 : 8;
@@ -1249,4 +1336,24 @@ extern "C" int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const v
     m0 += mc;
   }
   return QX_OK;
+}
+
+extern "C" int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const void* scales,
+                                  const void* zeros, int zeros_packed, int zero_offset,
+                                  const void* lora_A, const void* lora_B, void* y, int M, int K,
+                                  int N, int rank, int group_size, float lora_scale,
+                                  qx_stream_t stream) {
+  return w4a16_gemv_entry(x, qweight, scales, zeros, zeros_packed, zero_offset, lora_A, lora_B, y, M, K, N,
+                          rank, group_size, lora_scale, stream, 0, 0);
+}
+
+extern "C" int qx_w4a16_lora_gemv_swiglu(const void* x, const int32_t* qweight, const void* scales,
+                                         const void* zeros, int zeros_packed, int zero_offset,
+                                         const void* lora_A, const void* lora_B, void* y, int M, int K,
+                                         int N, int rank, int group_size, float lora_scale,
+                                         qx_stream_t stream) {
+  QX_REQUIRE(N > 0 && N % 16 == 0, "w4a16_gemv_swiglu: N=%d must be a multiple of 16 (gate|up blocks of 8)",
+             N);
+  return w4a16_gemv_entry(x, qweight, scales, zeros, zeros_packed, zero_offset, lora_A, lora_B, y, M, K, N,
+                          rank, group_size, lora_scale, stream, 1, 0);
 }

@@ -18,12 +18,13 @@ NCCL):
 The projections that read the same input are fused: q|k|v and gate|up are
 each one W4A16-LoRA call (weights side by side, LoRA A side by side, LoRA B
 block-diagonal, rank zero-padded to a supported size: the same math).  Per
-decode step and layer (9 launches): qkv GEMV -> per-head RMSNorm of q and k
+decode step and layer (8 launches): qkv GEMV -> per-head RMSNorm of q and k
 (Qwen3), RoPE (theta 1e6, keys stored post-RoPE at their absolute positions)
 and the ring append in one kernel -> GQA decode attention over sink + window
 (including the new token) -> o GEMV -> all-reduce + residual add + RMSNorm in
-one kernel -> gate|up GEMV -> SwiGLU -> down GEMV -> all-reduce + residual add
-+ the next RMSNorm in one kernel.  With more than one rank the all-reduce is a
+one kernel -> gate|up GEMV with the SwiGLU epilogue (gate and up columns
+interleaved in blocks of 8, so one CTA holds both halves of an output) -> down
+GEMV -> all-reduce + residual add + the next RMSNorm in one kernel.  With more than one rank the all-reduce is a
 one-shot exchange over NVLink peer memory inside that kernel
 (``nvlink_allreduce.py``); prefill chunks all-reduce with NCCL.  Prefill chunks
 run the same projections with the tensor-core GEMM; their attention (each
@@ -136,6 +137,26 @@ class FusedQuantLinear:
         return _C._w4a16(x, self.qweight, self.scales, self.qzeros, self.lora_A, self.lora_B,
                          self.group, self.lora_scale, 0)
 
+    def interleave_gate_up(self) -> "FusedQuantLinear":
+        """Reorders a fused [gate | up] pair into blocks of 8 gate and 8 up
+        columns (``_C.interleave_gate_up``) for ``swiglu``; ``__call__`` then
+        returns the reordered columns."""
+        inter = self.splits[0]
+        if len(self.splits) != 2 or self.splits[1] != inter:
+            raise ValueError("interleave_gate_up needs two parts of equal width")
+        il = _C.interleave_gate_up
+        self.qweight, self.scales = il(self.qweight, inter), il(self.scales, inter)
+        self.qzeros = il(self.qzeros, inter, packed=True)
+        self.lora_B = il(self.lora_B, inter)
+        self.interleaved = True
+        return self
+
+    def swiglu(self, x: torch.Tensor) -> torch.Tensor:
+        """silu(gate) * up of the interleaved gate|up pair: one launch for
+        decode rows (the GEMV's SwiGLU epilogue)"""
+        return _C._w4a16_swiglu(x, self.qweight, self.scales, self.qzeros, self.lora_A, self.lora_B,
+                                self.group, self.lora_scale, 0)
+
 
 def _padded_rank(r: int) -> int:
     """smallest LoRA rank the kernels take that holds r"""
@@ -180,7 +201,7 @@ class TPDecoder:
                 q_norm=normal((D,), base + 2), k_norm=normal((D,), base + 3),
                 qkv=FusedQuantLinear([q, k, v], _padded_rank(3 * cfg.lora_rank)),
                 o=ShardedQuantLinear(cfg.num_q_heads * D, H, cfg, base + 7, dev, r, w, "row"),
-                gate_up=FusedQuantLinear([gate, up], _padded_rank(2 * cfg.lora_rank)),
+                gate_up=FusedQuantLinear([gate, up], _padded_rank(2 * cfg.lora_rank)).interleave_gate_up(),
                 down=ShardedQuantLinear(cfg.intermediate, H, cfg, base + 10, dev, r, w, "row"),
             )
             del q, k, v, gate, up
@@ -235,7 +256,7 @@ class TPDecoder:
         return _C.fused_rmsnorm(t.contiguous(), w, self.cfg.rms_eps)
 
     def _mlp(self, L, h: torch.Tensor) -> torch.Tensor:
-        return self._allreduce(L["down"](_C.swiglu_packed(L["gate_up"](h))))
+        return self._allreduce(L["down"](L["gate_up"].swiglu(h)))
 
     # ------------------------------------------------------------------ decode
     def decode_step(self, tokens: torch.Tensor, return_hidden: bool = False):
@@ -254,9 +275,9 @@ class TPDecoder:
                                        cos, sin, self.cache.k[li], self.cache.v[li], cfg.sink,
                                        cfg.window, pos)
             att = _C.decode_attention(q, self.cache.k[li], self.cache.v[li], pos + 1, cfg.sink,
-                                      cfg.window)
+                                      cfg.window, after_append=True)
             h = self._reduce_add_norm(L["o"](att.view(B, self.hq * D)), x, L["post_norm"])  # x += o
-            dn = L["down"](_C.swiglu_packed(L["gate_up"](h)))
+            dn = L["down"](L["gate_up"].swiglu(h))
             nxt_w = self.layers[li + 1]["in_norm"] if li + 1 < n else self.final_norm
             h = self._reduce_add_norm(dn, x, nxt_w)  # x += down; the next RMSNorm
         self.cache.advance(1)

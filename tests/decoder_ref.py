@@ -33,6 +33,7 @@ class RefDecoder:
             for k in ("qkv", "o", "gate_up", "down"):
                 R[k] = _dense(L[k], self.dev)
             R["qkv_splits"], R["gate_up_splits"] = L["qkv"].splits, L["gate_up"].splits
+            R["gate_up_il"] = getattr(L["gate_up"], "interleaved", False)
             self.layers.append(R)
         self.cos, self.sin = dec.cos, dec.sin
         self.hq, self.hkv = dec.hq, dec.hkv
@@ -78,7 +79,11 @@ class RefDecoder:
             a = torch.einsum("bhl,blhd->bhd", sc.softmax(-1), V).reshape(B, self.hq * D)
             x = x + self._lin(a, L["o"])
             h = self._rms(x, L["post_norm"])
-            g, u = self._lin(h, L["gate_up"]).split(L["gate_up_splits"], dim=-1)
+            gu = self._lin(h, L["gate_up"])
+            if L["gate_up_il"]:  # blocks of 8 gate then 8 up columns
+                inter = L["gate_up_splits"][0]
+                gu = gu.view(B, inter // 8, 2, 8).transpose(1, 2).reshape(B, 2 * inter)
+            g, u = gu.split(L["gate_up_splits"], dim=-1)
             x = x + self._lin(g * torch.sigmoid(g) * u, L["down"])
         self.count += 1
         return x

@@ -90,3 +90,22 @@ def test_after_gemv_with_many_tiles(C):
     t = {k: dev_tensor(v) for k, v in d.items()}
     C.w4a16_lora_gemv(t["x"], t["qweight"], t["scales"], t["zeros"], t["lora_A"], t["lora_B"])
     _run(C, 32, 32, 8, 4, 4092, 4096 + 5, seed=77)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,count", [(1, 32, 8, 4096 + 7), (1, 4, 1, 4096), (1, 16, 4, 2000),
+                                            (2, 32, 8, 4096), (4, 32, 8, 3000), (1, 32, 8, 130),
+                                            (3, 8, 8, 1500)])
+def test_merge_modes_agree(C, B, Hq, Hkv, count):
+    """The cluster merge (default) and the workspace merge, each against the
+    oracle, and against each other within fp32-rounding distance."""
+    from qextract_infer_b200 import _lib
+    lib = _lib.load()
+    try:
+        _lib.check(lib.qx_decode_attention_pin_merge(1), "pin_merge")
+        a = _run(C, B, Hq, Hkv, 4, 4092, count, seed=count + B)
+        _lib.check(lib.qx_decode_attention_pin_merge(0), "pin_merge")
+        b = _run(C, B, Hq, Hkv, 4, 4092, count, seed=count + B)
+    finally:
+        lib.qx_decode_attention_pin_merge(0)
+    assert_close(a, b, 2e-3, 2e-3, "cluster vs workspace merge")
+    assert lib.qx_decode_attention_pin_merge(2) < 0

@@ -72,3 +72,37 @@ def test_qk_norm_rope_append(C, B, hq, hkv, D, pos):
     others = torch.ones(sink + window, dtype=torch.bool)
     others[slot] = False
     assert not kc[:, others].any() and not vc[:, others].any()
+
+
+@pytest.mark.parametrize("B,pos", [(1, 8191), (1, 100), (1, 2), (4, 4095), (32, 5000)])
+def test_attention_after_append_reads_the_appended_slot(C, B, pos):
+    """Decode attention launched early behind qk_norm_rope_append
+    (``after_append``: its first K/V tiles load while the append runs) equals
+    the attention launched after the append completed, bit for bit, and the
+    oracle; the appended slot held different (stale) values before."""
+    import numpy as np
+    from oracle import RingIndexOracle, gqa_decode_attention_ref
+    from tests._util import assert_close
+    hq, hkv, D, sink, window = 32, 8, 128, 4, 4092
+    g = _g(pos + B)
+    kc = torch.randn(B, sink + window, hkv, D, generator=g, device="cuda").half()
+    vc = torch.randn(B, sink + window, hkv, D, generator=g, device="cuda").half()
+    qkv = torch.randn(B, (hq + 2 * hkv) * D, generator=g, device="cuda").half()
+    qn = (1 + 0.1 * torch.randn(D, generator=g, device="cuda")).half()
+    kn = (1 + 0.1 * torch.randn(D, generator=g, device="cuda")).half()
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, device="cuda", dtype=torch.float32) / D))
+    ang = pos * inv
+    cos, sin = torch.cat([ang.cos(), ang.cos()]), torch.cat([ang.sin(), ang.sin()])
+    outs = []
+    for early in (True, False):
+        k2, v2 = kc.clone(), vc.clone()
+        torch.cuda.synchronize()
+        q = C.qk_norm_rope_append(qkv, hq, hkv, qn, kn, 1e-6, cos, sin, k2, v2, sink, window, pos)
+        outs.append(C.decode_attention(q, k2, v2, pos + 1, sink, window, after_append=early))
+        torch.cuda.synchronize()
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+    idx = RingIndexOracle(sink, window).indices(pos + 1)
+    qn_, kk, vv = q.cpu().numpy(), k2.cpu().numpy(), v2.cpu().numpy()
+    for b in range(B):
+        ref = gqa_decode_attention_ref(qn_[b], kk[b][idx], vv[b][idx], None)
+        assert_close(outs[0][b].cpu().numpy(), ref, 1e-2, 1e-2, f"b={b}")

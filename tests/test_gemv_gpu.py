@@ -259,9 +259,12 @@ def test_batch_rows_long_k_fall_back_to_fewer_rows(C):
     assert_close(to_np(y), ref, RTOL, ATOL, "M=32 K=12288")
 
 
-def test_host_buffer_entry_point_matches_device_path(C):
-    """qx_w4a16_lora_gemv_host (pinned host x in, pinned host y out, one C-ABI
-    call) returns exactly the device-path result, on two calls in a row."""
+@pytest.mark.parametrize("pinned", [True, False])
+def test_host_buffer_entry_point_matches_device_path(C, pinned):
+    """qx_w4a16_lora_gemv_host (host x in, host y out, one C-ABI call) returns
+    exactly the device-path result, on two calls in a row: pinned buffers (the
+    staging kernel and the GEMV's direct write into host memory) and pageable
+    ones (the copies)."""
     import ctypes
     from qextract_infer_b200 import _lib
     lib = _lib.load()
@@ -269,8 +272,10 @@ def test_host_buffer_entry_point_matches_device_path(C):
     t = _dev(d)
     ref = to_np(C.w4a16_lora_gemv(t["x"], t["qweight"], t["scales"], t["zeros"], t["lora_A"],
                                   t["lora_B"], 128, 32.0))
-    x_host = torch.from_numpy(d["x"]).pin_memory()
-    y_host = torch.zeros(3, 9728, dtype=torch.float16).pin_memory()
+    x_host = torch.from_numpy(d["x"].copy())
+    y_host = torch.zeros(3, 9728, dtype=torch.float16)
+    if pinned:
+        x_host, y_host = x_host.pin_memory(), y_host.pin_memory()
     x_dev = torch.empty(3, 2560, dtype=torch.float16, device="cuda")
     y_dev = torch.empty(3, 9728, dtype=torch.float16, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
@@ -284,3 +289,34 @@ def test_host_buffer_entry_point_matches_device_path(C):
         assert rc == 0, _lib.last_error()
         torch.cuda.synchronize()
         np.testing.assert_array_equal(y_host.numpy().view(np.uint16), ref.view(np.uint16))
+
+
+def test_host_buffer_calls_chained_through_host_memory(C):
+    """Two qx_w4a16_lora_gemv_host calls where the second one's x_host is the
+    first one's y_host (pinned), enqueued back to back: the second reads the
+    first one's output, not what the buffer held before."""
+    import ctypes
+    from qextract_infer_b200 import _lib
+    lib = _lib.load()
+    K = N = 1024
+    d1 = make_gemv_inputs(2, K, N, 16, seed=31)
+    d2 = make_gemv_inputs(2, K, N, 16, seed=32)
+    t1, t2 = _dev(d1), _dev(d2)
+    y1 = C.w4a16_lora_gemv(t1["x"], t1["qweight"], t1["scales"], t1["zeros"], t1["lora_A"],
+                           t1["lora_B"], 128, 32.0)
+    ref = to_np(C.w4a16_lora_gemv(y1, t2["qweight"], t2["scales"], t2["zeros"], t2["lora_A"],
+                                  t2["lora_B"], 128, 32.0))
+    x_host = torch.from_numpy(d1["x"].copy()).pin_memory()
+    mid = torch.zeros(2, N, dtype=torch.float16).pin_memory()
+    out = torch.zeros(2, N, dtype=torch.float16).pin_memory()
+    xd = torch.empty(2, K, dtype=torch.float16, device="cuda")
+    yd = torch.empty(2, N, dtype=torch.float16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    for xh, yh, t in ((x_host, mid, t1), (mid, out, t2)):
+        rc = lib.qx_w4a16_lora_gemv_host(
+            xh.data_ptr(), yh.data_ptr(), xd.data_ptr(), yd.data_ptr(), t["qweight"].data_ptr(),
+            t["scales"].data_ptr(), t["zeros"].data_ptr(), 1, 0, t["lora_A"].data_ptr(),
+            t["lora_B"].data_ptr(), 2, K, N, 16, 128, ctypes.c_float(2.0), st)
+        assert rc == 0, _lib.last_error()
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.numpy().view(np.uint16), ref.view(np.uint16))
