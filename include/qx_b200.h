@@ -294,6 +294,21 @@ int qx_decode_attention(const void* q, const void* k_cache, const void* v_cache,
                         int window, int64_t count, float softmax_scale, void* workspace,
                         size_t workspace_bytes, qx_stream_t stream);
 
+/* Prefill attention of one prompt chunk over the StreamingLLM ring, before the
+ * chunk is appended: q [batch, n, q_heads, 128] (the chunk's queries, at
+ * positions count .. count + n - 1), k_new / v_new [batch, n, kv_heads, 128]
+ * (the chunk's keys and values), k_cache / v_cache [batch, sink + window,
+ * kv_heads, 128] (the ring after `count` tokens: its valid slots are read in
+ * place, each at the position the ring's write rule gives it).  Key kp is
+ * visible to query p iff kp <= p and (kp < sink or kp > p - window).  out
+ * [batch, n, q_heads, 128] fp16; softmax_scale <= 0 means 1/sqrt(128).  Replaces
+ * the reference's gather (QExtractKVCache.get_kv, qextract/kv_cache.py:96-112)
+ * followed by an attention over the gathered copy. */
+int qx_prefill_attention(const void* q, const void* k_new, const void* v_new, const void* k_cache,
+                         const void* v_cache, void* out, int batch, int n, int q_heads,
+                         int kv_heads, int head_dim, int sink, int window, int64_t count,
+                         float softmax_scale, qx_stream_t stream);
+
 /* qx_decode_attention with flags.  QX_ATTN_AFTER_APPEND: the kernel just
  * before this call on `stream` wrote q and position count - 1 of every
  * sequence into the cache (a decode step's append) and nothing else this call

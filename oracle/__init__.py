@@ -34,4 +34,4 @@ from .gptq import (  # noqa: F401
 )
 from .norms import rmsnorm_ref, swiglu_ref, swiglu_ref_single_round  # noqa: F401
 from .ring import RingIndexOracle, RingCacheOracle  # noqa: F401
-from .attention import gqa_decode_attention_ref  # noqa: F401
+from .attention import gqa_decode_attention_ref, prefill_attention_ref, ring_positions  # noqa: F401

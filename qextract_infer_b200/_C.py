@@ -464,6 +464,34 @@ def decode_attention(q, k_cache, v_cache, count: int, sink: int, window: int,
     return out
 
 
+def prefill_attention(q, k_new, v_new, k_cache, v_cache, count: int, sink: int, window: int,
+                      softmax_scale: float | None = None):
+    """Attention of a prompt chunk before its append: ``q`` fp16 ``[B, n, Hq, D]``
+    at positions ``count ..``, ``k_new``/``v_new`` fp16 ``[B, n, Hkv, D]``, the
+    ring ``k_cache``/``v_cache`` ``[B, S+W, Hkv, D]`` after ``count`` tokens (read
+    in place).  Returns ``[B, n, Hq, D]``: causal, sinks + the last ``window``
+    positions visible (new component: the reference gathers the cache,
+    ``qextract/kv_cache.py:96-112``, and attends over the copy)."""
+    for t, nm in ((q, "q"), (k_new, "k_new"), (v_new, "v_new"), (k_cache, "k_cache"),
+                  (v_cache, "v_cache")):
+        _check_input(t, nm)
+        _check_fp16(t, nm)
+    B, n, Hq, D = q.shape
+    Hkv = k_new.size(2)
+    if tuple(k_new.shape) != (B, n, Hkv, D) or v_new.shape != k_new.shape:
+        raise RuntimeError("k_new / v_new must be [B, n, Hkv, D] like q")
+    if tuple(k_cache.shape) != (B, sink + window, Hkv, D) or v_cache.shape != k_cache.shape:
+        raise RuntimeError("cache must be [B, sink + window, Hkv, D]")
+    out = torch.empty_like(q)
+    st = _stream(q.device)
+    with torch.cuda.device(q.device):
+        _lib.check(_LIB.qx_prefill_attention(
+            q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+            out.data_ptr(), B, n, Hq, Hkv, D, sink, window, int(count), float(softmax_scale or 0.0),
+            st.cuda_stream), "prefill_attention")
+    return out
+
+
 class RingBufferKVCache:
     """StreamingLLM sink + ring-window KV cache (reference:
     ``csrc/include/ring_buffer.h:32-77``, ``csrc/kv_cache/ring_buffer.cu``).

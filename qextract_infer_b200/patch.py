@@ -9,6 +9,11 @@ Same entry point, flags and counters as the reference.  Fixes relative to it:
   "+1" storage convention;
 * projection inputs ``[B, T, K]`` keep their leading dims (the reference
   kernel returned a 1-D ``[N]``);
+* GPTQ act-order checkpoints (a ``g_idx`` that is not ``k // group_size``) are
+  accepted: the packed rows are re-ordered once so that every quantisation
+  group is contiguous (``act_order_repack``), the LoRA A rows alike, and each
+  call gathers the input columns in the same order (the reference kernel
+  assumes ``group = k // group_size``, ``w4a16_lora_gemv.cu:181``);
 * everything runs on the current CUDA stream.
 
 Optional extension: ``patch_plain_gptq=True`` also routes GPTQ layers that
@@ -100,7 +105,36 @@ def _patch_swiglu(mlp_module, fused_fn):
     mlp_module.forward = types.MethodType(new_forward, mlp_module)
 
 
+def act_order_repack(qweight: torch.Tensor, g_idx: torch.Tensor, group: int):
+    """GPTQ act-order: ``g_idx[k]`` is the quantisation group of input row k.
+    Returns ``(qweight', perm)`` with the packed rows re-ordered so that row j
+    of ``qweight'`` is input row ``perm[j]`` and belongs to group
+    ``j // group`` (``perm`` sorts the rows by group, stably), or ``None`` when
+    ``g_idx`` already is ``k // group``.  Raises if a group does not hold
+    exactly ``group`` rows.  Then ``x . W == x[..., perm] . W'`` with the
+    scales and zero points unchanged."""
+    K = qweight.size(0) * 8
+    g = g_idx.to(device=qweight.device, dtype=torch.int64).reshape(-1)
+    if g.numel() != K:
+        raise RuntimeError(f"g_idx has {g.numel()} entries, qweight {K} rows")
+    ar = torch.arange(K, device=qweight.device)
+    if torch.equal(g, ar // group):
+        return None
+    counts = torch.bincount(g, minlength=K // group)
+    if counts.numel() != K // group or not bool((counts == group).all()):
+        raise RuntimeError("act-order g_idx: every group must hold exactly group_size rows")
+    perm = torch.sort(g, stable=True).indices
+    shifts = torch.arange(0, 32, 4, device=qweight.device, dtype=torch.int64)
+    q = (qweight.to(torch.int64)[:, None, :] >> shifts[None, :, None]) & 0xF  # [K/8, 8, N]
+    q = q.reshape(K, -1).index_select(0, perm).reshape(K // 8, 8, -1)
+    packed = (q << shifts[None, :, None]).sum(1)
+    packed = torch.where(packed >= 2 ** 31, packed - 2 ** 32, packed).to(torch.int32)
+    return packed.contiguous(), perm
+
+
 def _gptq_tensors(layer):
+    """(qweight, scales, zeros, group, bias, perm): ``perm`` is the input-column
+    order of an act-order checkpoint (None otherwise)."""
     if not hasattr(layer, "qweight") or not hasattr(layer, "scales"):
         return None
     zeros = getattr(layer, "qzeros", getattr(layer, "zeros", None))
@@ -108,7 +142,13 @@ def _gptq_tensors(layer):
         return None
     group = int(getattr(layer, "group_size", 128))
     scales = layer.scales.half().contiguous()
-    return layer.qweight.contiguous(), scales, zeros.contiguous(), group, getattr(layer, "bias", None)
+    qweight, perm = layer.qweight.contiguous(), None
+    g_idx = getattr(layer, "g_idx", None)
+    if g_idx is not None:
+        r = act_order_repack(qweight, g_idx, group)
+        if r is not None:
+            qweight, perm = r
+    return qweight, scales, zeros.contiguous(), group, getattr(layer, "bias", None), perm
 
 
 def _patch_lora_gemv(proj_module, fused_fn, zero_offset: int) -> bool:
@@ -119,18 +159,22 @@ def _patch_lora_gemv(proj_module, fused_fn, zero_offset: int) -> bool:
     t = _gptq_tensors(base)
     if t is None:
         return False
-    qweight, scales, zeros, group, bias = t
+    qweight, scales, zeros, group, bias, perm = t
     lora_A = getattr(proj_module, "lora_A", None)
     if lora_A is None or "default" not in lora_A:
         return False
     # PEFT keeps nn.Linear weights: A [r, in] -> [in, r]; B [out, r] -> [r, out]
     A = proj_module.lora_A["default"].weight.detach().t().contiguous().half()
+    if perm is not None:
+        A = A.index_select(0, perm.to(A.device)).contiguous()
     B = proj_module.lora_B["default"].weight.detach().t().contiguous().half()
     alpha = getattr(proj_module, "lora_alpha", {}).get("default", 16.0)
 
     def new_forward(self, x):
         in_dtype = x.dtype
         xh = x.half() if in_dtype != torch.float16 else x
+        if perm is not None:
+            xh = xh.index_select(-1, perm)
         y = fused_fn(xh.contiguous(), qweight, scales, zeros, A, B, group, alpha,
                      zero_offset=zero_offset)
         if bias is not None:
@@ -145,11 +189,13 @@ def _patch_plain_gptq(proj_module, fused_fn, zero_offset: int) -> bool:
     t = _gptq_tensors(proj_module)
     if t is None:
         return False
-    qweight, scales, zeros, group, bias = t
+    qweight, scales, zeros, group, bias, perm = t
 
     def new_forward(self, x):
         in_dtype = x.dtype
         xh = x.half() if in_dtype != torch.float16 else x
+        if perm is not None:
+            xh = xh.index_select(-1, perm)
         y = fused_fn(xh.contiguous(), qweight, scales, zeros, group, zero_offset=zero_offset)
         if bias is not None:
             y = y + bias.to(y.dtype)

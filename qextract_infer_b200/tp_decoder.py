@@ -29,7 +29,7 @@ one-shot exchange over NVLink peer memory inside that kernel
 (``nvlink_allreduce.py``); prefill chunks all-reduce with NCCL.  Prefill chunks
 run the same projections with the tensor-core GEMM; their attention (each
 query over the sinks, the previous window and the causal part of its chunk)
-uses torch's scaled_dot_product_attention.
+is ``prefill_attention``, which reads the ring in place.
 
 Weights are synthetic: every full tensor comes from a generator seeded by
 (seed, layer, projection) on the device and each rank keeps its shard, so the
@@ -38,7 +38,6 @@ model is the same for every tensor-parallel size.
 
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 
 import numpy as np
@@ -306,13 +305,6 @@ class TPDecoder:
         return idx
 
     # ----------------------------------------------------------------- prefill
-    def _cache_positions(self, c: int) -> torch.Tensor:
-        """absolute positions of the cache's valid slots in logical order"""
-        S, W = self.cfg.sink, self.cfg.window
-        sinks = list(range(min(c, S)))
-        n_ring = min(max(c - S, 0), W)
-        return torch.tensor(sinks + list(range(c - n_ring, c)), device=self.device)
-
     def prefill(self, tokens: torch.Tensor, chunk: int = 2048, return_hidden: bool = False):
         """``tokens`` int64 [B, T] (device); returns the greedy next tokens [B]
         (and the last position's hidden state [B, H] if asked)."""
@@ -324,11 +316,6 @@ class TPDecoder:
             n = tc.size(1)
             c = self.cache.get_total_written()
             cos, sin = self.cos[c:c + n], self.sin[c:c + n]
-            qpos = torch.arange(c, c + n, device=self.device)
-            kpos = torch.cat([self._cache_positions(c), qpos])
-            # causal, and within the sinks or the last `window` positions
-            mask = (kpos[None, :] <= qpos[:, None]) & (
-                (kpos[None, :] < cfg.sink) | (kpos[None, :] > qpos[:, None] - cfg.window))
             x = self.embed.index_select(0, tc.reshape(-1)).view(B * n, cfg.hidden)
             for li, L in enumerate(self.layers):
                 h = _C.fused_rmsnorm(x, L["in_norm"], cfg.rms_eps)
@@ -338,20 +325,11 @@ class TPDecoder:
                 v = vp.reshape(B, n, self.hkv, D).contiguous()
                 q = self._rope(q.view(B, n, self.hq, D), cos, sin)
                 k = self._rope(k.view(B, n, self.hkv, D), cos, sin)
-                if c > 0:
-                    kc, vc = self.cache.get_kv(li)
-                    if B == 1:
-                        kc, vc = kc[None], vc[None]
-                    kk, vv = torch.cat([kc, k], dim=1), torch.cat([vc, v], dim=1)
-                else:
-                    kk, vv = k, v
-                rep = self.hq // self.hkv
-                att = torch.nn.functional.scaled_dot_product_attention(
-                    q.transpose(1, 2), kk.transpose(1, 2).repeat_interleave(rep, dim=1),
-                    vv.transpose(1, 2).repeat_interleave(rep, dim=1), attn_mask=mask,
-                    scale=1.0 / math.sqrt(D))  # [B, hq, n, D]
+                # the chunk over the ring (read in place) and its own keys, then the append
+                att = _C.prefill_attention(q, k.contiguous(), v, self.cache.k[li], self.cache.v[li], c,
+                                           cfg.sink, cfg.window)  # [B, n, hq, D]
                 self.cache.append(k, v, li)
-                att = att.transpose(1, 2).reshape(B * n, self.hq * D).contiguous()
+                att = att.reshape(B * n, self.hq * D)
                 x = x + self._allreduce(L["o"](att))
                 h = _C.fused_rmsnorm(x, L["post_norm"], cfg.rms_eps)
                 x = x + self._mlp(L, h)

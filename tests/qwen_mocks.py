@@ -15,24 +15,32 @@ import torch
 from torch import nn
 
 
-def dequant_torch(qweight, scales, qzeros, group):
+def dequant_torch(qweight, scales, qzeros, group, g_idx=None):
     K8, N = qweight.shape
     shifts = torch.arange(8, device=qweight.device, dtype=torch.int32) * 4
     q = (qweight.unsqueeze(1) >> shifts.view(1, 8, 1)) & 0xF  # [K/8, 8, N]
     q = q.reshape(K8 * 8, N).float()
     z = (qzeros.unsqueeze(2) >> shifts.view(1, 1, 8)) & 0xF  # [G, N/8, 8]
     z = z.reshape(qzeros.size(0), N).float()
-    g = torch.arange(K8 * 8, device=qweight.device) // group
+    g = torch.arange(K8 * 8, device=qweight.device) // group if g_idx is None else g_idx.long()
     return ((q - z[g]) * scales.float()[g]).half()
 
 
 class MockQuantLinear(nn.Module):
-    def __init__(self, K, N, group=128, seed=0):
+    """``act_order``: a GPTQ act-order layer, whose ``g_idx`` assigns the input
+    rows to the groups in a shuffled order (each group still holds ``group``
+    rows), with random zero points."""
+
+    def __init__(self, K, N, group=128, seed=0, act_order=False):
         super().__init__()
         rng = np.random.default_rng(seed)
         qw = rng.integers(0, 2 ** 32, size=(K // 8, N), dtype=np.uint64).astype(np.uint32).view(np.int32)
         sc = rng.uniform(0.005, 0.02, size=(K // group, N)).astype(np.float16)
         zn = np.full((K // group, N // 8), 0x88888888, dtype=np.uint32).view(np.int32)
+        if act_order:
+            zn = rng.integers(0, 2 ** 32, size=zn.shape, dtype=np.uint64).astype(np.uint32).view(np.int32)
+            self.register_buffer("g_idx", torch.from_numpy(
+                rng.permutation(np.arange(K) // group).astype(np.int32)))
         self.register_buffer("qweight", torch.from_numpy(qw))
         self.register_buffer("scales", torch.from_numpy(sc))
         self.register_buffer("qzeros", torch.from_numpy(zn))
@@ -41,14 +49,15 @@ class MockQuantLinear(nn.Module):
         self.bias = None
 
     def forward(self, x):
-        w = dequant_torch(self.qweight, self.scales, self.qzeros, self.group_size)
+        w = dequant_torch(self.qweight, self.scales, self.qzeros, self.group_size,
+                          getattr(self, "g_idx", None))
         return (x.float() @ w.float()).to(x.dtype)
 
 
 class MockLoraLinear(nn.Module):
-    def __init__(self, K, N, r=16, alpha=32.0, group=128, seed=0):
+    def __init__(self, K, N, r=16, alpha=32.0, group=128, seed=0, act_order=False):
         super().__init__()
-        self.base_layer = MockQuantLinear(K, N, group, seed)
+        self.base_layer = MockQuantLinear(K, N, group, seed, act_order)
         g = torch.Generator().manual_seed(seed + 1)
         a = nn.Linear(K, r, bias=False)
         b = nn.Linear(r, N, bias=False)
@@ -70,7 +79,7 @@ class MockLoraLinear(nn.Module):
 
 
 def make_tiny_qwen3(num_layers=2, hidden=256, inter=512, heads=4, kv_heads=2, head_dim=64,
-                    vocab=512, lora=True, seed=0):
+                    vocab=512, lora=True, seed=0, act_order=False):
     from transformers import Qwen3Config, Qwen3ForCausalLM
     cfg = Qwen3Config(vocab_size=vocab, hidden_size=hidden, intermediate_size=inter,
                       num_hidden_layers=num_layers, num_attention_heads=heads,
@@ -89,7 +98,8 @@ def make_tiny_qwen3(num_layers=2, hidden=256, inter=512, heads=4, kv_heads=2, he
         for name, (K, N) in shapes.items():
             parent = at if name in ("q_proj", "k_proj", "v_proj", "o_proj") else mlp
             s += 1
-            mod = MockLoraLinear(K, N, seed=s) if lora else MockQuantLinear(K, N, seed=s)
+            mod = (MockLoraLinear(K, N, seed=s, act_order=act_order) if lora
+                   else MockQuantLinear(K, N, seed=s, act_order=act_order))
             setattr(parent, name, mod)
         with torch.no_grad():
             layer.input_layernorm.weight.normal_(1.0, 0.1)

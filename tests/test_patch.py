@@ -42,11 +42,11 @@ def test_patched_forward_rejects_cpu_inputs():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("lora", [True, False])
-def test_patched_model_matches_unpatched(lora):
+@pytest.mark.parametrize("lora,act_order", [(True, False), (False, False), (True, True), (False, True)])
+def test_patched_model_matches_unpatched(lora, act_order):
     import qextract_infer_b200 as qx
     assert torch.cuda.is_available()
-    model = make_tiny_qwen3(num_layers=2, lora=lora).half().cuda().eval()
+    model = make_tiny_qwen3(num_layers=2, lora=lora, act_order=act_order).half().cuda().eval()
     ids = torch.randint(0, 512, (2, 9), generator=torch.Generator().manual_seed(0)).cuda()
     with torch.no_grad():
         ref = model(ids).logits.float()
@@ -58,3 +58,29 @@ def test_patched_model_matches_unpatched(lora):
     scale = ref.abs().max().item()
     err = (got - ref).abs().max().item()
     assert err <= 1e-2 * scale + 1e-2, (err, scale)
+
+
+def test_act_order_repack_cpu():
+    """act_order_repack: the re-ordered packed rows with the gathered input
+    columns give the same product as the act-order layer (oracle dequant with
+    g_idx); a g_idx of k // group is left alone; unequal groups are refused."""
+    import numpy as np
+    from qextract_infer_b200.patch import act_order_repack
+    from tests.qwen_mocks import dequant_torch
+    K, N, G = 512, 64, 128
+    rng = np.random.default_rng(3)
+    qw = torch.from_numpy(rng.integers(0, 2 ** 32, size=(K // 8, N), dtype=np.uint64)
+                          .astype(np.uint32).view(np.int32))
+    sc = torch.from_numpy(rng.uniform(0.005, 0.02, size=(K // G, N)).astype(np.float16))
+    qz = torch.from_numpy(rng.integers(0, 2 ** 32, size=(K // G, N // 8), dtype=np.uint64)
+                          .astype(np.uint32).view(np.int32))
+    g_idx = torch.from_numpy(rng.permutation(np.arange(K) // G).astype(np.int32))
+    x = torch.randn(3, K, generator=torch.Generator().manual_seed(1))
+    ref = x @ dequant_torch(qw, sc, qz, G, g_idx).float()
+    qw2, perm = act_order_repack(qw, g_idx, G)
+    got = x[:, perm] @ dequant_torch(qw2, sc, qz, G).float()
+    torch.testing.assert_close(got, ref, rtol=1e-5, atol=1e-4)
+    assert torch.equal(g_idx.long()[perm], torch.arange(K) // G)
+    assert act_order_repack(qw, torch.arange(K) // G, G) is None
+    with pytest.raises(RuntimeError, match="exactly group_size"):
+        act_order_repack(qw, torch.zeros(K, dtype=torch.int32), G)
