@@ -323,6 +323,22 @@ int qx_decode_attention_ex(const void* q, const void* k_cache, const void* v_cac
                            int window, int64_t count, float softmax_scale, void* workspace,
                            size_t workspace_bytes, int flags, qx_stream_t stream);
 
+/* One decode position in one kernel: the q/k head RMSNorm, RoPE and ring
+ * append of qx_qk_norm_rope_append followed by qx_decode_attention over the
+ * ring including the new token, bit-identical to that pair.  qkv: the fused
+ * projection output [batch, (q_heads + 2 kv_heads) * 128] fp16 (16-byte
+ * aligned); the new token's k and v go to the ring slot of position `pos`; out
+ * [batch, q_heads, 128].  Every CTA rotates the query heads of its KV head
+ * itself; the one whose slot chunk holds the new slot appends k and v.  When
+ * the grid is small it is launched early and loads its K/V tiles while the
+ * projection finishes.  Workspace as qx_decode_attention.  New component
+ * (the reference runs these as separate torch ops). */
+int qx_decode_attention_qkv(const void* qkv, const void* q_norm_w, const void* k_norm_w, float eps,
+                            const float* cos_row, const float* sin_row, void* k_cache, void* v_cache,
+                            void* out, int batch, int q_heads, int kv_heads, int head_dim, int sink,
+                            int window, int64_t pos, float softmax_scale, void* workspace,
+                            size_t workspace_bytes, qx_stream_t stream);
+
 /* How both decode-attention entry points merge the slot chunks of one
  * sequence and KV head (process-wide; results agree within fp32 rounding):
  * 0 (default) through distributed shared memory, the chunk CTAs forming one

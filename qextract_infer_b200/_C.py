@@ -464,6 +464,41 @@ def decode_attention(q, k_cache, v_cache, count: int, sink: int, window: int,
     return out
 
 
+def decode_attention_qkv(qkv: torch.Tensor, q_heads: int, kv_heads: int, q_norm: torch.Tensor,
+                         k_norm: torch.Tensor, eps: float, cos_row: torch.Tensor, sin_row: torch.Tensor,
+                         k_cache: torch.Tensor, v_cache: torch.Tensor, sink: int, window: int, pos: int,
+                         softmax_scale: float | None = None) -> torch.Tensor:
+    """``qk_norm_rope_append`` then ``decode_attention`` (count ``pos + 1``) in
+    one kernel: ``qkv`` fp16 ``[B, (q_heads + 2 kv_heads) * D]``; writes the new
+    token's k and v into ring slot ``pos``; returns ``[B, q_heads, D]``."""
+    for t, n in ((qkv, "qkv"), (q_norm, "q_norm"), (k_norm, "k_norm"), (k_cache, "k_cache"),
+                 (v_cache, "v_cache")):
+        _check_input(t, n)
+        _check_fp16(t, n)
+    D = q_norm.numel()
+    B = qkv.size(0)
+    if qkv.numel() != B * (q_heads + 2 * kv_heads) * D or k_norm.numel() != D:
+        raise RuntimeError("decode_attention_qkv: qkv must be [B, (q_heads + 2 kv_heads) * head_dim]")
+    if tuple(k_cache.shape) != (B, sink + window, kv_heads, D) or v_cache.shape != k_cache.shape:
+        raise RuntimeError("decode_attention_qkv: cache must be [B, sink + window, kv_heads, head_dim]")
+    for t, n in ((cos_row, "cos_row"), (sin_row, "sin_row")):
+        _check_input(t, n)
+        if t.dtype != torch.float32 or t.numel() != D:
+            raise RuntimeError(f"{n} must be float32 [{D}]")
+    out = torch.empty(B, q_heads, D, dtype=torch.float16, device=qkv.device)
+    dev = qkv.device
+    st = _stream(dev)
+    with torch.cuda.device(dev):
+        need = _LIB.qx_decode_attention_workspace_size(B, q_heads, kv_heads, D, sink, window)
+        ws = _workspace.get(dev, st, need, "decode_attention")
+        _lib.check(_LIB.qx_decode_attention_qkv(
+            qkv.data_ptr(), q_norm.data_ptr(), k_norm.data_ptr(), float(eps), cos_row.data_ptr(),
+            sin_row.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), B, q_heads,
+            kv_heads, D, int(sink), int(window), int(pos), float(softmax_scale or 0.0), ws.data_ptr(),
+            ws.numel(), st.cuda_stream), "decode_attention_qkv")
+    return out
+
+
 def prefill_attention(q, k_new, v_new, k_cache, v_cache, count: int, sink: int, window: int,
                       softmax_scale: float | None = None):
     """Attention of a prompt chunk before its append: ``q`` fp16 ``[B, n, Hq, D]``

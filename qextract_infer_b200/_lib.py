@@ -72,6 +72,9 @@ SIGNATURES = {
     "qx_prefill_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                      c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int64,
                                      c_float, c_void_p]),
+    "qx_decode_attention_qkv": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
+                                        c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                                        c_int, c_int64, c_float, c_void_p, c_size_t, c_void_p]),
     "qx_decode_attention_pin_merge": (c_int, [c_int]),
     "qx_decode_attention_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                             c_int, c_int, c_int, c_int, c_int64, c_float,

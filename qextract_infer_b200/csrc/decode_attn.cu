@@ -55,6 +55,8 @@ constexpr int COUNTER_SLOTS = 4096;              // fixed counter region at the 
 constexpr int MAX_CHUNKS = 64;                   // bounds the merge's shared memory
 constexpr int MAX_CLUSTER = 16;                  // chunks merged through distributed shared memory
 constexpr int CPART_OFF = WARPS * 16 * D * 4 + 2 * WARPS * 16 * 4;  // cluster merge: [G][PSTRIDE]
+constexpr int QS_BYTES = 16 * D * 2;             // fused form: the G <= 16 rotated query heads
+constexpr int SMEM_FUSED = SMEM + QS_BYTES;
 static_assert(THREADS == D, "one thread per head dimension in the merges");
 static_assert(WARPS == 4, "the chunk merge interleaves 4 chunk subsets, one per warp");
 static_assert(2 * 16 * MAX_CHUNKS * 4 + 32 * 4 + 4 * 16 * D * 4 <= SMEM, "merge fits the tile smem");
@@ -70,9 +72,18 @@ struct Params {
   float* part;          // [B*Hkv][nch][G][PSTRIDE], O 16-byte aligned
   unsigned* counters;   // [B*Hkv]
   int early;            // launched early: the K/V tiles of the first two rounds load before the
-                        // dependency wait, and slot `fresh` (the one the previous kernel wrote)
-                        // is reloaded after it
+                        // dependency wait, and slot `fresh` (the one the previous kernel wrote,
+                        // or this kernel's own append) is reloaded after it
   int fresh;
+  // fused q/k head norm + RoPE + ring append (qkv: the fused projection
+  // output [B][(Hq + 2 Hkv) D]; k / v of the new token go to slot `fresh`)
+  int fused;
+  const __half* qkv;
+  const __half* qnw;
+  const __half* knw;
+  const float* cosr;
+  const float* sinr;
+  float eps;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -171,10 +182,32 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
   else cp_async_commit();
   if (p.early) pdl_wait();  // q (and slot `fresh`) come from the previous kernel
 
+  const __half* qsrc = p.q + (size_t(b) * p.Hq + size_t(kvh) * p.G) * D;
+  if (p.fused) {
+    // the G query heads of this KV head: head norm + RoPE into shared memory;
+    // the CTA whose chunk holds the new token's slot appends its k and v
+    __half* qs = reinterpret_cast<__half*>(smem + SMEM);
+    const int heads = p.Hq + 2 * p.Hkv;
+    const __half* row = p.qkv + size_t(b) * heads * D;
+    for (int i = warp; i < p.G; i += WARPS)
+      head_norm_rope<4>(row + size_t(kvh * p.G + i) * D, p.qnw, p.eps, p.cosr, p.sinr, qs + i * D, lane);
+    if (p.fresh >= c0 && p.fresh < c1) {
+      const size_t dst = ((size_t(b) * p.cap + p.fresh) * p.Hkv + kvh) * D;
+      if (warp == 0) {
+        head_norm_rope<4>(row + size_t(p.Hq + kvh) * D, p.knw, p.eps, p.cosr, p.sinr,
+                          const_cast<__half*>(p.k) + dst, lane);
+      } else if (warp == 1) {
+        const uint2 v = reinterpret_cast<const uint2*>(row + size_t(p.Hq + p.Hkv + kvh) * D)[lane];
+        reinterpret_cast<uint2*>(const_cast<__half*>(p.v) + dst)[lane] = v;
+      }
+    }
+    __syncthreads();  // rotated q in shared memory; the appended slot visible to this CTA
+    qsrc = qs;
+  }
   // Q fragments (rows = query heads of this KV head, k = head dim)
   uint32_t qa[8][4];
   {
-    const __half* qb = p.q + (size_t(b) * p.Hq + size_t(kvh) * p.G) * D;
+    const __half* qb = qsrc;
     const bool r0 = g < p.G, r1 = g + 8 < p.G;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
@@ -192,7 +225,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
     __syncwarp();
     const uint32_t ks = wsm_u + (it & 1) * 2 * TILE_BYTES;
     const uint32_t vs = ks + TILE_BYTES;
-    if (p.early && it < 2) {
+    if ((p.early || p.fused) && it < 2) {
       // the tiles of the first two rounds were requested before the previous
       // kernel finished: reload the slot it wrote
       const int r = p.fresh - (c0 + t * TILE);
@@ -511,10 +544,10 @@ static int prepare_kernel(const int** fit_out) {
   std::lock_guard<std::mutex> lk(mu);
   if (!done[dev]) {
     QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<false>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM),
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_FUSED),
                 "decode_attention: set smem limit");
     QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<true>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM),
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_FUSED),
                 "decode_attention: set smem limit");
     QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<true>,
                                      cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
@@ -552,14 +585,15 @@ static int prepare_kernel(const int** fit_out) {
 static int launch(const Plan& pl, const Params& prm, int batch, int kv_heads, cudaStream_t st,
                   const char* what) {
   const dim3 grid(pl.nch, batch * kv_heads), block(THREADS);
+  const int smem = prm.fused ? SMEM_FUSED : SMEM;
   if (!pl.cluster && !prm.early) {
-    decode_attn_kernel<false><<<grid, block, SMEM, st>>>(prm);
+    decode_attn_kernel<false><<<grid, block, smem, st>>>(prm);
     return check_launch(what);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
-  cfg.dynamicSmemBytes = SMEM;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute at[2];
   int na = 0;
@@ -668,6 +702,72 @@ extern "C" int qx_decode_attention(const void* q, const void* k_cache, const voi
                                    void* workspace, size_t workspace_bytes, qx_stream_t stream) {
   return qx_decode_attention_ex(q, k_cache, v_cache, out, batch, q_heads, kv_heads, head_dim, sink, window,
                                 count, softmax_scale, workspace, workspace_bytes, 0, stream);
+}
+
+extern "C" int qx_decode_attention_qkv(const void* qkv, const void* q_norm_w, const void* k_norm_w,
+                                       float eps, const float* cos_row, const float* sin_row,
+                                       void* k_cache, void* v_cache, void* out, int batch, int q_heads,
+                                       int kv_heads, int head_dim, int sink, int window, int64_t pos,
+                                       float softmax_scale, void* workspace, size_t workspace_bytes,
+                                       qx_stream_t stream) {
+  QX_REQUIRE(batch > 0 && q_heads > 0 && kv_heads > 0 && q_heads % kv_heads == 0,
+             "decode_attention_qkv: bad heads q=%d kv=%d", q_heads, kv_heads);
+  QX_REQUIRE(head_dim == attn::D, "decode_attention_qkv: head_dim=%d unsupported (128)", head_dim);
+  QX_REQUIRE(q_heads / kv_heads <= 16, "decode_attention_qkv: GQA group %d > 16", q_heads / kv_heads);
+  QX_REQUIRE(sink >= 0 && window >= 1 && pos >= 0, "decode_attention_qkv: sink=%d window=%d pos=%lld",
+             sink, window, (long long)pos);
+  QX_REQUIRE(batch * kv_heads <= attn::COUNTER_SLOTS, "decode_attention_qkv: batch*kv_heads > %d",
+             attn::COUNTER_SLOTS);
+  QX_REQUIRE(qkv && q_norm_w && k_norm_w && cos_row && sin_row && k_cache && v_cache && out,
+             "decode_attention_qkv: null pointer");
+  QX_REQUIRE(aligned(qkv, 16) && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(out, 2),
+             "decode_attention_qkv: misaligned tensors");
+  const int cap = sink + window;
+  const int64_t count = pos + 1;
+  const int64_t valid64 = count <= sink ? count : sink + std::min<int64_t>(count - sink, window);
+  const int G = q_heads / kv_heads;
+  const int* fit = nullptr;
+  {
+    const int rc = attn::prepare_kernel(&fit);
+    if (rc != QX_OK) return rc;
+  }
+  const attn::Plan pl = attn::make_plan(batch, kv_heads, G, cap, int(valid64), device_sm_count(), fit);
+  if (!workspace || workspace_bytes < pl.total || !aligned(workspace, 256))
+    return fail(QX_ERR_WORKSPACE, "decode_attention_qkv: workspace needs %zu bytes, 256-byte aligned",
+                pl.total);
+  attn::Params prm{};
+  prm.q = static_cast<const __half*>(qkv);  // unused: the rotated q is built in shared memory
+  prm.k = static_cast<const __half*>(k_cache);
+  prm.v = static_cast<const __half*>(v_cache);
+  prm.out = static_cast<__half*>(out);
+  prm.Hq = q_heads;
+  prm.Hkv = kv_heads;
+  prm.G = G;
+  prm.cap = cap;
+  prm.valid = int(valid64);
+  prm.chunk = pl.chunk;
+  prm.nch = pl.nch;
+  const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf(float(head_dim));
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  prm.counters = reinterpret_cast<unsigned*>(ws);
+  prm.part = reinterpret_cast<float*>(ws + pl.off_part);
+  prm.fresh = int(pos < sink ? pos : sink + (pos - sink) % window);  // the new token's slot
+  prm.fused = 1;
+  prm.qkv = static_cast<const __half*>(qkv);
+  prm.qnw = static_cast<const __half*>(q_norm_w);
+  prm.knw = static_cast<const __half*>(k_norm_w);
+  prm.cosr = cos_row;
+  prm.sinr = sin_row;
+  prm.eps = eps;
+  // the previous kernel (the projection) writes no cache slot: with a small
+  // grid every tile may load while it finishes
+  prm.early = g_pdl_enabled.load(std::memory_order_relaxed) &&
+                      long(pl.nch) * batch * kv_heads <= 2L * device_sm_count()
+                  ? 1
+                  : 0;
+  return attn::launch(pl, prm, batch, kv_heads, reinterpret_cast<cudaStream_t>(stream),
+                      "decode_attention_qkv");
 }
 
 extern "C" int qx_decode_attention_pin_merge(int mode) {

@@ -104,9 +104,6 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(
   if (item >= batch * heads) return;
   const int b = item / heads, h = item - b * heads;
   const __half* src = qkv + (size_t(b) * heads + h) * D + lane * EPL;
-  float v[EPL];
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) v[e] = __half2float(src[e]);
   if (h >= hq + hkv) {  // v head: copy to the ring slot
     __half* dst = v_cache + ((size_t(b) * cap + slot) * hkv + (h - hq - hkv)) * D + lane * EPL;
 #pragma unroll
@@ -114,28 +111,9 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(
     return;
   }
   const bool is_q = h < hq;
-  const __half* nw = (is_q ? qw : kw) + lane * EPL;
-  float ss = 0.f;
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) ss = fmaf(v[e], v[e], ss);
-  ss = warp_sum(ss);
-  const float r = 1.0f / sqrtf(ss * (1.0f / D) + eps);
-#pragma unroll
-  for (int e = 0; e < EPL; ++e)  // the head norm's fp16 output
-    v[e] = __half2float(__float2half_rn((v[e] * r) * __half2float(nw[e])));
-  float o[EPL];
-  const bool lo = lane < 16;  // first half of the head
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) {
-    const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
-    const float rot = lo ? -partner : partner;
-    const int i = lane * EPL + e;
-    o[e] = __fadd_rn(__fmul_rn(v[e], cosr[i]), __fmul_rn(rot, sinr[i]));
-  }
-  __half* dst = is_q ? q_out + (size_t(b) * hq + h) * D + lane * EPL
-                     : k_cache + ((size_t(b) * cap + slot) * hkv + (h - hq)) * D + lane * EPL;
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) dst[e] = __float2half_rn(o[e]);
+  __half* dst = is_q ? q_out + (size_t(b) * hq + h) * D
+                     : k_cache + ((size_t(b) * cap + slot) * hkv + (h - hq)) * D;
+  head_norm_rope<EPL>(qkv + (size_t(b) * heads + h) * D, is_q ? qw : kw, eps, cosr, sinr, dst, lane);
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) {

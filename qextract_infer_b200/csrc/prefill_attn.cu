@@ -77,7 +77,7 @@ __device__ __forceinline__ uint32_t swz(int r, int ch) {
   return uint32_t(r * ROW_BYTES + ((ch ^ (r & 7)) << 4));
 }
 
-__global__ void __launch_bounds__(THREADS) prefill_attn_kernel(const Params p) {
+__global__ void __launch_bounds__(THREADS, 3) prefill_attn_kernel(const Params p) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;

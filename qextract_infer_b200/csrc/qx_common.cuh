@@ -148,4 +148,35 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// One warp, one attention head of 32 * EPL elements (lane holds elements
+// lane*EPL .. lane*EPL + EPL - 1): Qwen3's per-head RMSNorm (fp16 result, as
+// the HF module stores it) followed by rotate-half RoPE with the products and
+// the sum rounded as torch does them in fp32; writes the fp16 head to dst.
+// The rotate-half partner of element i (i +- D/2) sits 16 lanes away.
+template <int EPL>
+__device__ __forceinline__ void head_norm_rope(const __half* __restrict__ src, const __half* __restrict__ nw,
+                                               float eps, const float* __restrict__ cosr,
+                                               const float* __restrict__ sinr, __half* dst, int lane) {
+  constexpr int D = EPL * 32;
+  float v[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) v[e] = __half2float(src[lane * EPL + e]);
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) ss = fmaf(v[e], v[e], ss);
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss * (1.0f / D) + eps);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e)  // the head norm's fp16 output
+    v[e] = __half2float(__float2half_rn((v[e] * r) * __half2float(nw[lane * EPL + e])));
+  const bool lo = lane < 16;  // first half of the head
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
+    const float rot = lo ? -partner : partner;
+    const int i = lane * EPL + e;
+    dst[i] = __float2half_rn(__fadd_rn(__fmul_rn(v[e], cosr[i]), __fmul_rn(rot, sinr[i])));
+  }
+}
+
 }  // namespace qx

@@ -18,10 +18,10 @@ NCCL):
 The projections that read the same input are fused: q|k|v and gate|up are
 each one W4A16-LoRA call (weights side by side, LoRA A side by side, LoRA B
 block-diagonal, rank zero-padded to a supported size: the same math).  Per
-decode step and layer (8 launches): qkv GEMV -> per-head RMSNorm of q and k
-(Qwen3), RoPE (theta 1e6, keys stored post-RoPE at their absolute positions)
-and the ring append in one kernel -> GQA decode attention over sink + window
-(including the new token) -> o GEMV -> all-reduce + residual add + RMSNorm in
+decode step and layer (7 launches): qkv GEMV -> per-head RMSNorm of q and k
+(Qwen3), RoPE (theta 1e6, keys stored post-RoPE at their absolute positions),
+the ring append and the GQA decode attention over sink + window (including the
+new token) in one kernel -> o GEMV -> all-reduce + residual add + RMSNorm in
 one kernel -> gate|up GEMV with the SwiGLU epilogue (gate and up columns
 interleaved in blocks of 8, so one CTA holds both halves of an output) -> down
 GEMV -> all-reduce + residual add + the next RMSNorm in one kernel.  With more than one rank the all-reduce is a
@@ -270,11 +270,9 @@ class TPDecoder:
         h = _C.fused_rmsnorm(x, self.layers[0]["in_norm"], eps)
         n = len(self.layers)
         for li, L in enumerate(self.layers):
-            q = _C.qk_norm_rope_append(L["qkv"](h), self.hq, self.hkv, L["q_norm"], L["k_norm"], eps,
-                                       cos, sin, self.cache.k[li], self.cache.v[li], cfg.sink,
-                                       cfg.window, pos)
-            att = _C.decode_attention(q, self.cache.k[li], self.cache.v[li], pos + 1, cfg.sink,
-                                      cfg.window, after_append=True)
+            att = _C.decode_attention_qkv(L["qkv"](h), self.hq, self.hkv, L["q_norm"], L["k_norm"], eps,
+                                          cos, sin, self.cache.k[li], self.cache.v[li], cfg.sink,
+                                          cfg.window, pos)
             h = self._reduce_add_norm(L["o"](att.view(B, self.hq * D)), x, L["post_norm"])  # x += o
             dn = L["down"](L["gate_up"].swiglu(h))
             nxt_w = self.layers[li + 1]["in_norm"] if li + 1 < n else self.final_norm

@@ -106,3 +106,31 @@ def test_attention_after_append_reads_the_appended_slot(C, B, pos):
     for b in range(B):
         ref = gqa_decode_attention_ref(qn_[b], kk[b][idx], vv[b][idx], None)
         assert_close(outs[0][b].cpu().numpy(), ref, 1e-2, 1e-2, f"b={b}")
+
+
+@pytest.mark.parametrize("B,hq,hkv,pos", [(1, 32, 8, 8191), (1, 32, 8, 100), (1, 32, 8, 2), (4, 32, 8, 4095),
+                                          (32, 32, 8, 5000), (2, 16, 2, 4096), (1, 8, 8, 3)])
+def test_attention_qkv_equals_append_then_attention(C, B, hq, hkv, pos):
+    """decode_attention_qkv (head norm + RoPE + ring append + attention in one
+    kernel) against qk_norm_rope_append followed by decode_attention: the
+    output and the appended ring slot bit for bit, the other slots untouched."""
+    D, sink, window = 128, 4, 4092
+    g = _g(pos * 7 + B)
+    kc = torch.randn(B, sink + window, hkv, D, generator=g, device="cuda").half()
+    vc = torch.randn(B, sink + window, hkv, D, generator=g, device="cuda").half()
+    qkv = torch.randn(B, (hq + 2 * hkv) * D, generator=g, device="cuda").half()
+    qn = (1 + 0.1 * torch.randn(D, generator=g, device="cuda")).half()
+    kn = (1 + 0.1 * torch.randn(D, generator=g, device="cuda")).half()
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, device="cuda", dtype=torch.float32) / D))
+    ang = pos * inv
+    cos, sin = torch.cat([ang.cos(), ang.cos()]), torch.cat([ang.sin(), ang.sin()])
+    k1, v1 = kc.clone(), vc.clone()
+    q = C.qk_norm_rope_append(qkv, hq, hkv, qn, kn, 1e-6, cos, sin, k1, v1, sink, window, pos)
+    ref = C.decode_attention(q, k1, v1, pos + 1, sink, window)
+    k2, v2 = kc.clone(), vc.clone()
+    for _ in range(2):  # twice: the second call rewrites the same slot with the same values
+        out = C.decode_attention_qkv(qkv, hq, hkv, qn, kn, 1e-6, cos, sin, k2, v2, sink, window, pos)
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+        assert torch.equal(k2.view(torch.int16), k1.view(torch.int16))
+        assert torch.equal(v2.view(torch.int16), v1.view(torch.int16))
