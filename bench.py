@@ -477,6 +477,35 @@ def run_kernel_suite(args):
         us = _graph_time_us(torch, st, lambda i: c2.decode_attention(q, i % nl), min(steps, 4 * nl))
         emit("decode_attention", {"batch": B, "q_heads": 32, "kv_heads": Hkv, "head_dim": D,
                                   "valid_slots": S + W}, nb, us, {"per": "layer"})
+        # the decode step's form: q/k head norm + RoPE + ring append + attention in one kernel,
+        # straight from the q|k|v projection output
+        qkv = torch.randn(B, (32 + 2 * Hkv) * D, generator=gen, device=dev).half()
+        qn = (1 + 0.1 * torch.randn(D, generator=gen, device=dev)).half()
+        cs, sn = torch.rand(D, generator=gen, device=dev), torch.rand(D, generator=gen, device=dev)
+        us = _graph_time_us(torch, st, lambda i: _C.decode_attention_qkv(
+            qkv, 32, Hkv, qn, qn, 1e-6, cs, sn, c2.k_cache[i % nl], c2.v_cache[i % nl], S, W, 32768 + 64),
+            min(steps, 4 * nl))
+        emit("decode_attention_qkv", {"batch": B, "q_heads": 32, "kv_heads": Hkv, "head_dim": D,
+                                      "valid_slots": S + W}, nb + B * (32 + 2 * Hkv) * D * 2, us,
+             {"per": "layer", "fused": "q/k head norm + RoPE + ring append + attention"})
+        del c2
+    # prefill attention: a 2048-token chunk at position 6144 (4096 ring slots + the chunk)
+    for B in (1, 32):
+        n = 2048
+        pq = torch.randn(B, n, 32, D, generator=gen, device=dev).half()
+        pk = torch.randn(B, n, Hkv, D, generator=gen, device=dev).half()
+        pv = torch.randn(B, n, Hkv, D, generator=gen, device=dev).half()
+        kc = torch.randn(B, S + W, Hkv, D, generator=gen, device=dev).half()
+        vc = torch.randn(B, S + W, Hkv, D, generator=gen, device=dev).half()
+        us = _graph_time_us(torch, st, lambda i: _C.prefill_attention(pq, pk, pv, kc, vc, 6144, S, W),
+                            10 if B > 1 else 40)
+        flops = 4.0 * B * 32 * D * n * ((S + W) + n / 2)
+        print(json.dumps({"metric": "prefill_attention us & TFLOP/s", "kernel": "prefill_attention",
+                          "shape": {"batch": B, "chunk": n, "q_heads": 32, "kv_heads": Hkv,
+                                    "ring_slots": S + W, "position": 6144},
+                          "us_per_call": us, "TFLOP/s": flops / us / 1e6, "bound": "mma.sync"}),
+              flush=True)
+        del pq, pk, pv, kc, vc
     return 0
 
 
@@ -702,7 +731,10 @@ def run_profile_cases(args):
     profiles/ were captured from.  Sizes: RMSNorm 4096 x 4096, SwiGLU
     4096 x 12288, ring append of a 2048-token chunk (8 KV heads x 128), decode
     attention B=32 over a full 4 + 4092 ring, the decode-step kernels at B=32
-    (Qwen3-8B, TP 1), the prefill GEMM on the q shape (M=4096, K=N=4096, r=64).
+    (Qwen3-8B, TP 1), the prefill GEMM on the q shape (M=4096, K=N=4096, r=64),
+    prefill attention of a 2048-token chunk at position 6144, the gate|up GEMV
+    with the SwiGLU epilogue (one row) and the fused q/k norm + RoPE + append +
+    attention (one sequence).
     Prints one line per pass; no timing."""
     import torch
     import qextract_infer_b200 as qx
@@ -710,6 +742,7 @@ def run_profile_cases(args):
     dev = torch.device("cuda", torch.cuda.current_device())
     gen = torch.Generator(device=dev).manual_seed(5)
     H, I, D, Hkv, Hq, S, W, B = 4096, 12288, 128, 8, 32, 4, 4092, 32
+    G = 128
     x = torch.randn(4096, H, generator=gen, device=dev).half()
     w = (torch.randn(H, generator=gen, device=dev) * 0.1 + 1).half()
     g = torch.randn(4096, I, generator=gen, device=dev).half()
@@ -732,13 +765,32 @@ def run_profile_cases(args):
     vc = torch.zeros_like(kc)
     gu = torch.randn(B, 2 * I, generator=gen, device=dev).half()
     K = N = 4096
-    R, G = 64, 128
+    R = 64
     qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), generator=gen, device=dev, dtype=torch.int32)
     sc = (torch.rand(K // G, N, generator=gen, device=dev) * 0.015 + 0.005).half()
     qz = torch.full((K // G, N // 8), 0x88888888 - 2 ** 32, dtype=torch.int32, device=dev)
     A = (torch.randn(K, R, generator=gen, device=dev) * 0.02).half()
     Bl = (torch.randn(R, N, generator=gen, device=dev) * 0.02).half()
+    # prefill attention: a 2048-token chunk at position 6144 (the ring wraps), one sequence
+    pq = torch.randn(1, 2048, Hq, D, generator=gen, device=dev).half()
+    pk = torch.randn(1, 2048, Hkv, D, generator=gen, device=dev).half()
+    pv = torch.randn(1, 2048, Hkv, D, generator=gen, device=dev).half()
+    pkc = torch.randn(1, S + W, Hkv, D, generator=gen, device=dev).half()
+    pvc = torch.randn(1, S + W, Hkv, D, generator=gen, device=dev).half()
+    # gate|up with the SwiGLU epilogue, one row (Qwen3-8B: K 4096, 2 x 12288 columns, r 32)
+    gq = torch.randint(-2 ** 31, 2 ** 31 - 1, (H // 8, 2 * I), generator=gen, device=dev, dtype=torch.int32)
+    gs = (torch.rand(H // G, 2 * I, generator=gen, device=dev) * 0.015 + 0.005).half()
+    gz = torch.full((H // G, 2 * I // 8), 0x88888888 - 2 ** 32, dtype=torch.int32, device=dev)
+    gA = (torch.randn(H, 32, generator=gen, device=dev) * 0.02).half()
+    gB = (torch.randn(32, 2 * I, generator=gen, device=dev) * 0.02).half()
+    x1 = torch.randn(1, H, generator=gen, device=dev).half()
+    qkv1 = torch.randn(1, (Hq + 2 * Hkv) * D, generator=gen, device=dev).half()
+    kc1 = torch.randn(1, S + W, Hkv, D, generator=gen, device=dev).half()
+    vc1 = torch.randn(1, S + W, Hkv, D, generator=gen, device=dev).half()
     for rep in range(2):
+        _C.prefill_attention(pq, pk, pv, pkc, pvc, 6144, S, W)
+        _C.w4a16_lora_gemv_swiglu(x1, gq, gs, gz, gA, gB, G, 64.0)
+        _C.decode_attention_qkv(qkv1, Hq, Hkv, qn, qn, 1e-6, cos, sin, kc1, vc1, S, W, 8191)
         _C.fused_rmsnorm(x, w, 1e-6)
         _C.fused_swiglu(g, u)
         cache.append(kn, vn, 0)

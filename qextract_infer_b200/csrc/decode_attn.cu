@@ -57,6 +57,12 @@ constexpr int MAX_CLUSTER = 16;                  // chunks merged through distri
 constexpr int CPART_OFF = WARPS * 16 * D * 4 + 2 * WARPS * 16 * 4;  // cluster merge: [G][PSTRIDE]
 constexpr int QS_BYTES = 16 * D * 2;             // fused form: the G <= 16 rotated query heads
 constexpr int SMEM_FUSED = SMEM + QS_BYTES;
+// deep form: 4 tile stages per warp (every tile of a 256-slot chunk in flight at
+// once), for grids of at most one CTA per SM
+constexpr int SMEM4 = 2 * SMEM;
+__host__ __device__ constexpr int smem_bytes(int nb, bool fused) {
+  return (nb == 4 ? SMEM4 : SMEM) + (fused ? QS_BYTES : 0);
+}
 static_assert(THREADS == D, "one thread per head dimension in the merges");
 static_assert(WARPS == 4, "the chunk merge interleaves 4 chunk subsets, one per warp");
 static_assert(2 * 16 * MAX_CHUNKS * 4 + 32 * 4 + 4 * 16 * D * 4 <= SMEM, "merge fits the tile smem");
@@ -134,7 +140,8 @@ __device__ __forceinline__ void cluster_sync() {
 // CLUSTER: the grid's x extent (the chunks of one sequence and KV head) is one
 // thread-block cluster and the chunks are merged through distributed shared
 // memory; otherwise through the workspace by the last CTA.
-template <bool CLUSTER>
+// NB: K/V tile stages per warp (2, or 4 for grids of at most one CTA per SM)
+template <bool CLUSTER, int NB>
 __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
   pdl_trigger();
   if (!p.early) pdl_wait();  // no-op unless launched with programmatic dependent launch
@@ -151,7 +158,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
   const size_t slot_stride = size_t(p.Hkv) * D;  // halves between consecutive slots
   const __half* kb = p.k + (size_t(b) * p.cap * p.Hkv + kvh) * D;
   const __half* vb = p.v + (size_t(b) * p.cap * p.Hkv + kvh) * D;
-  unsigned char* wsm = smem + warp * WARP_SMEM;
+  unsigned char* wsm = smem + warp * (NB * 2 * TILE_BYTES);
   const uint32_t wsm_u = smem_u32(wsm);
 
   auto issue_tile = [&](int t, int stage) {
@@ -175,18 +182,19 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
   for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
 
-  // two tiles in flight per warp (an empty commit group where no tile is left)
-  if (warp < ntiles) issue_tile(warp, 0);
-  else cp_async_commit();
-  if (warp + WARPS < ntiles) issue_tile(warp + WARPS, 1);
-  else cp_async_commit();
+  // NB tiles in flight per warp (an empty commit group where no tile is left)
+#pragma unroll
+  for (int k = 0; k < NB; ++k) {
+    if (warp + k * WARPS < ntiles) issue_tile(warp + k * WARPS, k);
+    else cp_async_commit();
+  }
   if (p.early) pdl_wait();  // q (and slot `fresh`) come from the previous kernel
 
   const __half* qsrc = p.q + (size_t(b) * p.Hq + size_t(kvh) * p.G) * D;
   if (p.fused) {
     // the G query heads of this KV head: head norm + RoPE into shared memory;
     // the CTA whose chunk holds the new token's slot appends its k and v
-    __half* qs = reinterpret_cast<__half*>(smem + SMEM);
+    __half* qs = reinterpret_cast<__half*>(smem + (NB == 4 ? SMEM4 : SMEM));
     const int heads = p.Hq + 2 * p.Hkv;
     const __half* row = p.qkv + size_t(b) * heads * D;
     for (int i = warp; i < p.G; i += WARPS)
@@ -221,13 +229,14 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
 
 
   for (int it = 0, t = warp; t < ntiles; ++it, t += WARPS) {
-    cp_async_wait<1>();  // tile `it` landed; tile it + 1 may still be in flight
+    cp_async_wait<NB - 1>();  // tile `it` landed; the NB - 1 after it may still be in flight
     __syncwarp();
-    const uint32_t ks = wsm_u + (it & 1) * 2 * TILE_BYTES;
+    const int stage = it % NB;
+    const uint32_t ks = wsm_u + stage * 2 * TILE_BYTES;
     const uint32_t vs = ks + TILE_BYTES;
-    if ((p.early || p.fused) && it < 2) {
-      // the tiles of the first two rounds were requested before the previous
-      // kernel finished: reload the slot it wrote
+    if ((p.early || p.fused) && it < NB) {
+      // the tiles of the first NB rounds were requested before the previous
+      // kernel finished (or before this kernel appended): reload that slot
       const int r = p.fresh - (c0 + t * TILE);
       if (r >= 0 && r < TILE && p.fresh < c1) {
         const int ch = lane & 15;
@@ -308,8 +317,8 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
       }
     }
     __syncwarp();
-    // the stage is free: request tile it + 2 into it
-    if (t + 2 * WARPS < ntiles) issue_tile(t + 2 * WARPS, it & 1);
+    // the stage is free: request tile it + NB into it
+    if (t + NB * WARPS < ntiles) issue_tile(t + NB * WARPS, stage);
     else cp_async_commit();
   }
   cp_async_wait<0>();
@@ -484,6 +493,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
 struct Plan {
   int chunk, nch, nch_max;
   bool cluster;  // merge the chunks through distributed shared memory
+  int nb;        // tile stages per warp (2, or 4 when the grid holds at most one CTA per SM)
   size_t off_part, total;
 };
 
@@ -495,7 +505,8 @@ struct Plan {
 static std::atomic<int> g_merge_mode{0};
 
 // fit[n] (n <= MAX_CLUSTER): clusters of n CTAs the device holds at once
-// (0: not schedulable); null: no cluster merge
+// with 2 tile stages per warp, fit[MAX_CLUSTER + 1 + n] with 4 (0: not
+// schedulable); null: no cluster merge, 2 stages
 static Plan make_plan(int batch, int kv_heads, int G, int cap, int valid, int sms,
                       const int* fit = nullptr) {
   Plan pl{};
@@ -528,6 +539,12 @@ static Plan make_plan(int batch, int kv_heads, int G, int cap, int valid, int sm
       pl.cluster = true;
     }
   }
+  // 4 stages per warp when every CTA gets an SM of its own and each warp has
+  // at least 3 tiles: the whole chunk is requested at once (one HBM round trip)
+  pl.nb = 2;
+  if (fit && long(pl.nch) * bh <= sms && pl.chunk >= 3 * CHUNK_ALIGN &&
+      (!pl.cluster || fit[MAX_CLUSTER + 1 + pl.nch] >= bh))
+    pl.nb = 4;
   return pl;
 }
 
@@ -537,39 +554,52 @@ static Plan make_plan(int batch, int kv_heads, int G, int cap, int valid, int sm
 static int prepare_kernel(const int** fit_out) {
   static std::mutex mu;
   static bool done[64] = {};
-  static int fit[64][MAX_CLUSTER + 1] = {};
+  static int fit[64][2 * (MAX_CLUSTER + 1)] = {};
   int dev = 0;
   QX_CUDA_TRY(cudaGetDevice(&dev), "decode_attention: cudaGetDevice");
   QX_REQUIRE(dev >= 0 && dev < 64, "decode_attention: device index %d unsupported", dev);
   std::lock_guard<std::mutex> lk(mu);
   if (!done[dev]) {
-    QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<false>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_FUSED),
+    QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<false, 2>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(2, true)),
                 "decode_attention: set smem limit");
-    QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<true>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_FUSED),
+    QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<true, 2>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(2, true)),
                 "decode_attention: set smem limit");
-    QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<true>,
+    QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<false, 4>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(4, true)),
+                "decode_attention: set smem limit");
+    QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<true, 4>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(4, true)),
+                "decode_attention: set smem limit");
+    QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<true, 2>,
                                      cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
                 "decode_attention: allow 16-CTA clusters");
-    for (int cs = 2; cs <= MAX_CLUSTER; ++cs) {
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(cs, 1, 1);
-      cfg.blockDim = dim3(THREADS, 1, 1);
-      cfg.dynamicSmemBytes = SMEM;
-      cudaLaunchAttribute at[1];
-      at[0].id = cudaLaunchAttributeClusterDimension;
-      at[0].val.clusterDim.x = cs;
-      at[0].val.clusterDim.y = 1;
-      at[0].val.clusterDim.z = 1;
-      cfg.attrs = at;
-      cfg.numAttrs = 1;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, decode_attn_kernel<true>, &cfg) != cudaSuccess) {
-        cudaGetLastError();
-        n = 0;
+    QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<true, 4>,
+                                     cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                "decode_attention: allow 16-CTA clusters");
+    for (int nbi = 0; nbi < 2; ++nbi) {
+      for (int cs = 2; cs <= MAX_CLUSTER; ++cs) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(cs, 1, 1);
+        cfg.blockDim = dim3(THREADS, 1, 1);
+        cfg.dynamicSmemBytes = smem_bytes(nbi ? 4 : 2, true);
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = cs;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        const cudaError_t e = nbi ? cudaOccupancyMaxActiveClusters(&n, decode_attn_kernel<true, 4>, &cfg)
+                                  : cudaOccupancyMaxActiveClusters(&n, decode_attn_kernel<true, 2>, &cfg);
+        if (e != cudaSuccess) {
+          cudaGetLastError();
+          n = 0;
+        }
+        fit[dev][nbi * (MAX_CLUSTER + 1) + cs] = n;
       }
-      fit[dev][cs] = n;
     }
     done[dev] = true;
   }
@@ -585,9 +615,11 @@ static int prepare_kernel(const int** fit_out) {
 static int launch(const Plan& pl, const Params& prm, int batch, int kv_heads, cudaStream_t st,
                   const char* what) {
   const dim3 grid(pl.nch, batch * kv_heads), block(THREADS);
-  const int smem = prm.fused ? SMEM_FUSED : SMEM;
+  const int smem = smem_bytes(pl.nb, prm.fused != 0);
+  auto kern = pl.cluster ? (pl.nb == 4 ? decode_attn_kernel<true, 4> : decode_attn_kernel<true, 2>)
+                         : (pl.nb == 4 ? decode_attn_kernel<false, 4> : decode_attn_kernel<false, 2>);
   if (!pl.cluster && !prm.early) {
-    decode_attn_kernel<false><<<grid, block, smem, st>>>(prm);
+    kern<<<grid, block, smem, st>>>(prm);
     return check_launch(what);
   }
   cudaLaunchConfig_t cfg = {};
@@ -611,9 +643,7 @@ static int launch(const Plan& pl, const Params& prm, int batch, int kv_heads, cu
   }
   cfg.attrs = at;
   cfg.numAttrs = na;
-  QX_CUDA_TRY(pl.cluster ? cudaLaunchKernelEx(&cfg, decode_attn_kernel<true>, prm)
-                         : cudaLaunchKernelEx(&cfg, decode_attn_kernel<false>, prm),
-              what);
+  QX_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, prm), what);
   return check_launch(what);
 }
 

@@ -237,15 +237,16 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
                "r"(bytes)
                : "memory");
 }
-// try_wait suspends the thread (up to the hint, 1 ms) until the phase completes,
-// so waiting warps leave the issue slots to the computing ones.
+// try_wait suspends the thread for a system-dependent time while the phase is
+// incomplete (measured: without a suspend-time hint the GEMV runs 2-3 % faster
+// than with a 1 ms hint, e.g. 6.02 vs 6.17 us at the Qwen3-4B gate_proj shape).
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{ .reg .pred P; mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 P, [%1], %2, %3; "
+      "{ .reg .pred P; mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 P, [%1], %2; "
       "selp.u32 %0, 1, 0, P; }"
       : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(1000000u)
+      : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
 }
