@@ -339,6 +339,17 @@ int qx_decode_attention_qkv(const void* qkv, const void* q_norm_w, const void* k
                             int window, int64_t pos, float softmax_scale, void* workspace,
                             size_t workspace_bytes, qx_stream_t stream);
 
+/* Greedy head: logits = h W for h [batch, hidden] fp16 and W [hidden, vocab]
+ * fp16 (a rank's vocabulary slice, vocab contiguous), rounded to fp16, and per
+ * row the largest logit (as fp32) and its index + vocab_offset (the smallest
+ * index among equal maxima).  batch <= 32, hidden % 64 == 0, vocab % 8 == 0.
+ * Workspace: qx_lm_head_argmax_workspace_size(vocab) bytes, no
+ * initialisation.  New component (the reference leaves the lm_head to HF). */
+size_t qx_lm_head_argmax_workspace_size(int vocab);
+int qx_lm_head_argmax(const void* h, const void* weight, int batch, int hidden, int vocab,
+                      int64_t vocab_offset, float* out_val, int64_t* out_idx, void* workspace,
+                      size_t workspace_bytes, qx_stream_t stream);
+
 /* How both decode-attention entry points merge the slot chunks of one
  * sequence and KV head (process-wide; results agree within fp32 rounding):
  * 0 (default) through distributed shared memory, the chunk CTAs forming one

@@ -499,6 +499,31 @@ def decode_attention_qkv(qkv: torch.Tensor, q_heads: int, kv_heads: int, q_norm:
     return out
 
 
+def lm_head_argmax(h: torch.Tensor, weight: torch.Tensor, vocab_offset: int = 0):
+    """Greedy head: ``h`` fp16 ``[B, H]`` (B <= 32), ``weight`` fp16 ``[H, V]``
+    (a vocabulary slice).  Returns (max logit fp32 ``[B]``, index int64 ``[B]``
+    + ``vocab_offset``) of the fp16 logits ``h @ weight``; ties go to the
+    smallest index."""
+    for t, n in ((h, "h"), (weight, "weight")):
+        _check_input(t, n)
+        _check_fp16(t, n)
+    B, H = h.shape
+    if weight.dim() != 2 or weight.size(0) != H:
+        raise RuntimeError("lm_head_argmax: weight must be [H, V]")
+    V = weight.size(1)
+    dev = h.device
+    val = torch.empty(B, dtype=torch.float32, device=dev)
+    idx = torch.empty(B, dtype=torch.int64, device=dev)
+    st = _stream(dev)
+    with torch.cuda.device(dev):
+        need = _LIB.qx_lm_head_argmax_workspace_size(V)
+        ws = _workspace.get(dev, st, need, "lm_head_argmax")
+        _lib.check(_LIB.qx_lm_head_argmax(h.data_ptr(), weight.data_ptr(), B, H, V, int(vocab_offset),
+                                          val.data_ptr(), idx.data_ptr(), ws.data_ptr(), ws.numel(),
+                                          st.cuda_stream), "lm_head_argmax")
+    return val, idx
+
+
 def prefill_attention(q, k_new, v_new, k_cache, v_cache, count: int, sink: int, window: int,
                       softmax_scale: float | None = None):
     """Attention of a prompt chunk before its append: ``q`` fp16 ``[B, n, Hq, D]``

@@ -75,6 +75,9 @@ SIGNATURES = {
     "qx_decode_attention_qkv": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
                                         c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                                         c_int, c_int64, c_float, c_void_p, c_size_t, c_void_p]),
+    "qx_lm_head_argmax_workspace_size": (c_size_t, [c_int]),
+    "qx_lm_head_argmax": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int64, c_void_p, c_void_p,
+                                  c_void_p, c_size_t, c_void_p]),
     "qx_decode_attention_pin_merge": (c_int, [c_int]),
     "qx_decode_attention_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                             c_int, c_int, c_int, c_int, c_int64, c_float,

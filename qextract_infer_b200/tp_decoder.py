@@ -18,10 +18,11 @@ NCCL):
 The projections that read the same input are fused: q|k|v and gate|up are
 each one W4A16-LoRA call (weights side by side, LoRA A side by side, LoRA B
 block-diagonal, rank zero-padded to a supported size: the same math).  Per
-decode step and layer (7 launches): qkv GEMV -> per-head RMSNorm of q and k
-(Qwen3), RoPE (theta 1e6, keys stored post-RoPE at their absolute positions),
-the ring append and the GQA decode attention over sink + window (including the
-new token) in one kernel -> o GEMV -> all-reduce + residual add + RMSNorm in
+decode step and layer (7 launches at one or two sequences, 8 beyond): qkv GEMV
+-> per-head RMSNorm of q and k (Qwen3), RoPE (theta 1e6, keys stored post-RoPE
+at their absolute positions), the ring append and the GQA decode attention over
+sink + window (including the new token), in one kernel or as append + attention
+-> o GEMV -> all-reduce + residual add + RMSNorm in
 one kernel -> gate|up GEMV with the SwiGLU epilogue (gate and up columns
 interleaved in blocks of 8, so one CTA holds both halves of an output) -> down
 GEMV -> all-reduce + residual add + the next RMSNorm in one kernel.  With more than one rank the all-reduce is a
@@ -207,6 +208,10 @@ class TPDecoder:
             self.layers.append(L)
         self.cache = _C.RingBufferKVCache(cfg.num_layers, self.hkv, D, cfg.sink, cfg.window,
                                           batch=batch, device=dev)
+        # q/k norm + RoPE + append fused into the attention kernel for a few
+        # sequences (one launch fewer per layer, same time); for many, the
+        # separate append kernel is faster (32 sequences: 86 vs 96 us per layer)
+        self.fused_attention = batch * self.hkv <= 16
         self.max_pos = 1 << 16
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D))
         ang = torch.arange(self.max_pos, device=dev, dtype=torch.float32)[:, None] * inv[None, :]
@@ -270,9 +275,17 @@ class TPDecoder:
         h = _C.fused_rmsnorm(x, self.layers[0]["in_norm"], eps)
         n = len(self.layers)
         for li, L in enumerate(self.layers):
-            att = _C.decode_attention_qkv(L["qkv"](h), self.hq, self.hkv, L["q_norm"], L["k_norm"], eps,
-                                          cos, sin, self.cache.k[li], self.cache.v[li], cfg.sink,
-                                          cfg.window, pos)
+            qkv = L["qkv"](h)
+            if self.fused_attention:
+                att = _C.decode_attention_qkv(qkv, self.hq, self.hkv, L["q_norm"], L["k_norm"], eps,
+                                              cos, sin, self.cache.k[li], self.cache.v[li], cfg.sink,
+                                              cfg.window, pos)
+            else:
+                q = _C.qk_norm_rope_append(qkv, self.hq, self.hkv, L["q_norm"], L["k_norm"], eps, cos,
+                                           sin, self.cache.k[li], self.cache.v[li], cfg.sink, cfg.window,
+                                           pos)
+                att = _C.decode_attention(q, self.cache.k[li], self.cache.v[li], pos + 1, cfg.sink,
+                                          cfg.window, after_append=True)
             h = self._reduce_add_norm(L["o"](att.view(B, self.hq * D)), x, L["post_norm"])  # x += o
             dn = L["down"](L["gate_up"].swiglu(h))
             nxt_w = self.layers[li + 1]["in_norm"] if li + 1 < n else self.final_norm
@@ -282,7 +295,7 @@ class TPDecoder:
         return (nxt, x) if return_hidden else nxt
 
     def _greedy_logits(self, x: torch.Tensor) -> torch.Tensor:
-        """this rank's vocabulary slice of the logits [B, V / tp] (fp16, cuBLAS)"""
+        """this rank's vocabulary slice of the logits [B, V / tp] (fp16; tests only)"""
         h = _C.fused_rmsnorm(x, self.final_norm, self.cfg.rms_eps)
         return h @ self.lm_head
 
@@ -291,9 +304,7 @@ class TPDecoder:
 
     def _greedy_normed(self, h: torch.Tensor) -> torch.Tensor:
         """greedy tokens from the final-normed hidden state"""
-        logits = h @ self.lm_head
-        val, idx = logits.float().max(dim=-1)
-        idx = idx + self.rank * self.lm_head.size(1)
+        val, idx = _C.lm_head_argmax(h, self.lm_head, self.rank * self.lm_head.size(1))
         if self.world > 1:
             vals = [torch.empty_like(val) for _ in range(self.world)]
             idxs = [torch.empty_like(idx) for _ in range(self.world)]

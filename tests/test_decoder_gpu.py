@@ -25,13 +25,17 @@ def _close(a, b, what, tol=1e-2):
     assert err <= tol * scale + tol, f"{what}: max err {err} at scale {scale}"
 
 
-def test_prefill_and_decode_match_reference():
+@pytest.mark.parametrize("fused_attention", [True, False])
+def test_prefill_and_decode_match_reference(fused_attention):
+    """Both decode-step attention forms: the fused norm/RoPE/append/attention
+    kernel and the append kernel followed by attention."""
     from qextract_infer_b200.tp_decoder import TPDecoder
     assert torch.cuda.is_available()
     dev = torch.device("cuda", 0)
     cfg = _tiny_cfg()
     B, T = 2, 100
     dec = TPDecoder(cfg, batch=B, device=dev, seed=7)
+    dec.fused_attention = fused_attention
     ref = RefDecoder(dec)
     toks = torch.randint(0, cfg.vocab, (B, T), generator=torch.Generator().manual_seed(4)).to(dev)
     nxt, hid = dec.prefill(toks, chunk=64, return_hidden=True)
