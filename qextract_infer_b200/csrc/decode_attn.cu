@@ -54,7 +54,8 @@ constexpr int PSTRIDE = D + 4;                   // floats per (row) partial: m,
 constexpr int COUNTER_SLOTS = 4096;              // fixed counter region at the workspace start
 constexpr int MAX_CHUNKS = 64;                   // bounds the merge's shared memory
 constexpr int MAX_CLUSTER = 16;                  // chunks merged through distributed shared memory
-constexpr int CPART_OFF = WARPS * 16 * D * 4 + 2 * WARPS * 16 * 4;  // cluster merge: [G][PSTRIDE]
+constexpr int OSTRIDE = D + 8;                   // floats per row of the warp merge (conflict-free float2 stores)
+constexpr int CPART_OFF = WARPS * 16 * OSTRIDE * 4 + 2 * WARPS * 16 * 4;  // cluster merge: [G][PSTRIDE]
 constexpr int QS_BYTES = 16 * D * 2;             // fused form: the G <= 16 rotated query heads
 constexpr int SMEM_FUSED = SMEM + QS_BYTES;
 // deep form: 4 tile stages per warp (every tile of a 256-slot chunk in flight at
@@ -131,6 +132,14 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
   return v;
 }
 __device__ __forceinline__ void cluster_sync() {
@@ -329,14 +338,14 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
 
   // merge the warps of this CTA in shared memory (reuses the tile buffers)
   __syncthreads();
-  float* Os = reinterpret_cast<float*>(smem);            // [WARPS][16][D]
-  float* ms = Os + WARPS * 16 * D;                        // [WARPS][16]
+  float* Os = reinterpret_cast<float*>(smem);            // [WARPS][16][OSTRIDE]
+  float* ms = Os + WARPS * 16 * OSTRIDE;                  // [WARPS][16]
   float* ls = ms + WARPS * 16;                            // [WARPS][16]
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const int d = 8 * j + 2 * c;
-    *reinterpret_cast<float2*>(Os + (warp * 16 + g) * D + d) = make_float2(o[j][0], o[j][1]);
-    *reinterpret_cast<float2*>(Os + (warp * 16 + g + 8) * D + d) = make_float2(o[j][2], o[j][3]);
+    *reinterpret_cast<float2*>(Os + (warp * 16 + g) * OSTRIDE + d) = make_float2(o[j][0], o[j][1]);
+    *reinterpret_cast<float2*>(Os + (warp * 16 + g + 8) * OSTRIDE + d) = make_float2(o[j][2], o[j][3]);
   }
   if (c == 0) {
     ms[warp * 16 + g] = m_r[0];
@@ -358,7 +367,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
       for (int w = 0; w < WARPS; ++w) {
         const float f = ms[w * 16 + r] == -INFINITY ? 0.f : exp2f(ms[w * 16 + r] - mx);
         L = fmaf(ls[w * 16 + r], f, L);
-        O = fmaf(Os[(w * 16 + r) * D + d], f, O);
+        O = fmaf(Os[(w * 16 + r) * OSTRIDE + d], f, O);
       }
       mypart[r * PSTRIDE + 4 + d] = O;
       if (d == 0) {
@@ -370,38 +379,53 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
 
   if constexpr (CLUSTER) {
     // every chunk's (max, sum, O) is in its CTA's shared memory: this CTA
-    // merges outputs [lo, hi) of the G x D block, chunks summed in order
+    // merges output vectors [v0, v1) (4 head dims each) of the G x D block.
+    // A lane per (vector, chunk): 16 lanes read the chunks' (max, sum) and
+    // 16-byte O vector over distributed shared memory in one round, then
+    // reduce across the 16 lanes with butterfly shuffles (a fixed order:
+    // deterministic); chunks past nch contribute nothing.
     cluster_sync();
     const int nch = p.nch, G = p.G;
-    const int per = (G * D + nch - 1) / nch;
-    const int lo = ci * per, hi = min(G * D, lo + per);
+    const int nvec = G * (D / 4);
+    const int per = (nvec + nch - 1) / nch;
+    const int v0 = ci * per, v1 = min(nvec, v0 + per);
     const uint32_t base = smem_u32(smem + CPART_OFF);
-    for (int idx = lo + tid; idx < hi; idx += THREADS) {
-      const int r = idx / D, d = idx - r * D;
-      float mk[MAX_CLUSTER], lk[MAX_CLUSTER], ok[MAX_CLUSTER];
-#pragma unroll
-      for (int k = 0; k < MAX_CLUSTER; ++k) {
-        if (k < nch) {
-          const uint32_t a = cluster_map(base, uint32_t(k)) + uint32_t(r * PSTRIDE) * 4u;
-          mk[k] = ld_cluster_f32(a);
-          lk[k] = ld_cluster_f32(a + 4u);
-          ok[k] = ld_cluster_f32(a + uint32_t(4 + d) * 4u);
-        }
+    const int k = tid & 15;
+    for (int vb = v0; vb < v1; vb += THREADS / 16) {  // uniform trip count: whole warps shuffle
+      const int vv = vb + (tid >> 4);
+      const int r = vv / (D / 4), d0 = (vv - r * (D / 4)) * 4;
+      float mk = -INFINITY, lk = 0.f;
+      float4 ov = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (vv < v1 && k < nch) {
+        const uint32_t a = cluster_map(base, uint32_t(k)) + uint32_t(r * PSTRIDE) * 4u;
+        mk = ld_cluster_f32(a);
+        lk = ld_cluster_f32(a + 4u);
+        ov = ld_cluster_f32x4(a + uint32_t(4 + d0) * 4u);
       }
-      float mx = -INFINITY;
+      float mx = mk;
 #pragma unroll
-      for (int k = 0; k < MAX_CLUSTER; ++k)
-        if (k < nch) mx = fmaxf(mx, mk[k]);
-      float L = 0.f, O = 0.f;
+      for (int w = 1; w < 16; w <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, w));
+      const float f = mk == -INFINITY ? 0.f : exp2f(mk - mx);
+      float L = lk * f;
+      ov.x *= f;
+      ov.y *= f;
+      ov.z *= f;
+      ov.w *= f;
 #pragma unroll
-      for (int k = 0; k < MAX_CLUSTER; ++k) {
-        if (k < nch) {
-          const float f = mk[k] == -INFINITY ? 0.f : exp2f(mk[k] - mx);
-          L = fmaf(lk[k], f, L);
-          O = fmaf(ok[k], f, O);
-        }
+      for (int w = 1; w < 16; w <<= 1) {
+        L += __shfl_xor_sync(0xffffffffu, L, w);
+        ov.x += __shfl_xor_sync(0xffffffffu, ov.x, w);
+        ov.y += __shfl_xor_sync(0xffffffffu, ov.y, w);
+        ov.z += __shfl_xor_sync(0xffffffffu, ov.z, w);
+        ov.w += __shfl_xor_sync(0xffffffffu, ov.w, w);
       }
-      p.out[(size_t(b) * p.Hq + size_t(kvh) * G + r) * D + d] = __float2half_rn(O / L);
+      if (k == 0 && vv < v1) {
+        __half* dst = p.out + (size_t(b) * p.Hq + size_t(kvh) * G + r) * D + d0;
+        dst[0] = __float2half_rn(ov.x / L);
+        dst[1] = __float2half_rn(ov.y / L);
+        dst[2] = __float2half_rn(ov.z / L);
+        dst[3] = __float2half_rn(ov.w / L);
+      }
     }
     cluster_sync();  // the peers' shared memory stays live until every read is done
     return;

@@ -391,22 +391,23 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
       const uint32_t sz_bytes =
           uint32_t(p.gmax) * (COLS * 2 + (p.zeros_tma ? (p.zeros_packed ? COLS / 2 : COLS * 2) : 0));
       mbar_expect_tx(bar_st, sz_bytes);
-      // the weight groups with their LoRA A rows, scales / fp16 zero points of
-      // this CTA's groups (gmax rows; rows past the CTA's range are read but
-      // unused), the LoRA B tile
-      const uint64_t pol = evict_first_policy();
-      for (int i = 0; i < min(ngrp, nst); ++i) {
-        mbar_expect_tx(full0 + 8 * i, STAGE_TX);
-        tma_2d_hint(ring_s + i * STAGE, &p.tw, wx, (ks0 + i * KPG) * 4, full0 + 8 * i, pol);
-        if (R > 0)
-          bulk_g2s(ring_s + i * STAGE + WBYTES, p.A + size_t(k0 + i * GROUPK) * R, ABYTES, full0 + 8 * i);
-      }
+      // scales / fp16 zero points of this CTA's groups (gmax rows; rows past
+      // the CTA's range are read but unused) first: they are converted before
+      // the dependency wait; then the LoRA B tile and the weight groups with
+      // their LoRA A rows
       tma_2d(smem_addr(smem + L.sz_s), &p.ts, n_tile0, gr0, bar_st);
       if (p.zeros_tma)
         tma_2d(smem_addr(smem + L.sz_z), &p.tz, p.zeros_packed ? n_tile0 / 8 : n_tile0, gr0, bar_st);
       if (R > 0) {
         mbar_expect_tx(bar_b, uint32_t(R * COLS) * 2);
         tma_2d(smem_addr(smem + L.Bs), &p.tb, n_tile0, 0, bar_b);
+      }
+      const uint64_t pol = evict_first_policy();
+      for (int i = 0; i < min(ngrp, nst); ++i) {
+        mbar_expect_tx(full0 + 8 * i, STAGE_TX);
+        tma_2d_hint(ring_s + i * STAGE, &p.tw, wx, (ks0 + i * KPG) * 4, full0 + 8 * i, pol);
+        if (R > 0)
+          bulk_g2s(ring_s + i * STAGE + WBYTES, p.A + size_t(k0 + i * GROUPK) * R, ABYTES, full0 + 8 * i);
       }
     }
     // GPTQ qzeros rows of N/2 bytes that are not a 16 B multiple: plain loads
@@ -422,6 +423,27 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     }
   }
 
+  // scales and zero points of the CTA's groups as floats (s, s * z), by every
+  // thread before the dependency wait: they do not depend on the previous
+  // kernel and their copy is the first one issued (measured: 6.34 -> 6.23 us
+  // per call at the Qwen3-4B gate_proj shape against converting them after
+  // the activations are staged)
+  mbar_wait(bar_st, 0);
+  {
+    float2* sfw = reinterpret_cast<float2*>(smem + L.sf);
+    const __half* szs = reinterpret_cast<const __half*>(smem + L.sz_s);
+    for (int it = tid; it < ngrp * COLS; it += THREADS) {
+      const int gi = it >> 8, col = it & (COLS - 1);
+      const float sc = __half2float(szs[it]);
+      float z;
+      if (p.zeros_packed)
+        z = float(((reinterpret_cast<const uint32_t*>(smem + L.sz_z)[gi * (COLS / 8) + (col >> 3)] >>
+                    (4 * (col & 7))) & 0xFu) + unsigned(p.zero_offset));
+      else
+        z = __half2float(reinterpret_cast<const __half*>(smem + L.sz_z)[it]);
+      sfw[it] = make_float2(sc, sc * z);
+    }
+  }
   // activations (plain 128-bit loads) in MMA-B order (x0,x4 | x1,x5 | x2,x6 | x3,x7) per packed row,
   // and per group the sums over the two nibble classes:
   // (Off, Sx) = (1024 Xa + 64 Xb, Xa + Xb), by the whole CTA.  A group of a
@@ -459,23 +481,6 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
       if (ok && (it & (4 * KPG - 1)) == 0)
         *reinterpret_cast<float2*>(xksw + ((t / KPG) * Mp + m) * 2) =
             make_float2(fmaf(1024.f, xa, 64.f * xb), xa + xb);
-    }
-  }
-  // scales and zero points of the CTA's groups as floats (s, s * z)
-  mbar_wait(bar_st, 0);
-  {
-    float2* sfw = reinterpret_cast<float2*>(smem + L.sf);
-    const __half* szs = reinterpret_cast<const __half*>(smem + L.sz_s);
-    for (int it = tid; it < ngrp * COLS; it += THREADS) {
-      const int gi = it >> 8, col = it & (COLS - 1);
-      const float sc = __half2float(szs[it]);
-      float z;
-      if (p.zeros_packed)
-        z = float(((reinterpret_cast<const uint32_t*>(smem + L.sz_z)[gi * (COLS / 8) + (col >> 3)] >>
-                    (4 * (col & 7))) & 0xFu) + unsigned(p.zero_offset));
-      else
-        z = __half2float(reinterpret_cast<const __half*>(smem + L.sz_z)[it]);
-      sfw[it] = make_float2(sc, sc * z);
     }
   }
   __syncthreads();  // permuted activations, group sums, scales ready
