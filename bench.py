@@ -831,6 +831,151 @@ def run_profile_decode_step(args):
     return 0
 
 
+def _trace_lib():
+    """The profiling build of the library (per-CTA phase timestamps), loaded
+    beside the package's product library; built on demand."""
+    import ctypes
+    from qextract_infer_b200 import _lib, build
+    path = build.LIB_TRACE
+    if not os.path.exists(path):
+        build.build(trace=True)
+    lib = ctypes.CDLL(path)
+    for name, (res, argt) in _lib.SIGNATURES.items():
+        getattr(lib, name).restype = res
+        getattr(lib, name).argtypes = argt
+    return lib
+
+
+def _timeline_summary(t, names, calls):
+    """t [calls, grid, 16] int64 ns stamps -> per phase the median over calls
+    1..calls-1 of (median over CTAs of the phase - the call's first CTA entry),
+    in us; plus the previous call's last exit and the call period."""
+    import numpy as np
+    out = {}
+    firsts = [t[c, :, 0][t[c, :, 0] > 0].min() for c in range(calls)]
+    for slot, name in names:
+        vals = []
+        for c in range(1, calls):
+            v = t[c, :, slot]
+            v = v[v > 0]
+            if len(v):
+                vals.append((np.median(v) - firsts[c]) / 1e3)
+        if vals:
+            out[name] = round(float(np.median(vals)), 3)
+    last_exit = []
+    for c in range(1, calls):
+        ex = t[c - 1, :, names[-1][0]]
+        ex = ex[ex > 0]
+        if len(ex):
+            last_exit.append((ex.max() - firsts[c]) / 1e3)
+    out["previous_call_last_exit"] = round(float(np.median(last_exit)), 3) if last_exit else None
+    out["period"] = round(float((firsts[calls - 1] - firsts[1]) / (calls - 2) / 1e3), 3)
+    return out
+
+
+def run_timeline(args):
+    """Per-CTA phase timeline (%globaltimer) of a graph-replayed chain of
+    calls, from the profiling build of the library (libqx_b200_trace.so,
+    ``python -m qextract_infer_b200.build --trace``): the decode GEMV at the
+    Qwen3-4B gate_proj shape (8 calls over rotating weight sets) and the decode
+    attention of one sequence over a full 4 + 4092 ring (8 calls over 12
+    layers' caches).  One JSON line per kernel: each phase as the median over
+    the calls of (median CTA time - the call's first CTA entry), in us."""
+    import ctypes
+    import numpy as np
+    import torch
+    lib = _trace_lib()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    st = torch.cuda.Stream(dev)
+    calls = 8
+    # ---- decode GEMV, config 0
+    nsets = int(np.ceil(2.2 * L2_BYTES / BYTES_PER_CALL))
+    sets = make_weight_sets(torch, dev, nsets)
+    x = torch.randn(M, K, device=dev).half()
+    ys = [torch.empty(M, N, dtype=torch.float16, device=dev) for _ in range(2)]
+    scale = float(np.float32(ALPHA) / np.float32(RANK))
+    plan = (ctypes.c_int * 5)()
+    assert lib.qx_w4a16_gemv_plan(M, K, N, RANK, GROUP, 1, plan) == 0
+    grid = plan[0] * plan[1]
+
+    def gemv(i):
+        qw, sc, qz, A, B = sets[i % nsets]
+        rc = lib.qx_w4a16_lora_gemv(x.data_ptr(), qw.data_ptr(), sc.data_ptr(), qz.data_ptr(), 1, 0,
+                                    A.data_ptr(), B.data_ptr(), ys[i & 1].data_ptr(), M, K, N, RANK, GROUP,
+                                    scale, ctypes.c_void_p(st.cuda_stream))
+        if rc:
+            raise RuntimeError(lib.qx_last_error().decode())
+
+    def traced_chain(kernel, fn, nwarm, grid_max):
+        buf = torch.zeros(calls * grid_max * 16, dtype=torch.int64, device=dev)
+        with torch.cuda.stream(st):
+            for i in range(nwarm):
+                fn(i)
+        st.synchronize()
+        if lib.qx_trace_launches(kernel, ctypes.c_void_p(buf.data_ptr()), calls):
+            raise RuntimeError(lib.qx_last_error().decode())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for i in range(calls):
+                fn(i)
+        lib.qx_trace_launches(kernel, None, 0)
+        with torch.cuda.stream(st):
+            for _ in range(3):
+                g.replay()
+        st.synchronize()
+        buf.zero_()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st):
+            e0.record(st)
+            g.replay()
+            e1.record(st)
+        st.synchronize()
+        flat = buf.view(-1, 16).cpu().numpy()
+        n = int((flat[:, 0] > 0).sum()) // calls
+        del g
+        return flat[:calls * n].reshape(calls, n, 16), n, e0.elapsed_time(e1) * 1e3 / calls
+
+    t, n, us = traced_chain(0, gemv, nsets, grid)
+    names = [(0, "entry"), (1, "dependency_wait_passed"), (2, "first_group_landed"), (3, "weight_loop_done"),
+             (4, "helper_lora_down_done"), (5, "lora_up_done"), (6, "partials_sent"),
+             (7, "partials_received"), (8, "exit")]
+    d = {"timeline": "w4a16_lora_gemv", "workload": WORKLOAD, "grid": n, "calls": calls,
+         "us_per_call_traced": round(us, 3), "unit": "us from the call's first CTA entry",
+         "ctas_entered_before_previous_call_ended": round(float(np.mean(
+             [np.mean(t[c, :, 0] < t[c - 1, :, 8][t[c - 1, :, 8] > 0].max()) for c in range(1, calls)])), 3)}
+    d.update(_timeline_summary(t, names, calls))
+    print(json.dumps(d), flush=True)
+    del sets
+    torch.cuda.empty_cache()
+    # ---- decode attention, one sequence over a full ring
+    L, Hkv, D, S, W, Hq = 12, 8, 128, 4, 4092, 32
+    k = torch.randn(L, 1, S + W, Hkv, D, device=dev).half()
+    v = torch.randn(L, 1, S + W, Hkv, D, device=dev).half()
+    q = torch.randn(1, Hq, D, device=dev).half()
+    out = torch.empty_like(q)
+    wsb = lib.qx_decode_attention_workspace_size(1, Hq, Hkv, D, S, W)
+    ws = torch.zeros(wsb + 256, dtype=torch.uint8, device=dev)
+    count = 32768 + 64
+
+    def attn(i):
+        rc = lib.qx_decode_attention(q.data_ptr(), k[i % L].data_ptr(), v[i % L].data_ptr(), out.data_ptr(), 1,
+                                     Hq, Hkv, D, S, W, count, 0.0, ws.data_ptr(), wsb,
+                                     ctypes.c_void_p(st.cuda_stream))
+        if rc:
+            raise RuntimeError(lib.qx_last_error().decode())
+
+    t, n, us = traced_chain(1, attn, L, 64 * Hkv)
+    names = [(0, "entry"), (1, "dependency_wait_passed"), (2, "first_tile_landed"), (3, "tile_loop_done"),
+             (4, "warps_merged"), (5, "chunk_barrier_passed"), (6, "exit")]
+    d = {"timeline": "decode_attention", "workload": "one sequence, 32/8 heads x 128, 4 + 4092 ring full",
+         "grid": n, "calls": calls, "us_per_call_traced": round(us, 3),
+         "unit": "us from the call's first CTA entry"}
+    d.update(_timeline_summary(t, names, calls))
+    print(json.dumps(d), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -847,7 +992,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=8192, help="decode_tp: prompt tokens")
     ap.add_argument("--decode", type=int, default=64, help="decode_tp: greedy decode tokens")
     ap.add_argument("--workload", choices=["decode_gemv", "kernels", "prefill_gemm", "decode_tp",
-                                           "profile_cases", "profile_decode_step"],
+                                           "profile_cases", "profile_decode_step", "timeline"],
                     default="decode_gemv",
                     help="decode_gemv: the headline line; kernels: RMSNorm/SwiGLU/ring/attention lines; "
                          "prefill_gemm: the tcgen05 GEMM over the Qwen3-8B shapes at M=4096")
@@ -862,6 +1007,8 @@ def main():
         return run_profile_cases(args)
     if args.workload == "profile_decode_step":
         return run_profile_decode_step(args)
+    if args.workload == "timeline":
+        return run_timeline(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)

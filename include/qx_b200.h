@@ -50,6 +50,18 @@ const char* qx_last_error(void);
 int qx_get_device_error(unsigned* code, int reset);
 /* Library version string. */
 const char* qx_version(void);
+/* Profiling: per-CTA phase timestamps (%globaltimer, ns) of the next
+ * `launches` launches of one kernel family into `buf` (device memory,
+ * launches x grid x 16 uint64; launch i, CTA c at (i * grid + c) * 16; slot 15
+ * holds the SM id; which slot is which phase is listed beside each kernel's
+ * trace points).  Only the profiling build of the library
+ * (libqx_b200_trace.so, compiled with -DQX_TRACE) records; the product library
+ * returns QX_ERR_UNSUPPORTED and carries no trace code in its kernels.
+ * buf = NULL stops tracing.  No counterpart in the reference. */
+#define QX_TRACE_GEMV 0
+#define QX_TRACE_DECODE_ATTENTION 1
+#define QX_TRACE_SLOTS 16
+int qx_trace_launches(int kernel, void* buf, int launches);
 /* Host plumbing for callers without their own CUDA runtime binding (ctypes,
  * cgo, JNI): one cudaMemcpyAsync of `bytes` from src to dst on `stream`, the
  * direction taken from the pointers (pinned host or device).  No counterpart

@@ -24,6 +24,7 @@ SIGNATURES = {
     "qx_last_error": (c_char_p, []),
     "qx_version": (c_char_p, []),
     "qx_copy_async": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+    "qx_trace_launches": (c_int, [c_int, c_void_p, c_int]),
     "qx_w4a16_lora_gemv": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p,
                                    c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float,
                                    c_void_p]),

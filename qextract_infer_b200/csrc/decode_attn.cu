@@ -91,7 +91,14 @@ struct Params {
   const float* cosr;
   const float* sinr;
   float eps;
+  unsigned long long* trace;  // profiling build only (qx_trace_launches): phase timestamps
+  int trace_launch;
 };
+
+// Trace slots of an attention CTA (profiling build): 0 entry, 1 dependency
+// wait passed, 2 first K/V tile landed, 3 tile loop done, 4 warps merged,
+// 5 chunk barrier passed (cluster merge), 6 exit
+enum AttnTrace { TR_ENTRY, TR_WAITED, TR_TILE0, TR_LOOP, TR_WARP_MERGE, TR_CHUNK_SYNC, TR_EXIT };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -153,6 +160,8 @@ __device__ __forceinline__ void cluster_sync() {
 template <bool CLUSTER, int NB>
 __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
   pdl_trigger();
+  unsigned long long* const trc = trace_base(p.trace, p.trace_launch);
+  trace_stamp(trc, TR_ENTRY, threadIdx.x == 0);
   if (!p.early) pdl_wait();  // no-op unless launched with programmatic dependent launch
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ unsigned s_is_last;
@@ -198,6 +207,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
     else cp_async_commit();
   }
   if (p.early) pdl_wait();  // q (and slot `fresh`) come from the previous kernel
+  trace_stamp(trc, TR_WAITED, threadIdx.x == 0);
 
   const __half* qsrc = p.q + (size_t(b) * p.Hq + size_t(kvh) * p.G) * D;
   if (p.fused) {
@@ -239,6 +249,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
 
   for (int it = 0, t = warp; t < ntiles; ++it, t += WARPS) {
     cp_async_wait<NB - 1>();  // tile `it` landed; the NB - 1 after it may still be in flight
+    trace_stamp(trc, TR_TILE0, threadIdx.x == 0 && it == 0);
     __syncwarp();
     const int stage = it % NB;
     const uint32_t ks = wsm_u + stage * 2 * TILE_BYTES;
@@ -331,6 +342,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
     else cp_async_commit();
   }
   cp_async_wait<0>();
+  trace_stamp(trc, TR_LOOP, threadIdx.x == 0);
   l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 1);
   l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 2);
   l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 1);
@@ -377,6 +389,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
     }
   }
 
+  trace_stamp(trc, TR_WARP_MERGE, threadIdx.x == 0);
   if constexpr (CLUSTER) {
     // every chunk's (max, sum, O) is in its CTA's shared memory: this CTA
     // merges output vectors [v0, v1) (4 head dims each) of the G x D block.
@@ -385,6 +398,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
     // reduce across the 16 lanes with butterfly shuffles (a fixed order:
     // deterministic); chunks past nch contribute nothing.
     cluster_sync();
+    trace_stamp(trc, TR_CHUNK_SYNC, threadIdx.x == 0);
     const int nch = p.nch, G = p.G;
     const int nvec = G * (D / 4);
     const int per = (nvec + nch - 1) / nch;
@@ -428,6 +442,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
       }
     }
     cluster_sync();  // the peers' shared memory stays live until every read is done
+    trace_stamp(trc, TR_EXIT, threadIdx.x == 0);
     return;
   }
 
@@ -512,6 +527,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
     }
   }
   if (tid == 0) p.counters[bh] = 0u;
+  trace_stamp(trc, TR_EXIT, tid == 0);
 }
 
 struct Plan {
@@ -642,8 +658,10 @@ static int launch(const Plan& pl, const Params& prm, int batch, int kv_heads, cu
   const int smem = smem_bytes(pl.nb, prm.fused != 0);
   auto kern = pl.cluster ? (pl.nb == 4 ? decode_attn_kernel<true, 4> : decode_attn_kernel<true, 2>)
                          : (pl.nb == 4 ? decode_attn_kernel<false, 4> : decode_attn_kernel<false, 2>);
+  Params pt = prm;
+  pt.trace = trace_next(QX_TRACE_DECODE_ATTENTION, &pt.trace_launch);
   if (!pl.cluster && !prm.early) {
-    kern<<<grid, block, smem, st>>>(prm);
+    kern<<<grid, block, smem, st>>>(pt);
     return check_launch(what);
   }
   cudaLaunchConfig_t cfg = {};
@@ -667,7 +685,7 @@ static int launch(const Plan& pl, const Params& prm, int batch, int kv_heads, cu
   }
   cfg.attrs = at;
   cfg.numAttrs = na;
-  QX_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, prm), what);
+  QX_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, pt), what);
   return check_launch(what);
 }
 

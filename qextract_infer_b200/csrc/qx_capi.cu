@@ -44,7 +44,47 @@ int device_sm_count() {
   return cache[dev];
 }
 
+namespace {
+struct TraceTarget {
+  unsigned long long* buf = nullptr;
+  int next = 0, launches = 0;
+};
+std::mutex g_trace_mu;
+TraceTarget g_trace[2];  // QX_TRACE_GEMV, QX_TRACE_DECODE_ATTENTION
+}  // namespace
+
+unsigned long long* trace_next(int kernel, int* launch) {
+#ifdef QX_TRACE
+  std::lock_guard<std::mutex> lk(g_trace_mu);
+  TraceTarget& t = g_trace[kernel];
+  if (t.buf == nullptr || t.next >= t.launches) return nullptr;
+  *launch = t.next++;
+  return t.buf;
+#else
+  (void)kernel;
+  *launch = 0;
+  return nullptr;
+#endif
+}
+
 }  // namespace qx
+
+extern "C" int qx_trace_launches(int kernel, void* buf, int launches) {
+  QX_REQUIRE(kernel == QX_TRACE_GEMV || kernel == QX_TRACE_DECODE_ATTENTION, "trace: unknown kernel %d",
+             kernel);
+  QX_REQUIRE(buf == nullptr || launches > 0, "trace: launches=%d", launches);
+#ifdef QX_TRACE
+  std::lock_guard<std::mutex> lk(qx::g_trace_mu);
+  qx::g_trace[kernel].buf = static_cast<unsigned long long*>(buf);
+  qx::g_trace[kernel].next = 0;
+  qx::g_trace[kernel].launches = buf ? launches : 0;
+  return QX_OK;
+#else
+  return qx::fail(QX_ERR_UNSUPPORTED,
+                  "trace: this library was built without tracing (profiling build: "
+                  "python -m qextract_infer_b200.build --trace)");
+#endif
+}
 
 extern "C" const char* qx_last_error(void) { return qx::g_last_error; }
 

@@ -136,6 +136,47 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// ---------------------------------------------------------------- trace --
+// Per-CTA phase timestamps for profiling builds (-DQX_TRACE,
+// libqx_b200_trace.so): a traced launch writes QX_TRACE_SLOTS uint64 per CTA
+// (slot QX_TRACE_SLOTS - 1: the SM id).  In the product build trace_base()
+// is a constant null and every trace_stamp() compiles to nothing.
+// Host side: the next trace buffer and launch index of a kernel family
+// (nullptr when tracing is off or the build has no tracing).
+unsigned long long* trace_next(int kernel, int* launch);
+
+__device__ __forceinline__ unsigned long long* trace_base(unsigned long long* buf, int launch) {
+#ifdef QX_TRACE
+  if (buf == nullptr) return nullptr;
+  const size_t grid = size_t(gridDim.x) * gridDim.y * gridDim.z;
+  const size_t cta = (size_t(blockIdx.z) * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+  unsigned long long* b = buf + (size_t(launch) * grid + cta) * QX_TRACE_SLOTS;
+  if (threadIdx.x == 0) {
+    unsigned sm;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+    b[QX_TRACE_SLOTS - 1] = sm;
+  }
+  return b;
+#else
+  (void)buf;
+  (void)launch;
+  return nullptr;
+#endif
+}
+__device__ __forceinline__ void trace_stamp(unsigned long long* b, int slot, bool who) {
+#ifdef QX_TRACE
+  if (b != nullptr && who) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    b[slot] = t;
+  }
+#else
+  (void)b;
+  (void)slot;
+  (void)who;
+#endif
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -10,15 +10,17 @@
 //                      ~1.6 % of the FLOPs), stored as fp16 high and low parts
 //                      [M][64] (zero-padded ranks) for the GEMM's TMA
 //   w4a16_gemm_kernel  one CTA per 128 x 256 output tile:
-//     warp 0      TMA producer: x tile [128 x 64] (128B swizzle, K-major), the
-//                 int4 weight tile [8 packed rows x 256 columns], scales and
-//                 zero points of the K block; 3-stage ring (full/empty mbarriers)
+//     warp 0      TMA producers: lane 0 the int4 weight tile [8 packed rows x
+//                 256 columns], scales and zero points of each K block (a
+//                 6-stage ring freed by the dequant warps), lane 1 the x tile
+//                 [128 x 64] (128B swizzle, K-major; a 4-stage ring freed by
+//                 the MMA commits)
 //     warp 1      TMEM allocation (256 columns: a 128 x 256 fp32 accumulator)
 //                 and, from one thread, tcgen05.mma kind::f16 (M=128, N=256,
 //                 K=16) on shared-memory descriptors; tcgen05.commit releases
-//                 the ring stages
+//                 the x and B stages
 //     warps 2-9   dequantise the weight tile into the K-major, 128B-swizzled fp16
-//                 B operand (3 stages): per packed word, PRMT + LOP3 put
+//                 B operand (2 stages): per packed word, PRMT + LOP3 put
 //                 (1024 + q_2i | 64 + q_2i+1) in a half2 (the nibble lands in
 //                 the mantissa of 1024 and, four bits up, of 64), HSUB2 removes
 //                 (1024 + z | 64 + z) exactly and HMUL2 applies the scale:
@@ -43,7 +45,22 @@ namespace qx {
 namespace gemm {
 
 constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int STAGES = 3;
+// Three rings, each as deep as its producer's latency needs: x tiles (the MMA
+// A operand, mostly L2 hits; a stage is freed by the MMA commit), packed
+// weights with their scales and zero points (from HBM; freed as soon as the
+// dequant warps have read them, so they run furthest ahead) and dequantised
+// B tiles (dequant warps -> MMA).  Measured with one ring of 3 stages for
+// x + weights and 3 for B: 666 TFLOP/s over the 7 Qwen3-8B shapes (2 stages:
+// 549): the weights' stage stayed busy until the MMA of its k-block retired.
+#ifndef QX_GEMM_XS
+#define QX_GEMM_XS 4
+#define QX_GEMM_WS 6
+#define QX_GEMM_BS 2
+#endif
+constexpr int XS = QX_GEMM_XS;  // x-tile stages
+constexpr int WS = QX_GEMM_WS;  // packed-weight stages
+constexpr int BS = QX_GEMM_BS;  // dequantised-B stages (>= 2: the LoRA B tile is staged raw in slot 1)
+static_assert(BS >= 2, "the raw LoRA B tile uses B slot 1");
 constexpr int THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 dequant + epilogue
 constexpr int DQ_WARPS = 8;
 constexpr int A_BYTES = BM * BK * 2;   // 16 KB
@@ -53,15 +70,18 @@ constexpr int SZ_BYTES = 2048;         // scales + zeros of up to 2 groups
 constexpr int MAX_RANK = 64;
 
 // shared-memory carve-up (bytes from a 1024-aligned base)
-constexpr int OFF_A = 0;
-constexpr int OFF_BF = OFF_A + STAGES * A_BYTES;
-constexpr int OFF_LH = OFF_BF + STAGES * BF_BYTES;  // LoRA h (hi | lo), 2 x 16 KB
-constexpr int OFF_WQ = OFF_LH + 2 * A_BYTES;
-constexpr int OFF_SZ = OFF_WQ + STAGES * WQ_BYTES;
-constexpr int OFF_BAR = OFF_SZ + STAGES * SZ_BYTES;
-constexpr int NBARS = 4 * STAGES + 2;  // full_a, empty_a, full_b, empty_b, tmem_full, lora
+constexpr int OFF_A = 0;                            // x tiles [XS]
+constexpr int OFF_BF = OFF_A + XS * A_BYTES;        // dequantised B [BS]
+constexpr int OFF_LH = OFF_BF + BS * BF_BYTES;      // LoRA h (hi | lo), 2 x 16 KB
+constexpr int OFF_WQ = OFF_LH + 2 * A_BYTES;        // packed weights [WS]
+constexpr int OFF_SZ = OFF_WQ + WS * WQ_BYTES;      // scales + zero points [WS]
+constexpr int OFF_BAR = OFF_SZ + WS * SZ_BYTES;
+// full_x, empty_x [XS], full_w, empty_w [WS], full_b, empty_b [BS], tmem_full, lora
+constexpr int NBARS = 2 * (XS + WS + BS) + 2;
 constexpr int OFF_TMEM = OFF_BAR + NBARS * 8;
 constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;  // + alignment slack
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory of the GEMM rings");
+static_assert(OFF_BF % 1024 == 0 && OFF_LH % 1024 == 0, "128B-swizzled operands on 1 KB boundaries");
 
 struct alignas(64) GemmParams {
   CUtensorMap tx;  // x fp16 [M][K], box {64, 128}, 128B swizzle
@@ -177,17 +197,24 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
   const int lora_items = R > 0 ? 1 : 0;
 
   const uint32_t sb = smem_u32(smem);
-  const uint32_t full_a = sb + OFF_BAR, empty_a = full_a + 8 * STAGES;
-  const uint32_t full_b = empty_a + 8 * STAGES, empty_b = full_b + 8 * STAGES;
-  const uint32_t tmem_full = empty_b + 8 * STAGES;
+  const uint32_t full_x = sb + OFF_BAR, empty_x = full_x + 8 * XS;
+  const uint32_t full_w = empty_x + 8 * XS, empty_w = full_w + 8 * WS;
+  const uint32_t full_b = empty_w + 8 * WS, empty_b = full_b + 8 * BS;
+  const uint32_t tmem_full = empty_b + 8 * BS;
   const uint32_t lora_full = tmem_full + 8;
   const int kp = ((R + 15) / 16) * 16;  // LoRA K extent of the MMAs
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
 
   if (warp == 0 && lane == 0) {
-    for (int i = 0; i < STAGES; ++i) {
-      bar_init(full_a + 8 * i, 1);
-      bar_init(empty_a + 8 * i, 1 + DQ_WARPS);  // MMA commit + the dequant warps
+    for (int i = 0; i < XS; ++i) {
+      bar_init(full_x + 8 * i, 1);
+      bar_init(empty_x + 8 * i, 1);  // MMA commit
+    }
+    for (int i = 0; i < WS; ++i) {
+      bar_init(full_w + 8 * i, 1);
+      bar_init(empty_w + 8 * i, DQ_WARPS);  // the dequant warps have read the stage
+    }
+    for (int i = 0; i < BS; ++i) {
       bar_init(full_b + 8 * i, DQ_WARPS);
       bar_init(empty_b + 8 * i, 1);
     }
@@ -207,27 +234,33 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  const int ab_bytes = A_BYTES + WQ_BYTES + p.grows * BN * 2 + p.grows * (p.zeros_packed ? BN / 2 : BN * 2);
+  const int w_bytes = WQ_BYTES + p.grows * BN * 2 + p.grows * (p.zeros_packed ? BN / 2 : BN * 2);
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      if (lora_items) {  // (alpha/r) h hi / lo tiles; the LoRA B tile [kp][256] (raw) into ring slot 1
+    // ------------------------------------------------------------ TMA producers
+    if (lane == 0) {  // packed weights, scales and zero points (released by the dequant warps)
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % WS;
+        if (kb >= WS) bar_wait(empty_w + 8 * s, ((kb / WS) - 1) & 1);
+        bar_expect(full_w + 8 * s, uint32_t(w_bytes));
+        tma2d_ef(sb + OFF_WQ + s * WQ_BYTES, &p.tw, n0 / 2, kb * 8, full_w + 8 * s);
+        const int grow = (kb * BK) / p.group;
+        unsigned char* sz = smem + OFF_SZ + s * SZ_BYTES;
+        tma2d(smem_u32(sz), &p.ts, n0, grow, full_w + 8 * s);
+        tma2d(smem_u32(sz + 1024), &p.tz, p.zeros_packed ? n0 / 8 : n0, grow, full_w + 8 * s);
+      }
+    } else if (lane == 1) {  // the LoRA tiles, then the x tiles (released by the MMA)
+      if (lora_items) {  // (alpha/r) h hi / lo tiles; the LoRA B tile [kp][256] (raw) into B slot 1
         bar_expect(lora_full, uint32_t(2 * A_BYTES + kp * BN * 2));
         tma2d(sb + OFF_LH, &p.th, 0, m0, lora_full);
         tma2d(sb + OFF_LH + A_BYTES, &p.th, 0, p.M + m0, lora_full);
         tma2d(sb + OFF_BF + BF_BYTES, &p.tb, n0, 0, lora_full);
       }
       for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % STAGES;
-        if (kb >= STAGES) bar_wait(empty_a + 8 * s, ((kb / STAGES) - 1) & 1);
-        bar_expect(full_a + 8 * s, uint32_t(ab_bytes));
-        tma2d(sb + OFF_A + s * A_BYTES, &p.tx, kb * BK, m0, full_a + 8 * s);
-        tma2d_ef(sb + OFF_WQ + s * WQ_BYTES, &p.tw, n0 / 2, kb * 8, full_a + 8 * s);
-        const int grow = (kb * BK) / p.group;
-        unsigned char* sz = smem + OFF_SZ + s * SZ_BYTES;
-        tma2d(smem_u32(sz), &p.ts, n0, grow, full_a + 8 * s);
-        tma2d(smem_u32(sz + 1024), &p.tz, p.zeros_packed ? n0 / 8 : n0, grow, full_a + 8 * s);
+        const int s = kb % XS;
+        if (kb >= XS) bar_wait(empty_x + 8 * s, ((kb / XS) - 1) & 1);
+        bar_expect(full_x + 8 * s, uint32_t(A_BYTES));
+        tma2d(sb + OFF_A + s * A_BYTES, &p.tx, kb * BK, m0, full_x + 8 * s);
       }
     }
   } else if (warp == 1) {
@@ -244,9 +277,9 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
         umma_commit(empty_b);
       }
       for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % STAGES, i = kb + lora_items, t = i % STAGES;
-        bar_wait(full_a + 8 * s, (kb / STAGES) & 1);
-        bar_wait(full_b + 8 * t, (i / STAGES) & 1);
+        const int s = kb % XS, i = kb + lora_items, t = i % BS;
+        bar_wait(full_x + 8 * s, (kb / XS) & 1);
+        bar_wait(full_b + 8 * t, (i / BS) & 1);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k)
@@ -254,7 +287,7 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
                kmajor_sw128_desc(sb + OFF_BF + t * BF_BYTES + k * 32),
                (lora_items | kb | k) != 0);
         umma_commit(empty_b + 8 * t);
-        umma_commit(empty_a + 8 * s);
+        umma_commit(empty_x + 8 * s);
       }
       umma_commit(tmem_full);
     }
@@ -280,9 +313,9 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
       if (lane == 0) bar_arrive(full_b);
     }
     for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % STAGES, i = kb + lora_items, t = i % STAGES;
-      if (i >= STAGES) bar_wait(empty_b + 8 * t, ((i / STAGES) - 1) & 1);
-      bar_wait(full_a + 8 * s, (kb / STAGES) & 1);
+      const int s = kb % WS, i = kb + lora_items, t = i % BS;
+      if (i >= BS) bar_wait(empty_b + 8 * t, ((i / BS) - 1) & 1);
+      bar_wait(full_w + 8 * s, (kb / WS) & 1);
       const uint32_t* wq = reinterpret_cast<const uint32_t*>(smem + OFF_WQ + s * WQ_BYTES);
       const unsigned char* sz = smem + OFF_SZ + s * SZ_BYTES;
       unsigned char* bf = smem + OFF_BF + t * BF_BYTES;
@@ -335,7 +368,7 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
       __syncwarp();
       if (lane == 0) {
         bar_arrive(full_b + 8 * t);
-        bar_arrive(empty_a + 8 * s);
+        bar_arrive(empty_w + 8 * s);
       }
     }
     // ------------------------------------------------------------ epilogue

@@ -121,7 +121,15 @@ struct alignas(64) Params {
   int stage;                    // bytes per ring stage: a group's packed weights, then its LoRA A rows
   uint32_t s_magic, cpr_magic;  // ceil(2^32 / S) (S > 1), ceil(2^32 / cpr): exact floor division of small values
   Layout lay;                   // shared-memory carve-up, computed on the host
+  unsigned long long* trace;    // profiling build only (qx_trace_launches): phase timestamps
+  int trace_launch;
 };
+
+// Trace slots of a GEMV CTA (profiling build): 0 entry, 1 dependency wait
+// passed, 2 first weight group landed, 3 weight loop done, 4 helper's LoRA
+// down-projection done, 5 LoRA up-projection done, 6 partials sent to the
+// owners, 7 partials received (owners), 8 exit (owners)
+enum GemvTrace { TR_ENTRY, TR_WAITED, TR_GROUP0, TR_LOOP, TR_LORA_DOWN, TR_LORA_UP, TR_SENT, TR_RECEIVED, TR_EXIT };
 
 
 __host__ __device__ inline unsigned take(unsigned& o, size_t bytes) {
@@ -361,6 +369,8 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   // The next kernel in the stream may launch as soon as every CTA of this one
   // is resident: it only streams its own weights until it waits for us.
   grid_dep_launch();
+  unsigned long long* const trc = trace_base(p.trace, p.trace_launch);
+  trace_stamp(trc, TR_ENTRY, tid == 0);
 
   if (warp == WARPS && lane == 0) {
     prefetch_tmap(&p.tw);
@@ -459,6 +469,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     // the activations may come from the previous kernel in the stream: wait
     // for it here, after every weight and static copy has been started
     if (p.pdl && !p.x_early) grid_dep_wait();
+    trace_stamp(trc, TR_WAITED, tid == 0);
     const __half* xg = p.x + k0;
     for (int id = warp; id < M * TB; id += WARPS + 1) {
       const int m = id / TB, it = (id - m * TB) * 32 + lane, t = it >> 2, cc = it & 3;
@@ -538,6 +549,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
       if (m0 + 1 < M) hs[(m0 + 1) * R + j0 + 8] = h4[0][3] + h4[1][3];
     }
     mbar_arrive(bar_h);  // every lane: its h_s stores are released
+    trace_stamp(trc, TR_LORA_DOWN, lane == 0);
     return;
   }
 
@@ -576,6 +588,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   const unsigned char* wlane = smem + L.ring + c * ROWB + lcol * 4;
   for (int gi = 0; gi < ngrp; ++gi) {
     mbar_wait(full0 + 8 * st, use & 1);
+    trace_stamp(trc, TR_GROUP0, tid == 0 && gi == 0);
 #pragma unroll
     for (int j = 0; j < KPG; ++j) {
       const int t = gi * KPG + j;
@@ -674,6 +687,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     }
   }
 
+  trace_stamp(trc, TR_LOOP, tid == 0);
   if (lora_warps) {  // the warps' LoRA tiles into h_s [M][r]
     float* hp = reinterpret_cast<float*>(smem + L.hs);
     const int RT8 = R >> 3, ntl = lora_tiles(M, R);
@@ -754,6 +768,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     }
   }
 
+  trace_stamp(trc, TR_LORA_UP, tid == 0);
   // host-resident activations were read before the dependency wait: the
   // previous kernel may still write the output (a previous call's y)
   if (p.pdl && p.x_early) grid_dep_wait();
@@ -777,9 +792,11 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     }
   }
 
+  trace_stamp(trc, TR_SENT, tid == 0);
   // this CTA's columns: wait for the S partials, sum in rank order, round
   if (own_cols > 0) {
     mbar_wait(bar_rv, 0);
+    trace_stamp(trc, TR_RECEIVED, tid == 0);
     const int cb = n_tile0 + s * CPR;
     if (p.act) {
       // SwiGLU: output j of the block pair (gate cols 16b..16b+7, up cols
@@ -796,6 +813,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
         }
         p.y[size_t(m) * N2 + (cb >> 1) + j] = __float2half_rn(silu_mul(round_h(gs), round_h(us)));
       }
+      trace_stamp(trc, TR_EXIT, tid == 0);
       return;
     }
     if (M == 1) {
@@ -804,6 +822,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
         for (int r2 = 0; r2 < S; ++r2) v += recv[r2 * CPR + cc];
         p.y[cb + cc] = __float2half_rn(v);
       }
+      trace_stamp(trc, TR_EXIT, tid == 0);
       return;
     }
     // the compute threads as (row, column) pairs: rpi rows per pass
@@ -819,6 +838,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
         }
       }
     }
+    trace_stamp(trc, TR_EXIT, tid == 0);
   }
 }
 
@@ -1046,6 +1066,7 @@ static int run(Params prm, cudaStream_t st) {
     if (g_params.size() >= PARAM_CACHE_MAX) g_params.clear();
     g_params.emplace(key, ParamEntry{prm, pl});
   }
+  prm.trace = trace_next(QX_TRACE_GEMV, &prm.trace_launch);
   return launch<NT, KPG, LW>(prm, pl, st);
 }
 
