@@ -19,7 +19,7 @@
 //                 and, from one thread, tcgen05.mma kind::f16 (M=128, N=256,
 //                 K=16) on shared-memory descriptors; tcgen05.commit releases
 //                 the x and B stages
-//     warps 2-9   dequantise the weight tile into the K-major, 128B-swizzled fp16
+//     warps 2-17  dequantise the weight tile into the K-major, 128B-swizzled fp16
 //                 B operand (2 stages): per packed word, PRMT + LOP3 put
 //                 (1024 + q_2i | 64 + q_2i+1) in a half2 (the nibble lands in
 //                 the mantissa of 1024 and, four bits up, of 64), HSUB2 removes
@@ -29,7 +29,7 @@
 //                 (tcgen05.ld 32x32b, fp32 -> fp16, 16-byte stores)
 //   The LoRA term enters the same accumulator first: A = the high and low
 //   parts of (alpha/r) h (two MMAs, ~22-bit product) and the LoRA B tile, both
-//   by TMA before the weight stream; warps 2-9 transpose the B tile into the
+//   by TMA before the weight stream; the dequant warps transpose the B tile into the
 //   K-major swizzled layout in shared memory.
 // Every wait is bounded (2 s, then QX_DEVERR_MBAR_TIMEOUT in the device
 // error word); every copy targets this CTA only.
@@ -61,8 +61,18 @@ constexpr int XS = QX_GEMM_XS;  // x-tile stages
 constexpr int WS = QX_GEMM_WS;  // packed-weight stages
 constexpr int BS = QX_GEMM_BS;  // dequantised-B stages (>= 2: the LoRA B tile is staged raw in slot 1)
 static_assert(BS >= 2, "the raw LoRA B tile uses B slot 1");
-constexpr int THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 dequant + epilogue
-constexpr int DQ_WARPS = 8;
+// Dequantisation is the kernel's issue-bound part (per 8 weights: LDS, 4 x
+// PRMT/LOP3/HSUB2/HMUL2, STS): 16 warps (two threads per tile column, each
+// half of the K block's packed rows) give every scheduler four warps of
+// independent chains (measured with 8 warps: 44 % issue-active, the top
+// stall a fixed-latency dependency).
+#ifndef QX_GEMM_DQ_WARPS
+#define QX_GEMM_DQ_WARPS 16
+#endif
+constexpr int DQ_WARPS = QX_GEMM_DQ_WARPS;
+constexpr int DQ_PARTS = DQ_WARPS / 8;           // threads per tile column
+constexpr int THREADS = 64 + DQ_WARPS * 32;      // warp 0 TMA, warp 1 MMA, warps 2.. dequant + epilogue
+static_assert(DQ_WARPS == 8 || DQ_WARPS == 16, "8 or 16 dequant warps");
 constexpr int A_BYTES = BM * BK * 2;   // 16 KB
 constexpr int BF_BYTES = BN * BK * 2;  // 32 KB
 constexpr int WQ_BYTES = 8 * BN * 4;   // 8 KB
@@ -293,14 +303,17 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
     }
   } else {
     // ------------------------------------------------------------ dequant warps
-    const int dt = tid - 64;  // 0..255: the tile column this thread dequantises
+    const int dt = (tid - 64) & (BN - 1);  // the tile column this thread dequantises
+    const int part = (tid - 64) >> 8;       // which packed rows of the K block: [part * PPR, + PPR)
+    constexpr int PPR = 8 / DQ_PARTS;
     if (lora_items) {  // transpose the raw LoRA B tile (ring slot 1) into K-major ring slot 0
       if (lane == 0) bar_wait(lora_full, 0);
       __syncwarp();
       bar_wait(lora_full, 0);
       const __half* braw = reinterpret_cast<const __half*>(smem + OFF_BF + BF_BYTES);
       unsigned char* bf = smem + OFF_BF;
-      for (int ch = 0; ch < kp / 8; ++ch) {
+      const int nch = kp / 8 / DQ_PARTS;  // 16-byte chunks of the column per thread
+      for (int ch = part * nch; ch < (part + 1) * nch; ++ch) {
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e)
@@ -309,7 +322,7 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
         *reinterpret_cast<uint4*>(bf + dt * 128 + ((ch ^ (dt & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      asm volatile("bar.sync 1, 256;" ::: "memory");  // every warp is done reading slot 1
+      asm volatile("bar.sync 1, %0;" ::"n"(DQ_WARPS * 32) : "memory");  // every warp is done reading slot 1
       if (lane == 0) bar_arrive(full_b);
     }
     for (int kb = 0; kb < KB; ++kb) {
@@ -338,7 +351,8 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
       }
       if (p.zeros_packed) {  // integer zero points: exact half2 arithmetic
 #pragma unroll
-        for (int pr = 0; pr < 8; ++pr) {
+        for (int r = 0; r < PPR; ++r) {
+          const int pr = part * PPR + r;
           const uint32_t v = wq[pr * BN + dt];
           const int gl = p.grows > 1 ? (pr * 8) / p.group : 0;  // groups of 32: two per K block
           const uint32_t z2 = gl ? zz[1] : zz[0], s2 = gl ? ss[1] : ss[0];
@@ -347,7 +361,8 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
           *reinterpret_cast<uint4*>(bf + dt * 128 + ((pr ^ (dt & 7)) << 4)) = o;
         }
       } else {  // fp16 zero points may be fractional: fp16((q - z) * s) in fp32, as the oracle
-        for (int pr = 0; pr < 8; ++pr) {
+        for (int r = 0; r < PPR; ++r) {
+          const int pr = part * PPR + r;
           const uint32_t v = wq[pr * BN + dt];
           const int gl = p.grows > 1 ? (pr * 8) / p.group : 0;
           const float sf = __half2float(reinterpret_cast<const __half*>(sz)[gl * BN + dt]);
@@ -376,10 +391,11 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
     __syncwarp();
     bar_wait(tmem_full, 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int q = warp & 3, chalf = (warp - 2) >> 2;  // TMEM lane quarter, column half
+    constexpr int CW = BN / (DQ_WARPS / 4);  // columns per warp
+    const int q = warp & 3, cpart = (warp - 2) >> 2;  // TMEM lane quarter, column block
     const int row = q * 32 + lane, m = m0 + row;
-    for (int cb = 0; cb < 4; ++cb) {
-      const int col = chalf * 128 + cb * 32;
+    for (int cb = 0; cb < CW / 32; ++cb) {
+      const int col = cpart * CW + cb * 32;
       uint32_t r[32];
       const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(col);
       asm volatile(
