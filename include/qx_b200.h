@@ -112,6 +112,25 @@ int qx_w4a16_lora_gemv_swiglu(const void* x, const int32_t* qweight, const void*
                               int M, int K, int N, int rank, int group_size, float lora_scale,
                               qx_stream_t stream);
 
+/* The decode step's residual add + RMSNorm as the GEMV's prologue (one launch
+ * instead of qx_add_rmsnorm + the GEMV): every CTA forms r = fp16(residual +
+ * delta) over whole rows, x = fp16((r * rsqrt(mean(r^2) + eps)) * norm_weight)
+ * with the rounding of qx_add_rmsnorm, and runs the GEMV (swiglu = 1: the
+ * SwiGLU form of qx_w4a16_lora_gemv_swiglu) on x; r is written to
+ * residual_out (the new residual stream).  residual / delta / residual_out fp16
+ * [M, K], norm_weight fp16 [K]; M <= 8 rows (each CTA reads the whole rows);
+ * residual_out must not overlap residual or delta (callers alternate two
+ * residual buffers).  Matches qx_add_rmsnorm followed by the GEMV up to the
+ * order of the sum of squares.  Replaces the patched layer's RMSNorm
+ * (qextract/patch.py:73-87) together with the residual add that the HF decoder
+ * layer runs before it, ahead of the MLP / attention projections. */
+int qx_w4a16_lora_gemv_addnorm(const void* residual, const void* delta, const void* norm_weight,
+                               float eps, void* residual_out, const int32_t* qweight,
+                               const void* scales, const void* zeros, int zeros_packed,
+                               int zero_offset, const void* lora_A, const void* lora_B, void* y,
+                               int M, int K, int N, int rank, int group_size, float lora_scale,
+                               int swiglu, qx_stream_t stream);
+
 /* Programmatic dependent launch for the GEMV (on by default; 0 turns it
  * off).  When on, a GEMV launches as soon as every CTA of the GEMV before it
  * in the stream is running: it streams its weights and stages scales /

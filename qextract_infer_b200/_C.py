@@ -395,6 +395,39 @@ def _w4a16_swiglu(input, qweight, scales, zeros, lora_A, lora_B, group_size, lor
     return out
 
 
+def _w4a16_addnorm(residual, delta, norm_weight, eps, residual_out, qweight, scales, zeros, lora_A, lora_B,
+                   group_size, lora_scale, zero_offset, swiglu: bool = False):
+    """The decode step's residual add + RMSNorm fused into the projection that
+    follows (``qx_w4a16_lora_gemv_addnorm``): ``residual_out = fp16(residual +
+    delta)``, ``x = rmsnorm(residual_out) * norm_weight`` and returns the
+    W4A16-LoRA projection of x (``swiglu``: the SwiGLU form over interleaved
+    gate|up operands, ``[M, N / 2]``).  Up to 8 rows; ``residual_out`` is a
+    separate buffer (callers alternate two)."""
+    w = _weights(qweight, scales, zeros, lora_A, lora_B, group_size, zero_offset)
+    for t, n in ((residual, "residual"), (delta, "delta"), (norm_weight, "norm_weight"),
+                 (residual_out, "residual_out")):
+        _check_input(t, n)
+        _check_fp16(t, n)
+    K, N = w.K, w.N
+    if residual.size(-1) != K or residual.shape != delta.shape or residual.shape != residual_out.shape \
+            or norm_weight.numel() != K:
+        raise RuntimeError(f"w4a16_lora_gemv_addnorm: residual, delta and residual_out must be [M, {K}], "
+                           f"norm_weight [{K}]")
+    di = residual.get_device()
+    if di != w.dev:
+        raise RuntimeError(f"residual is on cuda:{di} but the weights are on cuda:{w.dev}")
+    lead = residual.shape[:-1]
+    M = residual.numel() // K
+    out = torch.empty(lead + ((N // 2) if swiglu else N,), dtype=torch.float16, device=residual.device)
+    rc = _LIB.qx_w4a16_lora_gemv_addnorm(residual.data_ptr(), delta.data_ptr(), norm_weight.data_ptr(),
+                                         float(eps), residual_out.data_ptr(), *w.args, out.data_ptr(), M, K, N,
+                                         w.rank, w.group, lora_scale, 1 if swiglu else 0,
+                                         _raw_stream(residual.device))
+    if rc < 0:
+        _lib.check(rc, "w4a16_gemv_addnorm")
+    return out
+
+
 def w4a16_lora_gemv_swiglu(input, qweight, scales, zeros, lora_A, lora_B, group_size: int = 128,
                            lora_alpha: float = 16.0, *, zero_offset: int = 0):
     """``fused_swiglu(gate, up)`` of one W4A16-LoRA gate|up projection whose

@@ -31,6 +31,9 @@ SIGNATURES = {
     "qx_w4a16_lora_gemv_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                           c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                           c_int, c_float, c_void_p]),
+    "qx_w4a16_lora_gemv_addnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
+                                           c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                           c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_void_p]),
     "qx_set_pdl": (c_int, [c_int]),
     "qx_w4a16_lora_gemv_host": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_int,

@@ -90,7 +90,7 @@ constexpr int ROWB = 1056;               // smem bytes per staged packed row (1 
 constexpr int MAX_NST = 4;               // weight stages (quantisation groups) in flight per CTA
 constexpr int MROWS = 32;                // batch rows per launch (4 n-tiles of 8)
 constexpr int MAX_S = 16;                // largest cluster (non-portable size)
-constexpr size_t SMEM_LIMIT = 227 * 1024;
+constexpr size_t SMEM_LIMIT = 226 * 1024;  // dynamic; 1 KB left for the static arrays
 
 __host__ __device__ constexpr int ctas_per_sm(int nt) { return nt == 1 ? 3 : (nt == 2 ? 2 : 1); }
 
@@ -118,6 +118,15 @@ struct alignas(64) Params {
   int act;                      // 1: SwiGLU epilogue over column blocks (8 gate, 8 up), y [M][N/2]
   int x_early;                  // x is not written by the previous kernel (host rows): read it
                                 // before the dependency wait, wait before the output stores
+  // residual add + RMSNorm prologue (qx_w4a16_lora_gemv_addnorm, up to 8 rows):
+  // x = fp16((r rsqrt(mean(r^2) + eps)) w) with r = fp16(res + delta) over the
+  // whole row; the CTAs of tile 0 write r (their K ranges) to res_out
+  int addnorm;
+  const __half* res;
+  const __half* delta;
+  const __half* nw;
+  __half* res_out;
+  float eps;
   int stage;                    // bytes per ring stage: a group's packed weights, then its LoRA A rows
   uint32_t s_magic, cpr_magic;  // ceil(2^32 / S) (S > 1), ceil(2^32 / cpr): exact floor division of small values
   Layout lay;                   // shared-memory carve-up, computed on the host
@@ -327,6 +336,8 @@ template <int NT, int KPG, bool LW>
 __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     w4a16_gemv_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ float s_ss[WARPS + 1][8];  // addnorm: per-warp sums of squares of the rows
+  __shared__ float s_rs[8];         // addnorm: rsqrt(mean(r^2) + eps) per row
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -470,13 +481,69 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
     // for it here, after every weight and static copy has been started
     if (p.pdl && !p.x_early) grid_dep_wait();
     trace_stamp(trc, TR_WAITED, tid == 0);
+    if (p.addnorm) {
+      // the residual add over whole rows (the norm needs every column), sums
+      // of squares in fp32; r of this CTA's K range goes to xraw (normalised
+      // in place below), and tile 0's CTAs store it as the new residual
+      const int K8 = p.K >> 3;
+      for (int m = 0; m < M; ++m) {
+        float acc = 0.f;
+        for (int cix = tid; cix < K8; cix += THREADS) {
+          // plain loads: the previous kernels wrote these rows
+          const uint4 a = *reinterpret_cast<const uint4*>(p.res + size_t(m) * p.K + cix * 8);
+          const uint4 b = *reinterpret_cast<const uint4*>(p.delta + size_t(m) * p.K + cix * 8);
+          const uint32_t ad[4] = {a.x, a.y, a.z, a.w}, bd[4] = {b.x, b.y, b.z, b.w};
+          uint32_t od[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 fa = h2_to_f2(ad[j]), fb = h2_to_f2(bd[j]);
+            const __half2 s2 = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);  // the fp16 residual add
+            od[j] = *reinterpret_cast<const uint32_t*>(&s2);
+            const float2 f = __half22float2(s2);
+            acc = fmaf(f.x, f.x, acc);
+            acc = fmaf(f.y, f.y, acc);
+          }
+          const int kl = cix * 8 - k0;
+          if (kl >= 0 && kl < Ks) {
+            const uint4 r8 = make_uint4(od[0], od[1], od[2], od[3]);
+            *reinterpret_cast<uint4*>(xraw + m * XS + kl) = r8;
+            if (tile == 0) *reinterpret_cast<uint4*>(p.res_out + size_t(m) * p.K + cix * 8) = r8;
+          }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) s_ss[warp][m] = acc;
+      }
+      __syncthreads();  // every warp of the CTA stages (the helper warp too)
+      if (tid < M) {
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w <= WARPS; ++w) t += s_ss[w][tid];
+        s_rs[tid] = 1.0f / sqrtf(t * (1.0f / float(p.K)) + p.eps);
+      }
+      __syncthreads();
+    }
     const __half* xg = p.x + k0;
     for (int id = warp; id < M * TB; id += WARPS + 1) {
       const int m = id / TB, it = (id - m * TB) * 32 + lane, t = it >> 2, cc = it & 3;
       const bool ok = it < Ts * 4;  // Ts * 4 is a multiple of 4 * KPG: groups never straddle
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (ok) {
-        v = *reinterpret_cast<const uint4*>(xg + size_t(m) * p.K + t * KSTEP + cc * 8);
+        if (p.addnorm) {  // x = fp16((r * rs) * w) from the staged r, as qx_add_rmsnorm rounds it
+          const uint4 r8 = *reinterpret_cast<const uint4*>(xraw + m * XS + t * KSTEP + cc * 8);
+          const uint4 w8 = ldg_v4(p.nw + k0 + t * KSTEP + cc * 8);
+          const uint32_t rd[4] = {r8.x, r8.y, r8.z, r8.w}, wd[4] = {w8.x, w8.y, w8.z, w8.w};
+          const float rs = s_rs[m];
+          uint32_t od[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = h2_to_f2(rd[j]), gw = h2_to_f2(wd[j]);
+            const __half2 o = __floats2half2_rn((f.x * rs) * gw.x, (f.y * rs) * gw.y);
+            od[j] = *reinterpret_cast<const uint32_t*>(&o);
+          }
+          v = make_uint4(od[0], od[1], od[2], od[3]);
+        } else {
+          v = *reinterpret_cast<const uint4*>(xg + size_t(m) * p.K + t * KSTEP + cc * 8);
+        }
         *reinterpret_cast<uint4*>(xraw + m * XS + t * KSTEP + cc * 8) = v;  // natural order, LoRA-down
         xsw[(t * M + m) * 4 + cc] = make_uint4(prmt(v.x, v.z, 0x5410u), prmt(v.x, v.z, 0x7632u),
                                                 prmt(v.y, v.w, 0x5410u), prmt(v.y, v.w, 0x7632u));
@@ -1042,19 +1109,24 @@ static int run(Params prm, cudaStream_t st) {
   uint32_t ls_bits;
   std::memcpy(&ls_bits, &prm.lora_scale, 4);
   const ParamKey key{prm.qw, prm.scales, prm.zeros, prm.A, prm.B, dev, prm.M, prm.K, prm.N, prm.rank,
-                     prm.group, prm.zeros_packed, prm.zero_offset, prm.pdl + 2 * prm.act + 4 * prm.x_early, NT, KPG * 2 + (LW ? 1 : 0),
+                     prm.group, prm.zeros_packed, prm.zero_offset,
+                     prm.pdl + 2 * prm.act + 4 * prm.x_early + 8 * prm.addnorm, NT, KPG * 2 + (LW ? 1 : 0),
                      ls_bits};
   Plan pl;
   bool hit = false;
   {
     std::lock_guard<std::mutex> lk(g_param_mu);
     auto it = g_params.find(key);
-    if (it != g_params.end()) {
-      const __half* x = prm.x;
-      __half* y = prm.y;
+    if (it != g_params.end()) {  // the cached plan and maps; this call's rows and output
+      const Params call = prm;
       prm = it->second.prm;
-      prm.x = x;
-      prm.y = y;
+      prm.x = call.x;
+      prm.y = call.y;
+      prm.res = call.res;
+      prm.delta = call.delta;
+      prm.nw = call.nw;
+      prm.res_out = call.res_out;
+      prm.eps = call.eps;
       pl = it->second.pl;
       hit = true;
     }
@@ -1204,10 +1276,22 @@ static void* device_view(const void* host) {
 }  // namespace gemv
 }  // namespace qx
 
+namespace qx {
+namespace gemv {
+struct AddNorm {  // the residual add + RMSNorm prologue's operands
+  const void* res;
+  const void* delta;
+  const void* nw;
+  void* res_out;
+  float eps;
+};
+}  // namespace gemv
+}  // namespace qx
+
 static int w4a16_gemv_entry(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
                             int zeros_packed, int zero_offset, const void* lora_A, const void* lora_B, void* y,
                             int M, int K, int N, int rank, int group_size, float lora_scale,
-                            qx_stream_t stream, int act, int x_early);
+                            qx_stream_t stream, int act, int x_early, const gemv::AddNorm* an = nullptr);
 
 extern "C" int qx_w4a16_lora_gemv_host(const void* x_host, void* y_host, void* x_dev, void* y_dev,
                                        const int32_t* qweight, const void* scales, const void* zeros,
@@ -1309,7 +1393,7 @@ static int w4a16_gemv_entry(const void* x, const int32_t* qweight, const void* s
                                   const void* zeros, int zeros_packed, int zero_offset,
                                   const void* lora_A, const void* lora_B, void* y, int M, int K,
                                   int N, int rank, int group_size, float lora_scale,
-                                  qx_stream_t stream, int act, int x_early) {
+                                  qx_stream_t stream, int act, int x_early, const gemv::AddNorm* an) {
   QX_REQUIRE(M >= 0 && K > 0 && N > 0, "w4a16_gemv: bad sizes M=%d K=%d N=%d", M, K, N);
   if (M == 0) return QX_OK;
   QX_REQUIRE(K % gemv::KSTEP == 0, "w4a16_gemv: K=%d must be a multiple of 32", K);
@@ -1354,6 +1438,14 @@ static int w4a16_gemv_entry(const void* x, const int32_t* qweight, const void* s
     prm.pdl = g_pdl_enabled.load(std::memory_order_relaxed);
     prm.act = act;
     prm.x_early = x_early;
+    if (an) {  // a single launch (the host keeps M <= 8)
+      prm.addnorm = 1;
+      prm.res = static_cast<const __half*>(an->res);
+      prm.delta = static_cast<const __half*>(an->delta);
+      prm.nw = static_cast<const __half*>(an->nw);
+      prm.res_out = static_cast<__half*>(an->res_out);
+      prm.eps = an->eps;
+    }
     const int rc = gemv::dispatch(prm, group_size / gemv::KSTEP, st);
     if (rc == QX_ERR_UNSUPPORTED && mc > 8) {
       mrows = mc > 16 ? 16 : 8;
@@ -1372,6 +1464,34 @@ extern "C" int qx_w4a16_lora_gemv(const void* x, const int32_t* qweight, const v
                                   qx_stream_t stream) {
   return w4a16_gemv_entry(x, qweight, scales, zeros, zeros_packed, zero_offset, lora_A, lora_B, y, M, K, N,
                           rank, group_size, lora_scale, stream, 0, 0);
+}
+
+extern "C" int qx_w4a16_lora_gemv_addnorm(const void* residual, const void* delta, const void* norm_weight,
+                                          float eps, void* residual_out, const int32_t* qweight,
+                                          const void* scales, const void* zeros, int zeros_packed,
+                                          int zero_offset, const void* lora_A, const void* lora_B, void* y,
+                                          int M, int K, int N, int rank, int group_size, float lora_scale,
+                                          int swiglu, qx_stream_t stream) {
+  QX_REQUIRE(M >= 0 && M <= 8, "w4a16_gemv_addnorm: M=%d rows (1..8)", M);
+  QX_REQUIRE(K > 0 && K % 8 == 0, "w4a16_gemv_addnorm: K=%d must be a multiple of 8", K);
+  QX_REQUIRE(swiglu == 0 || swiglu == 1, "w4a16_gemv_addnorm: swiglu must be 0 or 1");
+  QX_REQUIRE(!swiglu || (N > 0 && N % 16 == 0), "w4a16_gemv_addnorm: N=%d must be a multiple of 16 with SwiGLU",
+             N);
+  QX_REQUIRE(residual && delta && norm_weight && residual_out, "w4a16_gemv_addnorm: null pointer");
+  QX_REQUIRE(aligned(residual, 16) && aligned(delta, 16) && aligned(norm_weight, 16) && aligned(residual_out, 16),
+             "w4a16_gemv_addnorm: residual, delta, norm_weight and residual_out must be 16-byte aligned");
+  const size_t rb = size_t(M) * K * 2;
+  const uintptr_t o0 = reinterpret_cast<uintptr_t>(residual_out);
+  auto overlaps = [&](const void* t) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(t);
+    return a < o0 + rb && o0 < a + rb;
+  };
+  QX_REQUIRE(!overlaps(residual) && !overlaps(delta),
+             "w4a16_gemv_addnorm: residual_out must not overlap residual or delta (other CTAs still read them)");
+  if (M == 0) return QX_OK;
+  const gemv::AddNorm an{residual, delta, norm_weight, residual_out, eps};
+  return w4a16_gemv_entry(residual, qweight, scales, zeros, zeros_packed, zero_offset, lora_A, lora_B, y, M, K,
+                          N, rank, group_size, lora_scale, stream, swiglu, 0, &an);
 }
 
 extern "C" int qx_w4a16_lora_gemv_swiglu(const void* x, const int32_t* qweight, const void* scales,

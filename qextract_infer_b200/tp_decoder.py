@@ -137,6 +137,13 @@ class FusedQuantLinear:
         return _C._w4a16(x, self.qweight, self.scales, self.qzeros, self.lora_A, self.lora_B,
                          self.group, self.lora_scale, 0)
 
+    def addnorm(self, res: torch.Tensor, delta: torch.Tensor, norm_w: torch.Tensor, eps: float,
+                res_out: torch.Tensor, swiglu: bool = False) -> torch.Tensor:
+        """``res_out = res + delta``, then this projection (its SwiGLU form with
+        ``swiglu``) of ``rmsnorm(res_out) * norm_w``: one launch (decode rows)."""
+        return _C._w4a16_addnorm(res, delta, norm_w, eps, res_out, self.qweight, self.scales, self.qzeros,
+                                 self.lora_A, self.lora_B, self.group, self.lora_scale, 0, swiglu)
+
     def interleave_gate_up(self) -> "FusedQuantLinear":
         """Reorders a fused [gate | up] pair into blocks of 8 gate and 8 up
         columns (``_C.interleave_gate_up``) for ``swiglu``; ``__call__`` then
@@ -271,11 +278,21 @@ class TPDecoder:
         eps = cfg.rms_eps
         pos = self.cache.get_total_written()
         cos, sin = self.cos[pos], self.sin[pos]
-        x = self.embed.index_select(0, tokens)  # [B, H], updated in place below
+        x = self.embed.index_select(0, tokens)  # [B, H], the residual stream
         h = _C.fused_rmsnorm(x, self.layers[0]["in_norm"], eps)
         n = len(self.layers)
+        # one GPU and a few rows: the residual add + RMSNorm before the MLP and
+        # before the next layer's q|k|v run as those projections' prologue (5
+        # launches per layer); the residual alternates between two buffers
+        fuse = self.world == 1 and B <= 8
+        xo = torch.empty_like(x) if fuse else None
+        dn = None
         for li, L in enumerate(self.layers):
-            qkv = L["qkv"](h)
+            if fuse and li > 0:
+                qkv = L["qkv"].addnorm(x, dn, L["in_norm"], eps, xo)  # x + down of the layer before
+                x, xo = xo, x
+            else:
+                qkv = L["qkv"](h)
             if self.fused_attention:
                 att = _C.decode_attention_qkv(qkv, self.hq, self.hkv, L["q_norm"], L["k_norm"], eps,
                                               cos, sin, self.cache.k[li], self.cache.v[li], cfg.sink,
@@ -286,7 +303,15 @@ class TPDecoder:
                                            pos)
                 att = _C.decode_attention(q, self.cache.k[li], self.cache.v[li], pos + 1, cfg.sink,
                                           cfg.window, after_append=True)
-            h = self._reduce_add_norm(L["o"](att.view(B, self.hq * D)), x, L["post_norm"])  # x += o
+            o = L["o"](att.view(B, self.hq * D))
+            if fuse:
+                gu = L["gate_up"].addnorm(x, o, L["post_norm"], eps, xo, swiglu=True)  # x + o
+                x, xo = xo, x
+                dn = L["down"](gu)
+                if li + 1 == n:
+                    h = _C.add_rmsnorm(x, dn, self.final_norm, eps)  # x += down; the final RMSNorm
+                continue
+            h = self._reduce_add_norm(o, x, L["post_norm"])  # x += o
             dn = L["down"](L["gate_up"].swiglu(h))
             nxt_w = self.layers[li + 1]["in_norm"] if li + 1 < n else self.final_norm
             h = self._reduce_add_norm(dn, x, nxt_w)  # x += down; the next RMSNorm

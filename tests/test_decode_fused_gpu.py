@@ -1,5 +1,6 @@
 """Fused decode-step kernels against the unfused operator sequence they
-replace: residual add + RMSNorm and packed SwiGLU bit-exact; q/k head norm +
+replace: residual add + RMSNorm and packed SwiGLU bit-exact; the GEMV with the
+residual add + RMSNorm prologue against add + norm + GEMV; q/k head norm +
 RoPE + ring append against the head-norm kernel followed by the fp32 torch
 rotation (within one fp16 ulp: the two sum-of-squares reductions run in
 different orders)."""
@@ -134,3 +135,59 @@ def test_attention_qkv_equals_append_then_attention(C, B, hq, hkv, pos):
         assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
         assert torch.equal(k2.view(torch.int16), k1.view(torch.int16))
         assert torch.equal(v2.view(torch.int16), v1.view(torch.int16))
+
+
+def _quant_linear(K, N, r, seed):
+    g = _g(seed)
+    qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), generator=g, device="cuda", dtype=torch.int32)
+    sc = (torch.rand(K // 128, N, generator=g, device="cuda") * 0.015 + 0.005).half()
+    qz = torch.full((K // 128, N // 8), 0x88888888 - 2 ** 32, dtype=torch.int32, device="cuda")
+    A = (torch.randn(K, r, generator=g, device="cuda") * 0.02).half()
+    B = (torch.randn(r, N, generator=g, device="cuda") * 0.02).half()
+    return qw, sc, qz, A, B
+
+
+@pytest.mark.parametrize("M,K,N,r,swiglu", [(1, 4096, 6144, 48, False), (1, 4096, 24576, 32, True),
+                                             (4, 2560, 9728, 16, False), (8, 4096, 4096, 16, True),
+                                             (3, 1024, 512, 0, False)])
+def test_gemv_addnorm_matches_add_rmsnorm_then_gemv(C, M, K, N, r, swiglu):
+    """The GEMV with the residual add + RMSNorm prologue against qx_add_rmsnorm
+    followed by the GEMV (the new residual bit-exact; the output within the
+    GEMV tolerance, rtol = atol = 1e-2: the two sums of squares run in
+    different orders), on two calls in a row with the residual buffers
+    swapped, as the decode step alternates them."""
+    qw, sc, qz, A, B = _quant_linear(K, N, max(r, 8), seed=M + K + N)
+    if r == 0:
+        A = B = None
+    w = (1 + 0.1 * torch.randn(K, generator=_g(3), device="cuda")).half()
+    res = torch.randn(M, K, generator=_g(4), device="cuda").half()
+    out_buf = torch.full_like(res, float("nan"))
+    for call in range(2):
+        d = torch.randn(M, K, generator=_g(10 + call), device="cuda").half()
+        x_ref = res.clone()
+        h = C.add_rmsnorm(x_ref, d, w, 1e-6)
+        scale = 2.0 if r else 0.0
+        if swiglu:
+            y_ref = C._w4a16_swiglu(h, qw, sc, qz, A, B, 128, scale, 0)
+        else:
+            y_ref = C._w4a16(h, qw, sc, qz, A, B, 128, scale, 0)
+        y = C._w4a16_addnorm(res, d, w, 1e-6, out_buf, qw, sc, qz, A, B, 128, scale, 0, swiglu)
+        torch.cuda.synchronize()
+        assert torch.equal(out_buf.view(torch.int16), x_ref.view(torch.int16)), f"call {call}: new residual"
+        assert y.shape == y_ref.shape
+        err = (y.float() - y_ref.float()).abs()
+        bound = 1e-2 + 1e-2 * y_ref.float().abs()
+        assert bool((err <= bound).all()), f"call {call}: max err {err.max().item()}"
+        res, out_buf = out_buf, res  # the residual alternates between the two buffers
+
+
+def test_gemv_addnorm_rejects_aliased_residual(C):
+    from qextract_infer_b200 import _lib
+    qw, sc, qz, A, B = _quant_linear(512, 256, 16, seed=1)
+    w = torch.ones(512, dtype=torch.float16, device="cuda")
+    res = torch.randn(2, 512, device="cuda").half()
+    with pytest.raises(_lib.QXError, match="overlap"):
+        C._w4a16_addnorm(res, res.clone(), w, 1e-6, res, qw, sc, qz, A, B, 128, 2.0, 0)
+    with pytest.raises(_lib.QXError, match="rows"):
+        big = torch.randn(9, 512, device="cuda").half()
+        C._w4a16_addnorm(big, big.clone(), w, 1e-6, torch.empty_like(big), qw, sc, qz, A, B, 128, 2.0, 0)
