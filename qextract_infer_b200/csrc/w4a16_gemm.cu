@@ -441,6 +441,7 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_gemm_kernel(const __grid_con
 // scaled result as fp16 high parts hl[m][0..63] and low parts hl[M + m][0..63]
 // (ranks r..63 zero), the tiles the GEMM's LoRA MMAs read.
 constexpr int LS_ROWS = 128, LS_K = 32, LS_THREADS = 256;
+constexpr int LS_STAGES = 3;  // x / A tiles in flight per CTA (two steps ahead of the MMAs)
 
 __host__ __device__ inline int lora_splits(int M) {  // K splits: about two CTAs per SM of 148
   const int rb = (M + LS_ROWS - 1) / LS_ROWS;
@@ -458,8 +459,8 @@ __global__ void __launch_bounds__(LS_THREADS) lora_down_split_kernel(const __hal
                                                                      const __half* __restrict__ A,
                                                                      float* __restrict__ part, int M,
                                                                      int K, int R, int kchunk) {
-  __shared__ __align__(128) __half xs[2][LS_ROWS][LS_K + 8];
-  __shared__ __align__(128) __half as[2][LS_K][MAX_RANK + 8];
+  __shared__ __align__(128) __half xs[LS_STAGES][LS_ROWS][LS_K + 8];
+  __shared__ __align__(128) __half as[LS_STAGES][LS_K][MAX_RANK + 8];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
   const int r0 = blockIdx.x * LS_ROWS;
@@ -481,16 +482,20 @@ __global__ void __launch_bounds__(LS_THREADS) lora_down_split_kernel(const __hal
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  if (nsteps > 0) load(0, 0);
+  // LS_STAGES - 1 steps in flight ahead of the one computed (an empty commit
+  // group where no step is left, so the wait count stays fixed)
+#pragma unroll
+  for (int sp = 0; sp < LS_STAGES - 1; ++sp) {
+    if (sp < nsteps) load(sp, sp);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   for (int st = 0; st < nsteps; ++st) {
-    if (st + 1 < nsteps) {
-      load(st + 1, (st + 1) & 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    }
+    const int nx = st + LS_STAGES - 1;
+    if (nx < nsteps) load(nx, nx % LS_STAGES);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group %0;" ::"n"(LS_STAGES - 1) : "memory");  // step st landed
     __syncthreads();
-    const int b = st & 1;
+    const int b = st % LS_STAGES;
 #pragma unroll
     for (int kk = 0; kk < LS_K; kk += 16) {
       uint32_t a[4];
