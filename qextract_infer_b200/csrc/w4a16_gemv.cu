@@ -317,11 +317,12 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
 }
 // st.async of two floats into a peer CTA's shared memory; completion counted
 // in bytes on the peer's mbarrier (both addresses already mapped with mapa)
-__device__ __forceinline__ void st_async_f2(uint32_t raddr, float a, float b, uint32_t rbar) {
+__device__ __forceinline__ void st_async_f4(uint32_t raddr, float a, float b, float c, float d,
+                                            uint32_t rbar) {
   asm volatile(
-      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
           raddr),
-      "f"(a), "f"(b), "r"(rbar)
+      "f"(a), "f"(b), "f"(c), "f"(d), "r"(rbar)
       : "memory");
 }
 __device__ __forceinline__ uint32_t map_rank(uint32_t addr, int rank) {
@@ -523,6 +524,24 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
       __syncthreads();
     }
     const __half* xg = p.x + k0;
+    // more than one 512-byte chunk per warp (wide batches): every chunk's
+    // global read is issued at once (cp.async into xraw, one wait), so the
+    // loop below runs on shared memory instead of one load round trip per
+    // chunk
+    const bool bulk = !p.addnorm && !p.x_early && M * TB > WARPS + 1;
+    if (bulk) {
+      for (int id = warp; id < M * TB; id += WARPS + 1) {
+        const int m = id / TB, it = (id - m * TB) * 32 + lane, t = it >> 2, cc = it & 3;
+        if (it < Ts * 4) {
+          const uint32_t dst = smem_addr(xraw + m * XS + t * KSTEP + cc * 8);
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst),
+                       "l"(xg + size_t(m) * p.K + t * KSTEP + cc * 8)
+                       : "memory");
+        }
+      }
+      asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+      __syncthreads();
+    }
     for (int id = warp; id < M * TB; id += WARPS + 1) {
       const int m = id / TB, it = (id - m * TB) * 32 + lane, t = it >> 2, cc = it & 3;
       const bool ok = it < Ts * 4;  // Ts * 4 is a multiple of 4 * KPG: groups never straddle
@@ -541,10 +560,12 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
             od[j] = *reinterpret_cast<const uint32_t*>(&o);
           }
           v = make_uint4(od[0], od[1], od[2], od[3]);
+        } else if (bulk) {
+          v = *reinterpret_cast<const uint4*>(xraw + m * XS + t * KSTEP + cc * 8);
         } else {
           v = *reinterpret_cast<const uint4*>(xg + size_t(m) * p.K + t * KSTEP + cc * 8);
         }
-        *reinterpret_cast<uint4*>(xraw + m * XS + t * KSTEP + cc * 8) = v;  // natural order, LoRA-down
+        if (!bulk) *reinterpret_cast<uint4*>(xraw + m * XS + t * KSTEP + cc * 8) = v;  // natural order, LoRA-down
         xsw[(t * M + m) * 4 + cc] = make_uint4(prmt(v.x, v.z, 0x5410u), prmt(v.x, v.z, 0x7632u),
                                                 prmt(v.y, v.w, 0x5410u), prmt(v.y, v.w, 0x7632u));
       }
@@ -842,20 +863,20 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
   // send the partial of the columns owned by CTA j into j's receive area
   // [S][M][CPR] (rows nt*8 + 2c (+1), columns lcol + 2pp (+1))
   asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  // (the lane's 4 columns lcol..lcol+3 lie in one 8-column block, so in one
+  // owner's range: one 16-byte st.async per row)
   if (col_ok) {
+    const int owner = __umulhi(uint32_t(lcol), p.cpr_magic), cc = lcol - owner * CPR;
+    const uint32_t rbase = map_rank(smem_addr(recv + size_t(s) * M * CPR + cc), owner);
+    const uint32_t rbar = map_rank(bar_rv, owner);
 #pragma unroll
-    for (int pp = 0; pp < 2; ++pp) {
-      const int cl = lcol + 2 * pp;
-      const int owner = __umulhi(uint32_t(cl), p.cpr_magic), cc = cl - owner * CPR;
-      const uint32_t rbase = map_rank(smem_addr(recv + size_t(s) * M * CPR + cc), owner);
-      const uint32_t rbar = map_rank(bar_rv, owner);
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int m0 = nt * 8 + 2 * c;
-        if (m0 < M) st_async_f2(rbase + m0 * CPR * 4, acc[pp][nt][0], acc[pp][nt][2], rbar);
-        if (m0 + 1 < M)
-          st_async_f2(rbase + (m0 + 1) * CPR * 4, acc[pp][nt][1], acc[pp][nt][3], rbar);
-      }
+    for (int nt = 0; nt < NT; ++nt) {
+      const int m0 = nt * 8 + 2 * c;
+      if (m0 < M)
+        st_async_f4(rbase + m0 * CPR * 4, acc[0][nt][0], acc[0][nt][2], acc[1][nt][0], acc[1][nt][2], rbar);
+      if (m0 + 1 < M)
+        st_async_f4(rbase + (m0 + 1) * CPR * 4, acc[0][nt][1], acc[0][nt][3], acc[1][nt][1], acc[1][nt][3],
+                    rbar);
     }
   }
 
@@ -892,16 +913,28 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
       trace_stamp(trc, TR_EXIT, tid == 0);
       return;
     }
-    // the compute threads as (row, column) pairs: rpi rows per pass
-    const int rpi = own_cols >= WARPS * 32 ? 1 : (WARPS * 32) / own_cols;
-    const int mi = tid / own_cols, c0 = tid - mi * own_cols;
+    // the compute threads as (row, 4-column group) pairs: rpi rows per pass,
+    // 16-byte reads of the partials (own_cols and CPR are multiples of 8)
+    const int ov = own_cols >> 2;
+    const int rpi = ov >= WARPS * 32 ? 1 : (WARPS * 32) / ov;
+    const int mi = tid / ov, c0 = tid - mi * ov;
     for (int m0 = 0; m0 < M; m0 += rpi) {
       const int m = m0 + mi;
       if (mi < rpi && m < M) {
-        for (int cc = c0; cc < own_cols; cc += WARPS * 32) {
-          float v = 0.f;
-          for (int r2 = 0; r2 < S; ++r2) v += recv[(size_t(r2) * M + m) * CPR + cc];
-          p.y[size_t(m) * N + cb + cc] = __float2half_rn(v);
+        for (int cv = c0; cv < ov; cv += WARPS * 32) {
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int r2 = 0; r2 < S; ++r2) {
+            const float4 u = *reinterpret_cast<const float4*>(recv + (size_t(r2) * M + m) * CPR + 4 * cv);
+            v.x += u.x;
+            v.y += u.y;
+            v.z += u.z;
+            v.w += u.w;
+          }
+          __half* yo = p.y + size_t(m) * N + cb + 4 * cv;
+          yo[0] = __float2half_rn(v.x);
+          yo[1] = __float2half_rn(v.y);
+          yo[2] = __float2half_rn(v.z);
+          yo[3] = __float2half_rn(v.w);
         }
       }
     }
