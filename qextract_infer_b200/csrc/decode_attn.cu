@@ -20,9 +20,11 @@
 // the warps merge in shared memory.  The chunks of one (sequence, KV head) are
 // then merged one of two ways:
 //  * cluster merge (when a sequence's slots are split into 2..16 chunks): the
-//    chunk CTAs form one thread-block cluster, keep their (max, sum, O) in
-//    shared memory and, after a cluster barrier, each merges a slice of the
-//    output by reading every chunk's values over distributed shared memory;
+//    chunk CTAs form one thread-block cluster; each CTA owns a slice of the
+//    output and every chunk pushes its (max, sum) rows and O elements for that
+//    slice into the owner's shared memory with st.async (completion counted
+//    in bytes on the owner's mbarrier, a bounded wait), so no CTA reads a
+//    peer and there is no cluster barrier after the tile loop;
 //  * global merge (more chunks, or the cluster form pinned off): each CTA
 //    writes (max, sum, O) to the workspace and the last CTA of the
 //    (sequence, KV head), found with an atomic counter, merges them.
@@ -61,13 +63,22 @@ constexpr int SMEM_FUSED = SMEM + QS_BYTES;
 // deep form: 4 tile stages per warp (every tile of a 256-slot chunk in flight at
 // once), for grids of at most one CTA per SM
 constexpr int SMEM4 = 2 * SMEM;
-__host__ __device__ constexpr int smem_bytes(int nb, bool fused) {
-  return (nb == 4 ? SMEM4 : SMEM) + (fused ? QS_BYTES : 0);
+// cluster merge: every chunk CTA pushes its (max, sum) rows and O vectors into
+// the owners' receive areas (O [nch][per][4] floats, then (max, sum) [nch][RMAX]
+// rows), past the tiles and the fused q heads: at most (G D / 4 + nch) O
+// vectors and nch (per / 32 + 2) rows for G <= 16, nch <= 16
+constexpr int RECV_BYTES = 9216;
+__host__ __device__ constexpr int smem_bytes(int nb, bool fused, bool cluster = false) {
+  return (nb == 4 ? SMEM4 : SMEM) + (fused ? QS_BYTES : 0) + (cluster ? RECV_BYTES : 0);
 }
 static_assert(THREADS == D, "one thread per head dimension in the merges");
 static_assert(WARPS == 4, "the chunk merge interleaves 4 chunk subsets, one per warp");
 static_assert(2 * 16 * MAX_CHUNKS * 4 + 32 * 4 + 4 * 16 * D * 4 <= SMEM, "merge fits the tile smem");
 static_assert(CPART_OFF % 16 == 0 && CPART_OFF + 16 * PSTRIDE * 4 <= SMEM, "cluster partial fits");
+
+// Sticky device-side error word of this file's kernel (QX_DEVERR_* bits),
+// merged into qx_get_device_error.
+static __device__ unsigned g_attn_error = 0;
 
 struct Params {
   const __half* q;
@@ -149,6 +160,27 @@ __device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
                : "memory");
   return v;
 }
+__device__ __forceinline__ void st_async_f32(uint32_t raddr, float a, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr),
+               "r"(__float_as_uint(a)), "r"(rbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_f2(uint32_t raddr, float a, float b, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+                   raddr),
+               "f"(a), "f"(b), "r"(rbar)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred P; mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 P, [%1], %2; "
+      "selp.u32 %0, 1, 0, P; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -172,6 +204,27 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
   const int c0 = ci * p.chunk;
   const int c1 = min(p.valid, c0 + p.chunk);
   const int ntiles = (c1 - c0 + TILE - 1) / TILE;
+
+  // cluster merge: this CTA owns output vectors [ci per, ci per + own_v) of the
+  // G x D block; its receive barrier expects every chunk's share of them
+  __shared__ __align__(8) unsigned long long s_rbar;
+  const int per = (p.G * (D / 4) + p.nch - 1) / p.nch;
+  const int rmax = per / (D / 4) + 2;
+  if constexpr (CLUSTER) {
+    if (tid == 0) {
+      const int own_v = max(0, min(per, p.G * (D / 4) - ci * per));
+      const int own_r = own_v ? (ci * per + own_v - 1) / (D / 4) - (ci * per) / (D / 4) + 1 : 0;
+      const uint32_t rb = smem_u32(&s_rbar);
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(rb) : "memory");
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(rb),
+                   "r"(uint32_t(p.nch * (own_v * 16 + own_r * 8)))
+                   : "memory");
+    }
+    __syncthreads();
+    // peers push only after every CTA of the cluster initialised its barrier
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  }
 
   const size_t slot_stride = size_t(p.Hkv) * D;  // halves between consecutive slots
   const __half* kb = p.k + (size_t(b) * p.cap * p.Hkv + kvh) * D;
@@ -366,8 +419,12 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
     ls[warp * 16 + g + 8] = l_r[1];
   }
   __syncthreads();
-  float* mypart = CLUSTER ? reinterpret_cast<float*>(smem + CPART_OFF)
-                          : p.part + (size_t(bh) * p.nch + ci) * p.G * PSTRIDE;
+  float* mypart = p.part + (size_t(bh) * p.nch + ci) * p.G * PSTRIDE;
+  // cluster form: the receive areas (past the tiles and the fused q heads)
+  const int roff = (NB == 4 ? SMEM4 : SMEM) + (p.fused ? QS_BYTES : 0);
+  const uint32_t recv_o = smem_u32(smem + roff);                       // [nch][per][4]
+  const uint32_t recv_ml = recv_o + uint32_t(p.nch * per * 16);         // [nch][rmax][2]
+  if constexpr (CLUSTER) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
   {
     const int d = tid;  // THREADS == D
     for (int r = 0; r < p.G; ++r) {
@@ -381,67 +438,67 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const Params p) {
         L = fmaf(ls[w * 16 + r], f, L);
         O = fmaf(Os[(w * 16 + r) * OSTRIDE + d], f, O);
       }
-      mypart[r * PSTRIDE + 4 + d] = O;
-      if (d == 0) {
-        mypart[r * PSTRIDE] = mx;
-        mypart[r * PSTRIDE + 1] = L;
+      if constexpr (CLUSTER) {
+        // O of vector v = r * 32 + d / 4 to its owner; (max, sum) of row r to
+        // every owner whose vectors cover part of the row
+        const int v = r * (D / 4) + (d >> 2);
+        const int j = v / per, lv = v - j * per;
+        st_async_f32(cluster_map(recv_o + uint32_t((ci * per + lv) * 4 + (d & 3)) * 4u, uint32_t(j)), O,
+                     cluster_map(smem_u32(&s_rbar), uint32_t(j)));
+        const int jlo = (r * (D / 4)) / per, jhi = min(p.nch - 1, (r * (D / 4) + D / 4 - 1) / per);
+        if (d <= jhi - jlo) {
+          const int jj = jlo + d, rr = r - (jj * per) / (D / 4);
+          st_async_f2(cluster_map(recv_ml + uint32_t(ci * rmax + rr) * 8u, uint32_t(jj)), mx, L,
+                      cluster_map(smem_u32(&s_rbar), uint32_t(jj)));
+        }
+      } else {
+        mypart[r * PSTRIDE + 4 + d] = O;
+        if (d == 0) {
+          mypart[r * PSTRIDE] = mx;
+          mypart[r * PSTRIDE + 1] = L;
+        }
       }
     }
   }
 
   trace_stamp(trc, TR_WARP_MERGE, threadIdx.x == 0);
   if constexpr (CLUSTER) {
-    // every chunk's (max, sum, O) is in its CTA's shared memory: this CTA
-    // merges output vectors [v0, v1) (4 head dims each) of the G x D block.
-    // A lane per (vector, chunk): 16 lanes read the chunks' (max, sum) and
-    // 16-byte O vector over distributed shared memory in one round, then
-    // reduce across the 16 lanes with butterfly shuffles (a fixed order:
-    // deterministic); chunks past nch contribute nothing.
-    cluster_sync();
-    trace_stamp(trc, TR_CHUNK_SYNC, threadIdx.x == 0);
+    // every chunk pushed its share of this CTA's output vectors [v0, v1) and
+    // the (max, sum) of their rows: wait for all of it (bounded), then merge
+    // the chunks in order (deterministic) from local shared memory
     const int nch = p.nch, G = p.G;
-    const int nvec = G * (D / 4);
-    const int per = (nvec + nch - 1) / nch;
-    const int v0 = ci * per, v1 = min(nvec, v0 + per);
-    const uint32_t base = smem_u32(smem + CPART_OFF);
-    const int k = tid & 15;
-    for (int vb = v0; vb < v1; vb += THREADS / 16) {  // uniform trip count: whole warps shuffle
-      const int vv = vb + (tid >> 4);
-      const int r = vv / (D / 4), d0 = (vv - r * (D / 4)) * 4;
-      float mk = -INFINITY, lk = 0.f;
-      float4 ov = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (vv < v1 && k < nch) {
-        const uint32_t a = cluster_map(base, uint32_t(k)) + uint32_t(r * PSTRIDE) * 4u;
-        mk = ld_cluster_f32(a);
-        lk = ld_cluster_f32(a + 4u);
-        ov = ld_cluster_f32x4(a + uint32_t(4 + d0) * 4u);
+    const int v0 = ci * per, own_v = max(0, min(per, G * (D / 4) - v0));
+    if (own_v > 0) {
+      const uint32_t rb = smem_u32(&s_rbar);
+      if (!mbar_try(rb, 0)) {
+        unsigned long long t0, t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+        while (!mbar_try(rb, 0)) {
+          asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+          if (t - t0 > kWaitLimitNs) {
+            if (tid == 0) atomicOr(&g_attn_error, QX_DEVERR_MBAR_TIMEOUT);
+            break;
+          }
+        }
       }
-      float mx = mk;
-#pragma unroll
-      for (int w = 1; w < 16; w <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, w));
-      const float f = mk == -INFINITY ? 0.f : exp2f(mk - mx);
-      float L = lk * f;
-      ov.x *= f;
-      ov.y *= f;
-      ov.z *= f;
-      ov.w *= f;
-#pragma unroll
-      for (int w = 1; w < 16; w <<= 1) {
-        L += __shfl_xor_sync(0xffffffffu, L, w);
-        ov.x += __shfl_xor_sync(0xffffffffu, ov.x, w);
-        ov.y += __shfl_xor_sync(0xffffffffu, ov.y, w);
-        ov.z += __shfl_xor_sync(0xffffffffu, ov.z, w);
-        ov.w += __shfl_xor_sync(0xffffffffu, ov.w, w);
-      }
-      if (k == 0 && vv < v1) {
-        __half* dst = p.out + (size_t(b) * p.Hq + size_t(kvh) * G + r) * D + d0;
-        dst[0] = __float2half_rn(ov.x / L);
-        dst[1] = __float2half_rn(ov.y / L);
-        dst[2] = __float2half_rn(ov.z / L);
-        dst[3] = __float2half_rn(ov.w / L);
+      trace_stamp(trc, TR_CHUNK_SYNC, threadIdx.x == 0);
+      const float* ro = reinterpret_cast<const float*>(smem + roff);
+      const float* rml = ro + nch * per * 4;
+      const int r0 = v0 / (D / 4);
+      for (int e = tid; e < own_v * 4; e += THREADS) {
+        const int v = v0 + (e >> 2), r = v / (D / 4), d = (v - r * (D / 4)) * 4 + (e & 3);
+        float mx = -INFINITY;
+        for (int k = 0; k < nch; ++k) mx = fmaxf(mx, rml[(k * rmax + r - r0) * 2]);
+        float L = 0.f, O = 0.f;
+        for (int k = 0; k < nch; ++k) {
+          const float mk = rml[(k * rmax + r - r0) * 2];
+          const float f = mk == -INFINITY ? 0.f : exp2f(mk - mx);
+          L = fmaf(rml[(k * rmax + r - r0) * 2 + 1], f, L);
+          O = fmaf(ro[(k * per) * 4 + e], f, O);
+        }
+        p.out[(size_t(b) * p.Hq + size_t(kvh) * G + r) * D + d] = __float2half_rn(O / L);
       }
     }
-    cluster_sync();  // the peers' shared memory stays live until every read is done
     trace_stamp(trc, TR_EXIT, threadIdx.x == 0);
     return;
   }
@@ -604,13 +661,13 @@ static int prepare_kernel(const int** fit_out) {
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(2, true)),
                 "decode_attention: set smem limit");
     QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<true, 2>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(2, true)),
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(2, true, true)),
                 "decode_attention: set smem limit");
     QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<false, 4>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(4, true)),
                 "decode_attention: set smem limit");
     QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<true, 4>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(4, true)),
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(4, true, true)),
                 "decode_attention: set smem limit");
     QX_CUDA_TRY(cudaFuncSetAttribute(decode_attn_kernel<true, 2>,
                                      cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
@@ -623,7 +680,7 @@ static int prepare_kernel(const int** fit_out) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(cs, 1, 1);
         cfg.blockDim = dim3(THREADS, 1, 1);
-        cfg.dynamicSmemBytes = smem_bytes(nbi ? 4 : 2, true);
+        cfg.dynamicSmemBytes = smem_bytes(nbi ? 4 : 2, true, true);
         cudaLaunchAttribute at[1];
         at[0].id = cudaLaunchAttributeClusterDimension;
         at[0].val.clusterDim.x = cs;
@@ -655,7 +712,7 @@ static int prepare_kernel(const int** fit_out) {
 static int launch(const Plan& pl, const Params& prm, int batch, int kv_heads, cudaStream_t st,
                   const char* what) {
   const dim3 grid(pl.nch, batch * kv_heads), block(THREADS);
-  const int smem = smem_bytes(pl.nb, prm.fused != 0);
+  const int smem = smem_bytes(pl.nb, prm.fused != 0, pl.cluster);
   auto kern = pl.cluster ? (pl.nb == 4 ? decode_attn_kernel<true, 4> : decode_attn_kernel<true, 2>)
                          : (pl.nb == 4 ? decode_attn_kernel<false, 4> : decode_attn_kernel<false, 2>);
   Params pt = prm;
@@ -690,6 +747,16 @@ static int launch(const Plan& pl, const Params& prm, int batch, int kv_heads, cu
 }
 
 }  // namespace attn
+
+int attn_device_error(unsigned* code, int reset) {
+  QX_CUDA_TRY(cudaMemcpyFromSymbol(code, attn::g_attn_error, sizeof(unsigned)), "get_device_error: read");
+  if (reset) {
+    const unsigned zero = 0;
+    QX_CUDA_TRY(cudaMemcpyToSymbol(attn::g_attn_error, &zero, sizeof(unsigned)), "get_device_error: reset");
+  }
+  return QX_OK;
+}
+
 }  // namespace qx
 
 using namespace qx;

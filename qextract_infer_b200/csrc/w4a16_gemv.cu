@@ -1273,6 +1273,7 @@ using namespace qx;
 namespace qx {
 int gemm_device_error(unsigned* code, int reset);      // w4a16_gemm.cu
 int nvar_device_error(unsigned* code, int reset);      // nvlink_allreduce.cu
+int attn_device_error(unsigned* code, int reset);      // decode_attn.cu
 }
 
 extern "C" int qx_get_device_error(unsigned* code, int reset) {
@@ -1289,6 +1290,9 @@ extern "C" int qx_get_device_error(unsigned* code, int reset) {
   if (rc != QX_OK) return rc;
   *code |= other;
   rc = qx::nvar_device_error(&other, reset);
+  if (rc != QX_OK) return rc;
+  *code |= other;
+  rc = qx::attn_device_error(&other, reset);
   if (rc != QX_OK) return rc;
   *code |= other;
   return QX_OK;
