@@ -57,9 +57,7 @@ constexpr int COUNTER_SLOTS = 4096;              // fixed counter region at the 
 constexpr int MAX_CHUNKS = 64;                   // bounds the merge's shared memory
 constexpr int MAX_CLUSTER = 16;                  // chunks merged through distributed shared memory
 constexpr int OSTRIDE = D + 8;                   // floats per row of the warp merge (conflict-free float2 stores)
-constexpr int CPART_OFF = WARPS * 16 * OSTRIDE * 4 + 2 * WARPS * 16 * 4;  // cluster merge: [G][PSTRIDE]
 constexpr int QS_BYTES = 16 * D * 2;             // fused form: the G <= 16 rotated query heads
-constexpr int SMEM_FUSED = SMEM + QS_BYTES;
 // deep form: 4 tile stages per warp (every tile of a 256-slot chunk in flight at
 // once), for grids of at most one CTA per SM
 constexpr int SMEM4 = 2 * SMEM;
@@ -74,7 +72,6 @@ __host__ __device__ constexpr int smem_bytes(int nb, bool fused, bool cluster = 
 static_assert(THREADS == D, "one thread per head dimension in the merges");
 static_assert(WARPS == 4, "the chunk merge interleaves 4 chunk subsets, one per warp");
 static_assert(2 * 16 * MAX_CHUNKS * 4 + 32 * 4 + 4 * 16 * D * 4 <= SMEM, "merge fits the tile smem");
-static_assert(CPART_OFF % 16 == 0 && CPART_OFF + 16 * PSTRIDE * 4 <= SMEM, "cluster partial fits");
 
 // Sticky device-side error word of this file's kernel (QX_DEVERR_* bits),
 // merged into qx_get_device_error.
@@ -147,19 +144,6 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
-__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
 __device__ __forceinline__ void st_async_f32(uint32_t raddr, float a, uint32_t rbar) {
   asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr),
                "r"(__float_as_uint(a)), "r"(rbar)
@@ -180,9 +164,6 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 // CLUSTER: the grid's x extent (the chunks of one sequence and KV head) is one
