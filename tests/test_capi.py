@@ -107,3 +107,26 @@ def test_ops_reject_cpu_tensors():
         _C.fused_rmsnorm(x, torch.ones(128, dtype=torch.float16))
     with pytest.raises(RuntimeError, match="CUDA tensor"):
         _C.fused_swiglu(x, x)
+
+
+def test_trace_entry_point_is_closed_in_the_product_library():
+    """The product library carries no trace code: qx_trace_launches answers
+    QX_ERR_UNSUPPORTED (only libqx_b200_trace.so records), and it validates the
+    kernel family first."""
+    lib = _lib.load()
+    assert lib.qx_trace_launches(0, ctypes.c_void_p(16), 4) == -4
+    assert "without tracing" in _lib.last_error()
+    assert lib.qx_trace_launches(7, None, 0) == -1
+    assert "unknown kernel" in _lib.last_error()
+
+
+def test_addnorm_gemv_validation_errors():
+    """qx_w4a16_lora_gemv_addnorm rejects more than 8 rows and a residual_out
+    that overlaps the residual (other CTAs still read it) before any launch."""
+    lib = _lib.load()
+    args = lambda res, out, M: (res, 16 * 4096, 16, 1e-6, out, 16, 16, 16, 1, 0, 16, 16, 16,  # noqa: E731
+                                M, 256, 128, 16, 128, 2.0, 0, None)
+    assert lib.qx_w4a16_lora_gemv_addnorm(*args(16, 16 * 8192, 9)) == -1
+    assert "rows" in _lib.last_error()
+    assert lib.qx_w4a16_lora_gemv_addnorm(*args(16, 16 + 64, 2)) == -1
+    assert "overlap" in _lib.last_error()
