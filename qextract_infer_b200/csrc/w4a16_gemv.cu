@@ -96,7 +96,7 @@ __host__ __device__ constexpr int ctas_per_sm(int nt) { return nt == 1 ? 3 : (nt
 
 // Shared-memory carve-up (byte offsets), identical on host and device.
 struct Layout {
-  unsigned bars, ring, sz_s, sz_z, sf, xraw, xs, xks, Bs, hs, recv, total;
+  unsigned bars, ring, sz_s, sz_z, sf, xraw, xs, xks, Bs, hs, lu, recv, total;
 };
 
 struct alignas(64) Params {
@@ -198,6 +198,8 @@ __host__ __device__ inline Layout layout(int M, int KPG, int Ts_max, int rank, i
   L.xks = take(o, size_t(gmax) * Mp * 2 * 4);         // per group (Off, Sx) per row [g][Mp]
   L.Bs = take(o, size_t(rank) * COLS * 2);            // LoRA B tile [r][256]
   L.hs = take(o, size_t(M) * rank * 4);                // h_s [M][r]
+  // the helper's LoRA term (alpha/r) h_s B[:, tile] [M][256] (helper path only)
+  L.lu = take(o, (rank > 0 && !lora_on_warps(M, rank)) ? size_t(M) * COLS * 4 : 0);
   L.recv = take(o, size_t(S) * M * owner_cols(S, act) * 4);  // partials from the cluster [S][M][cpr]
   L.total = o;
   return L;
@@ -636,8 +638,33 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
       if (m0 < M) hs[m0 * R + j0 + 8] = h4[0][2] + h4[1][2];
       if (m0 + 1 < M) hs[(m0 + 1) * R + j0 + 8] = h4[0][3] + h4[1][3];
     }
-    mbar_arrive(bar_h);  // every lane: its h_s stores are released
     trace_stamp(trc, TR_LORA_DOWN, lane == 0);
+    __syncwarp();  // every rank of h_s in shared memory
+    // the LoRA up-projection in fp32 on the helper while the compute warps
+    // still stream weights (it then costs them one shared-memory read after
+    // their loop instead of a chain of MMAs): lane owns columns 8 lane..8 lane + 7
+    mbar_wait(bar_b, 0);
+    {
+      const __half* Bs = reinterpret_cast<const __half*>(smem + L.Bs) + lane * 8;
+      float* lu = reinterpret_cast<float*>(smem + L.lu) + lane * 8;
+      for (int m = 0; m < M; ++m) {
+        float a8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int jr = 0; jr < R; ++jr) {
+          const float hv = p.lora_scale * hs[m * R + jr];
+          const uint4 b8 = *reinterpret_cast<const uint4*>(Bs + jr * COLS);
+          const uint32_t bw[4] = {b8.x, b8.y, b8.z, b8.w};
+#pragma unroll
+          for (int q2 = 0; q2 < 4; ++q2) {
+            const float2 f = h2_to_f2(bw[q2]);
+            a8[2 * q2] = fmaf(hv, f.x, a8[2 * q2]);
+            a8[2 * q2 + 1] = fmaf(hv, f.y, a8[2 * q2 + 1]);
+          }
+        }
+        *reinterpret_cast<float4*>(lu + m * COLS) = make_float4(a8[0], a8[1], a8[2], a8[3]);
+        *reinterpret_cast<float4*>(lu + m * COLS + 4) = make_float4(a8[4], a8[5], a8[6], a8[7]);
+      }
+    }
+    mbar_arrive(bar_h);  // every lane: its LoRA-term stores are released
     return;
   }
 
@@ -791,15 +818,36 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
       }
     }
   }
-  // this CTA's LoRA term (alpha/r) h_s B[:, tile] joins its partial sums on
-  // the tensor cores: A = B^T (rows = this lane's columns), B operand =
-  // (alpha/r) h_s^T split into fp16 high and low parts (~22-bit product)
-  if (R > 0) {
+  if (R > 0 && !lora_warps) {
+    // the helper's LoRA term of this lane's rows and 4 columns
+    mbar_wait(bar_h, 0);
+    const float* lu = reinterpret_cast<const float*>(smem + L.lu) + lcol;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int m0 = nt * 8 + 2 * c;
+      if (m0 < M) {
+        const float4 u = *reinterpret_cast<const float4*>(lu + m0 * COLS);
+        acc[0][nt][0] += u.x;
+        acc[0][nt][2] += u.y;
+        acc[1][nt][0] += u.z;
+        acc[1][nt][2] += u.w;
+      }
+      if (m0 + 1 < M) {
+        const float4 u = *reinterpret_cast<const float4*>(lu + (m0 + 1) * COLS);
+        acc[0][nt][1] += u.x;
+        acc[0][nt][3] += u.y;
+        acc[1][nt][1] += u.z;
+        acc[1][nt][3] += u.w;
+      }
+    }
+  }
+  // wide batches and ranks: this CTA's LoRA term (alpha/r) h_s B[:, tile]
+  // joins its partial sums on the tensor cores: A = B^T (rows = this lane's
+  // columns), B operand = (alpha/r) h_s^T split into fp16 high and low parts
+  // (~22-bit product)
+  if (R > 0 && lora_warps) {
     const int RT = R >= 16 ? R / 16 : 1;
-    if (lora_warps)
-      asm volatile("bar.sync 1, %0;" ::"n"(WARPS * 32) : "memory");  // every warp's h_s partials
-    else
-      mbar_wait(bar_h, 0);
+    asm volatile("bar.sync 1, %0;" ::"n"(WARPS * 32) : "memory");  // every warp's h_s partials
     mbar_wait(bar_b, 0);
     const float* hs = reinterpret_cast<const float*>(smem + L.hs);
     const __half* Bs = reinterpret_cast<const __half*>(smem + L.Bs);
