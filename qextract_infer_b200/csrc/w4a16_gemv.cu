@@ -174,6 +174,13 @@ __device__ __forceinline__ float round_h(float v) { return __half2float(__float2
 // compute warps stream the weights.
 __host__ __device__ inline bool lora_on_warps(int M, int rank) { return rank > 0 && (M > 8 || rank >= 32); }
 __host__ __device__ inline int lora_tiles(int M, int rank) { return ((M + 15) / 16) * (rank / 8); }
+// one-row launches with the helper's down-projection: the helper also forms the
+// up-projection (alpha/r) h_s B[:, tile] in fp32 while the compute warps still
+// stream weights (measured at the Qwen3-4B gate_proj shape: 6.29 -> 6.11 us per
+// call; at 2-8 rows the compute warps' MMA pair after the loop stays faster)
+__host__ __device__ inline bool lora_up_on_helper(int M, int rank) {
+  return M == 1 && rank > 0 && !lora_on_warps(M, rank);
+}
 // tiles per compute warp (registers of the kernel instance: NT batch tiles)
 __host__ __device__ constexpr int lora_items(int nt) { return nt == 4 ? 4 : 2; }
 // bytes of one ring stage: KPG*4 packed rows of 1056 B, then KPG*32 rows of A
@@ -198,8 +205,7 @@ __host__ __device__ inline Layout layout(int M, int KPG, int Ts_max, int rank, i
   L.xks = take(o, size_t(gmax) * Mp * 2 * 4);         // per group (Off, Sx) per row [g][Mp]
   L.Bs = take(o, size_t(rank) * COLS * 2);            // LoRA B tile [r][256]
   L.hs = take(o, size_t(M) * rank * 4);                // h_s [M][r]
-  // the helper's LoRA term (alpha/r) h_s B[:, tile] [M][256] (helper path only)
-  L.lu = take(o, (rank > 0 && !lora_on_warps(M, rank)) ? size_t(M) * COLS * 4 : 0);
+  L.lu = take(o, lora_up_on_helper(M, rank) ? COLS * 4 : 0);  // the helper's LoRA term [256]
   L.recv = take(o, size_t(S) * M * owner_cols(S, act) * 4);  // partials from the cluster [S][M][cpr]
   L.total = o;
   return L;
@@ -639,32 +645,30 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
       if (m0 + 1 < M) hs[(m0 + 1) * R + j0 + 8] = h4[0][3] + h4[1][3];
     }
     trace_stamp(trc, TR_LORA_DOWN, lane == 0);
-    __syncwarp();  // every rank of h_s in shared memory
-    // the LoRA up-projection in fp32 on the helper while the compute warps
-    // still stream weights (it then costs them one shared-memory read after
-    // their loop instead of a chain of MMAs): lane owns columns 8 lane..8 lane + 7
-    mbar_wait(bar_b, 0);
-    {
+    if (lora_up_on_helper(M, R)) {
+      // one row: the up-projection in fp32 here, while the compute warps still
+      // stream weights (it then costs them one shared-memory read after their
+      // loop instead of a chain of MMAs); lane owns columns 8 lane..8 lane + 7
+      __syncwarp();  // every rank of h_s in shared memory
+      mbar_wait(bar_b, 0);
       const __half* Bs = reinterpret_cast<const __half*>(smem + L.Bs) + lane * 8;
       float* lu = reinterpret_cast<float*>(smem + L.lu) + lane * 8;
-      for (int m = 0; m < M; ++m) {
-        float a8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int jr = 0; jr < R; ++jr) {
-          const float hv = p.lora_scale * hs[m * R + jr];
-          const uint4 b8 = *reinterpret_cast<const uint4*>(Bs + jr * COLS);
-          const uint32_t bw[4] = {b8.x, b8.y, b8.z, b8.w};
+      float a8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int jr = 0; jr < R; ++jr) {
+        const float hv = p.lora_scale * hs[jr];
+        const uint4 b8 = *reinterpret_cast<const uint4*>(Bs + jr * COLS);
+        const uint32_t bw[4] = {b8.x, b8.y, b8.z, b8.w};
 #pragma unroll
-          for (int q2 = 0; q2 < 4; ++q2) {
-            const float2 f = h2_to_f2(bw[q2]);
-            a8[2 * q2] = fmaf(hv, f.x, a8[2 * q2]);
-            a8[2 * q2 + 1] = fmaf(hv, f.y, a8[2 * q2 + 1]);
-          }
+        for (int q2 = 0; q2 < 4; ++q2) {
+          const float2 f = h2_to_f2(bw[q2]);
+          a8[2 * q2] = fmaf(hv, f.x, a8[2 * q2]);
+          a8[2 * q2 + 1] = fmaf(hv, f.y, a8[2 * q2 + 1]);
         }
-        *reinterpret_cast<float4*>(lu + m * COLS) = make_float4(a8[0], a8[1], a8[2], a8[3]);
-        *reinterpret_cast<float4*>(lu + m * COLS + 4) = make_float4(a8[4], a8[5], a8[6], a8[7]);
       }
+      *reinterpret_cast<float4*>(lu) = make_float4(a8[0], a8[1], a8[2], a8[3]);
+      *reinterpret_cast<float4*>(lu + 4) = make_float4(a8[4], a8[5], a8[6], a8[7]);
     }
-    mbar_arrive(bar_h);  // every lane: its LoRA-term stores are released
+    mbar_arrive(bar_h);  // every lane: its h_s (and LoRA-term) stores are released
     return;
   }
 
@@ -818,36 +822,27 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm(NT))
       }
     }
   }
-  if (R > 0 && !lora_warps) {
-    // the helper's LoRA term of this lane's rows and 4 columns
+  const bool up_helper = !lora_warps && lora_up_on_helper(M, R);
+  if (up_helper) {
+    // the helper's LoRA term of this lane's 4 columns (row 0: lanes with c == 0)
     mbar_wait(bar_h, 0);
-    const float* lu = reinterpret_cast<const float*>(smem + L.lu) + lcol;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int m0 = nt * 8 + 2 * c;
-      if (m0 < M) {
-        const float4 u = *reinterpret_cast<const float4*>(lu + m0 * COLS);
-        acc[0][nt][0] += u.x;
-        acc[0][nt][2] += u.y;
-        acc[1][nt][0] += u.z;
-        acc[1][nt][2] += u.w;
-      }
-      if (m0 + 1 < M) {
-        const float4 u = *reinterpret_cast<const float4*>(lu + (m0 + 1) * COLS);
-        acc[0][nt][1] += u.x;
-        acc[0][nt][3] += u.y;
-        acc[1][nt][1] += u.z;
-        acc[1][nt][3] += u.w;
-      }
+    if (c == 0) {
+      const float4 u = *reinterpret_cast<const float4*>(smem + L.lu + lcol * 4);
+      acc[0][0][0] += u.x;
+      acc[0][0][2] += u.y;
+      acc[1][0][0] += u.z;
+      acc[1][0][2] += u.w;
     }
   }
-  // wide batches and ranks: this CTA's LoRA term (alpha/r) h_s B[:, tile]
-  // joins its partial sums on the tensor cores: A = B^T (rows = this lane's
-  // columns), B operand = (alpha/r) h_s^T split into fp16 high and low parts
-  // (~22-bit product)
-  if (R > 0 && lora_warps) {
+  // otherwise this CTA's LoRA term (alpha/r) h_s B[:, tile] joins its partial
+  // sums on the tensor cores: A = B^T (rows = this lane's columns), B operand
+  // = (alpha/r) h_s^T split into fp16 high and low parts (~22-bit product)
+  if (R > 0 && !up_helper) {
     const int RT = R >= 16 ? R / 16 : 1;
-    asm volatile("bar.sync 1, %0;" ::"n"(WARPS * 32) : "memory");  // every warp's h_s partials
+    if (lora_warps)
+      asm volatile("bar.sync 1, %0;" ::"n"(WARPS * 32) : "memory");  // every warp's h_s partials
+    else
+      mbar_wait(bar_h, 0);
     mbar_wait(bar_b, 0);
     const float* hs = reinterpret_cast<const float*>(smem + L.hs);
     const __half* Bs = reinterpret_cast<const __half*>(smem + L.Bs);
