@@ -83,8 +83,10 @@ def test_batch_rows(C, M):
     (32, 8, 8, 32), (128, 8, 8, 128), (128, 24, 16, 64), (256, 264, 32, 128),
     (4096, 1024, 64, 128), (12288, 256, 16, 128), (2560, 2560, 128, 128), (512, 4096, 0, 128),
 ])
-def test_shapes_and_ranks(C, K, N, rank, group):
-    d = make_gemv_inputs(2, K, N, max(rank, 8), group_size=group, seed=K + N + rank)
+@pytest.mark.parametrize("M", [1, 2])
+def test_shapes_and_ranks(C, K, N, rank, group, M):
+    # one row takes the helper warp's fp32 LoRA up-projection, two rows the MMA pair
+    d = make_gemv_inputs(M, K, N, max(rank, 8), group_size=group, seed=K + N + rank + M)
     t = _dev(d)
     if rank:
         y = C.w4a16_lora_gemv(t["x"], t["qweight"], t["scales"], t["zeros"], t["lora_A"],
