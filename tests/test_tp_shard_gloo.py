@@ -2,7 +2,7 @@
 
 One small Qwen3-shaped layer (column-parallel q/k/v/gate/up, row-parallel
 o/down with the LoRA partials in the same all-reduce, vocabulary-split greedy)
-computed shard by shard with the numpy oracle at world sizes 2 and 4, against
+computed shard by shard with the numpy oracle at world sizes 2, 4 and 8, against
 the unsharded oracle (rtol = atol = 1e-2).  The sharding code under test is
 the decoder's own (``qextract_infer_b200.tp_shard``); see
 ``tests/tp_shard_worker.py``.
@@ -26,7 +26,7 @@ def _worker(rank, world, port):
     tp_shard_worker.run(rank, world, port)
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_sharding_matches_unsharded_oracle(world, monkeypatch):
     # loopback rendezvous (the host name may not resolve) and a few threads per rank
     monkeypatch.setenv("GLOO_SOCKET_IFNAME", "lo")
