@@ -45,7 +45,10 @@
 //             helper warp for up to 8 rows and ranks below 32, else by the
 //             compute warps (16 x 8 tiles spread over the warps).  The LoRA
 //             product is linear in K, so each CTA adds (alpha/r) h_s B[:, tile]
-//             into its own partial sums and no h is exchanged.
+//             into its own partial sums and no h is exchanged: at one row the
+//             helper warp forms that term in fp32 as soon as h_s is complete,
+//             while the compute warps still stream; otherwise the compute
+//             warps add it with a hi/lo fp16 MMA pair after their loop.
 //   reduce  = each CTA sends its fp32 partial of the columns owned by CTA j
 //             straight into CTA j's shared memory with st.async, which
 //             completes on CTA j's receive mbarrier; CTA j waits for its
