@@ -13,9 +13,11 @@ value  : device throughput in GB/s (algorithmic bytes / CUDA-event time) over
          different weight set from a rotation whose total size exceeds 2x L2,
          so every call streams its weights from HBM.  Summed over ranks for
          N > 1 (independent replicas, weak scaling), time = max over ranks.
-e2e    : the same metric through the public Python API
-         (qextract_infer_b200.w4a16_lora_gemv) with x copied host->device from
-         pinned memory and y copied back every step.
+e2e    : the same metric through the reference-facing C-ABI host entry point
+         (qx_w4a16_lora_gemv_host, as a C / cgo / ctypes plugin calls it), with
+         pinned host x and y every step: the GEMV reads x_host over the bus and
+         writes y into y_host (M*K*2 bytes in, M*N*2 out per step), event-timed
+         around the calls.
 roofline, cpu_baseline, clocks, gpu_launches: see the keys in the JSON line.
 
 Under torchrun every rank runs its own replica; rank 0 prints one JSON line.
